@@ -1,0 +1,165 @@
+// gemm_tc_sm100.cu -- host launchers for the tcgen05 tile kernels (gemm_tc_sm100.cuh):
+// TMA descriptor encoding, kernel instantiation table, persistent / cluster launch.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+
+#include "gemm_tc_sm100.cuh"
+#include "../runtime/internal.h"
+#include "../runtime/tensor_map.h"
+
+namespace clove {
+namespace rt {
+
+CLOVE_DEFINE_ERROR_READER(read_clear_error_tc)
+
+namespace {
+
+using kern::EpiParams;
+using kern::OpF16;
+using kern::OpI8;
+using kern::TcShape;
+
+typedef void (*TcKernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, EpiParams);
+
+struct TcEntry {
+  int op, bn, split, out_bytes;
+  const void* fn;
+  int smem_bytes;
+  int bk, b_atom_elems, chunk, stg_row, b_sw;
+};
+
+template <class Op, int BN, bool SPLIT, int OUT>
+TcEntry make_entry(int op) {
+  using S = TcShape<Op, BN, SPLIT, OUT>;
+  TcEntry e;
+  e.op = op;
+  e.bn = BN;
+  e.split = SPLIT ? 2 : 1;  // "split" entries serve every cluster size 2..8
+  e.out_bytes = OUT;
+  e.fn = reinterpret_cast<const void*>(&kern::gemm_tc_kernel<Op, BN, SPLIT, OUT>);
+  e.smem_bytes = S::SMEM_BYTES;
+  e.bk = S::BK;
+  e.b_atom_elems = S::B_ATOM_ELEMS;
+  e.chunk = S::CHUNK;
+  e.stg_row = S::STG_ROW;
+  e.b_sw = S::B_SW;
+  return e;
+}
+
+struct Table {
+  static constexpr int kMax = 32;
+  TcEntry e[kMax];
+  std::atomic<uint64_t> attr_set[kMax];  // bit d: smem attribute set on device d
+  int n = 0;
+  template <class Op, int BN, bool SPLIT, int OUT>
+  void add(int op) {
+    attr_set[n].store(0);
+    e[n++] = make_entry<Op, BN, SPLIT, OUT>(op);
+  }
+  Table() {
+    add<OpF16, 64, false, 2>(kTcF16);
+    add<OpF16, 128, false, 2>(kTcF16);
+    add<OpF16, 256, false, 2>(kTcF16);
+    add<OpF16, 32, true, 2>(kTcF16);
+    add<OpF16, 64, true, 2>(kTcF16);
+    add<OpI8, 64, false, 2>(kTcI8);
+    add<OpI8, 128, false, 2>(kTcI8);
+    add<OpI8, 256, false, 2>(kTcI8);
+    add<OpI8, 32, true, 2>(kTcI8);
+    add<OpI8, 64, true, 2>(kTcI8);
+    add<OpI8, 64, false, 4>(kTcI8);
+    add<OpI8, 128, false, 4>(kTcI8);
+    add<OpI8, 256, false, 4>(kTcI8);
+    add<OpI8, 32, true, 4>(kTcI8);
+    add<OpI8, 64, true, 4>(kTcI8);
+  }
+};
+
+Table& table() {
+  static Table t;
+  return t;
+}
+
+int find_entry(int op, int bn, int split, int out_bytes) {
+  Table& t = table();
+  const int want_split = split > 1 ? 2 : 1;
+  for (int i = 0; i < t.n; ++i) {
+    const TcEntry& e = t.e[i];
+    if (e.op == op && e.bn == bn && e.split == want_split && e.out_bytes == out_bytes) return i;
+  }
+  return -1;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int op, int bn, int split, int out_bytes) {
+  if (split < 1 || split > 8) return false;
+  return find_entry(op, bn, split, out_bytes) >= 0;
+}
+
+int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
+                   void* C, int M, int N, int K, const kern::EpiParams& ep,
+                   const DeviceInfo& dev, cudaStream_t stream) {
+  const int ei = find_entry(op, bn, split, out_bytes);
+  if (ei < 0)
+    return fail(CLOVE_ERR_UNSUPPORTED, "no tensor-core kernel for op=%d bn=%d split=%d out=%d", op,
+                bn, split, out_bytes);
+  const TcEntry* e = &table().e[ei];
+  std::atomic<uint64_t>& attr_set = table().attr_set[ei];
+  const int elem = op == kTcF16 ? 2 : 1;
+  const CUtensorMapDataType in_dt =
+      op == kTcF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType out_dt =
+      out_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_INT32;
+
+  CUtensorMap tmA, tmB, tmC;
+  int rc;
+  // A [M,K]: box 128 B of K x 128 rows, 128B swizzle.
+  rc = encode_tmap_2d(&tmA, in_dt, elem, A, K, M, static_cast<uint64_t>(K) * elem, e->bk, 128, 128);
+  if (rc) return rc;
+  // B [K,N]: box (swizzle width of N) x BK rows.
+  rc = encode_tmap_2d(&tmB, in_dt, elem, B, N, K, static_cast<uint64_t>(N) * elem, e->b_atom_elems,
+                      e->bk, e->b_sw);
+  if (rc) return rc;
+  // C [M,N]: box CHUNK cols x 32 rows, swizzle = staging row bytes.
+  rc = encode_tmap_2d(&tmC, out_dt, out_bytes, C, N, M, static_cast<uint64_t>(N) * out_bytes,
+                      e->chunk, 32, e->stg_row);
+  if (rc) return rc;
+
+  const uint64_t bit = 1ull << (dev.device & 63);
+  if ((attr_set.load(std::memory_order_acquire) & bit) == 0) {
+    rc = check_cuda(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         e->smem_bytes),
+                    "cudaFuncSetAttribute(max dynamic smem)");
+    if (rc) return rc;
+    attr_set.fetch_or(bit, std::memory_order_acq_rel);
+  }
+
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  EpiParams epv = ep;
+  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(e->smem_bytes);
+  cfg.stream = stream;
+  if (split > 1) {
+    cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>(tiles), 1);
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(split);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  } else {
+    const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;
+  }
+  return check_cuda(cudaLaunchKernelExC(&cfg, e->fn, args), "gemm_tc launch");
+}
+
+}  // namespace rt
+}  // namespace clove

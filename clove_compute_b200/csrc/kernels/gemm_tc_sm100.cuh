@@ -1,0 +1,483 @@
+// gemm_tc_sm100.cuh -- tcgen05 GEMM for sm_100a: C[M,N] = epilogue(A[M,K] . B[K,N]).
+//
+// Replaces the reference's WMMA kernel (src/kernels/gemm_fp16.cu:30-215) and its
+// SIMT int8 kernel (src/kernels/gemm_int8.cu:16-117). Layouts are the reference's:
+// A row-major [M,K] (K-major operand), B row-major [K,N] (MN-major operand),
+// C row-major [M,N] fp16.
+//
+// Structure (one CTA = 6 warps):
+//   warp 0      TMA producer: A box [128 rows x 128 B] + B boxes [BK rows x swizzle width]
+//               into a STAGES-deep ring of 128B/64B/32B-swizzled smem tiles.
+//   warp 1      TMEM allocator + MMA issuer: 4 tcgen05.mma per stage (K = 32 bytes each),
+//               tcgen05.commit frees the stage; accumulators double-buffered in TMEM.
+//   warps 2-5   epilogue: tcgen05.ld (TMEM lane quarter = warp % 4), fp32/int32 math,
+//               fp16 pack into swizzled smem, TMA store per 32-row slab.
+// Persistent mode: grid <= #SMs, tiles strided over CTAs, grouped rasterisation.
+// Split mode: a cluster of S CTAs shares one output tile, each CTA takes 1/S of the
+// K blocks, partial accumulators are summed in a fixed order by CTA rank 0 over
+// distributed shared memory (exact for int32, deterministic for fp32).
+#pragma once
+
+#include "params.h"
+#include "sm100_ptx.cuh"
+
+namespace clove {
+namespace kern {
+
+// Operand formats.
+struct OpF16 {
+  static constexpr int kElemBytes = 2;
+  static constexpr bool kInt = false;
+  // fp32 accumulator, f16 x f16, A K-major, B MN-major.
+  static constexpr uint32_t idesc(int n) { return dev::make_idesc(1, 0, 0, 0, 1, n, 128); }
+};
+struct OpI8 {
+  static constexpr int kElemBytes = 1;
+  static constexpr bool kInt = true;
+  // s32 accumulator, s8 x s8, A K-major, B MN-major.
+  static constexpr uint32_t idesc(int n) { return dev::make_idesc(2, 1, 1, 0, 1, n, 128); }
+};
+
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per CTA on sm_100
+
+template <class Op, int BN_, bool SPLIT_, int OUT_BYTES_>
+struct TcShape {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr bool SPLIT = SPLIT_;
+  static constexpr int OUT_BYTES = OUT_BYTES_;
+  static constexpr int ELEM = Op::kElemBytes;
+  static constexpr int BK = 128 / ELEM;      // K elements per 128-byte row
+  static constexpr int UMMA_K = 32 / ELEM;   // K per tcgen05.mma
+  static constexpr int KSTEPS = BK / UMMA_K;  // 4
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int BN_BYTES = BN * ELEM;
+  static constexpr int B_SW = BN_BYTES >= 128 ? 128 : BN_BYTES;  // swizzle width of B
+  static constexpr int B_ATOMS = BN_BYTES / B_SW;
+  static constexpr int B_ATOM_ELEMS = B_SW / ELEM;
+  static constexpr int B_BYTES = BK * BN_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int CHUNK = BN < (128 / OUT_BYTES) ? BN : (128 / OUT_BYTES);  // cols / store
+  static constexpr int STG_ROW = CHUNK * OUT_BYTES;                             // bytes / row
+  static constexpr int STG_BUF = 32 * STG_ROW;
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x 4 KB (1 KB aligned)
+  static constexpr int PART_ROW = BN * 4 + 16;
+  static constexpr int PART_BYTES = SPLIT ? ((BM * PART_ROW + 1023) / 1024) * 1024 : 0;
+  static constexpr int ACC_BUFS = SPLIT ? 1 : 2;
+  static constexpr int TMEM_COLS = (ACC_BUFS * BN) < 32 ? 32 : (ACC_BUFS * BN);
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int STAGES_FIT =
+      (kSmemLimit - 1024 - EPI_BYTES - PART_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES + EPI_BYTES + PART_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 192;
+
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N constraint for M=128");
+  static_assert(BN_BYTES % B_SW == 0, "B tile must be whole swizzle atoms");
+  static_assert(B_SW == 32 || B_SW == 64 || B_SW == 128, "B swizzle width");
+  static_assert(STG_ROW == 32 || STG_ROW == 64 || STG_ROW == 128, "C staging row");
+  static_assert(STG_BUF <= 4096, "staging buffer");
+  static_assert(STAGES >= 2, "pipeline depth");
+  static_assert(SMEM_BYTES <= kSmemLimit, "smem budget");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS <= 512, "TMEM alloc size");
+  static_assert(!SPLIT || BN <= 64, "split mode keeps the whole tile in registers");
+};
+
+// Grouped rasterisation: bands of 16 M-tiles, N-tiles walked inside a band so
+// that concurrently running CTAs share A rows and B columns in L2.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& m_blk,
+                                            int& n_blk) {
+  constexpr int kGroupM = 16;
+  const int per_group = kGroupM * tiles_n;
+  const int g = tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(tiles_m - first_m, kGroupM);
+  const int r = tile - g * per_group;
+  m_blk = first_m + r % gm;
+  n_blk = r / gm;
+}
+
+__device__ __forceinline__ uint32_t swz_chunk(uint32_t row, uint32_t chunk, uint32_t row_bytes) {
+  // Swizzle<B,4,3> on the byte address of a row-major staging tile whose rows are
+  // row_bytes wide (B = log2(row_bytes/16)): 16-byte chunk index ^= address bits 7+.
+  const uint32_t mask = row_bytes / 16 - 1;
+  return chunk ^ (((row * row_bytes) >> 7) & mask);
+}
+
+template <class Op, int BN, bool SPLIT, int OUT_BYTES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep) {
+  using S = TcShape<Op, BN, SPLIT, OUT_BYTES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* epi_base = smem + S::STAGES * S::STAGE_BYTES;
+  uint8_t* part_base = epi_base + S::EPI_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(part_base + S::PART_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S::STAGES;
+  uint64_t* tfull = bars + 2 * S::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = dev::warp_idx();
+  const uint32_t lane = dev::lane_idx();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      dev::mbar_init(&full[s], 1);
+      dev::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      dev::mbar_init(&tfull[b], 1);
+      dev::mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    dev::fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&tmA);
+    dev::prefetch_tmap(&tmB);
+    dev::prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(tmem_slot, S::TMEM_COLS);
+    dev::tmem_relinquish_alloc_permit();
+  }
+  dev::tc_fence_before_sync();
+  __syncthreads();
+  dev::tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + S::BM - 1) / S::BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kb_total = (K + S::BK - 1) / S::BK;
+  int tile_first, tile_stride, kb_begin, kb_end;
+  if constexpr (SPLIT) {
+    const int rank = static_cast<int>(blockIdx.x);  // cluster spans gridDim.x
+    const int parts = static_cast<int>(gridDim.x);
+    tile_first = static_cast<int>(blockIdx.y);
+    tile_stride = num_tiles;  // exactly one tile per cluster
+    kb_begin = rank * kb_total / parts;
+    kb_end = (rank + 1) * kb_total / parts;
+  } else {
+    tile_first = static_cast<int>(blockIdx.x);
+    tile_stride = static_cast<int>(gridDim.x);
+    kb_begin = 0;
+    kb_end = kb_total;
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t armed = 0;  // bit s: stage s has a load in flight (for error unwinding)
+      uint32_t armed_parity = 0;
+      for (int tile = tile_first; tile < num_tiles; tile += tile_stride) {
+        int m_blk, n_blk;
+        if constexpr (SPLIT) {
+          m_blk = tile / tiles_n;
+          n_blk = tile % tiles_n;
+        } else {
+          tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+        }
+        bool ok = true;
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!dev::mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          dev::mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          uint8_t* a_dst = stage_base + stage * S::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + S::A_BYTES;
+          dev::tma_load_2d(a_dst, &tmA, &full[stage], kb * S::BK, m_blk * S::BM);
+#pragma unroll
+          for (int a = 0; a < S::B_ATOMS; ++a) {
+            dev::tma_load_2d(b_dst + a * (S::BK * S::B_SW), &tmB, &full[stage],
+                             n_blk * BN + a * S::B_ATOM_ELEMS, kb * S::BK);
+          }
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // Error unwinding: let every load still in flight land before the CTA exits.
+        volatile int no_abort = 0;
+        for (int s = 0; s < S::STAGES; ++s)
+          if (armed & (1u << s)) dev::mbar_wait(&full[s], (armed_parity >> s) & 1u, &no_abort);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = Op::idesc(BN);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = tile_first; tile < num_tiles && ok; tile += tile_stride, ++it) {
+        const uint32_t buf = static_cast<uint32_t>(it) & (S::ACC_BUFS - 1);
+        const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
+        if (!dev::mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag)) break;
+        dev::tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!dev::mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after_sync();
+          const uint32_t a_addr = dev::smem_u32(stage_base + stage * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < S::KSTEPS; ++k) {
+            const uint64_t adesc =
+                dev::make_smem_desc(a_addr + k * 32, 0, 1024, dev::kLayoutSw128);
+            const uint64_t bdesc = dev::make_smem_desc(
+                b_addr + k * S::UMMA_K * S::B_SW, S::BK * S::B_SW, 8 * S::B_SW,
+                dev::layout_for_swizzle_bytes(S::B_SW));
+            const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
+            if constexpr (Op::kInt)
+              dev::mma_i8_ss(d_tmem, adesc, bdesc, kIdesc, acc);
+            else
+              dev::mma_f16_ss(d_tmem, adesc, bdesc, kIdesc, acc);
+          }
+          dev::mma_commit(&empty[stage]);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        dev::mma_commit(&tfull[buf]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t q = warp & 3u;  // TMEM lane quarter this warp may access
+    const int row_in_tile = static_cast<int>(q * 32 + lane);
+    uint8_t* stg_base = epi_base + (warp - 2) * (2 * 4096);
+    uint32_t stg_count = 0;
+    int it = 0;
+    for (int tile = tile_first; tile < num_tiles; tile += tile_stride, ++it) {
+      int m_blk, n_blk;
+      if constexpr (SPLIT) {
+        m_blk = tile / tiles_n;
+        n_blk = tile % tiles_n;
+      } else {
+        tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+      }
+      const uint32_t buf = static_cast<uint32_t>(it) & (S::ACC_BUFS - 1);
+      const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
+      bool have_acc = kb_end > kb_begin;
+      if (have_acc) {
+        const bool got = __all_sync(0xffffffffu, dev::mbar_wait(&tfull[buf], use & 1u, abort_flag));
+        if (!got) {
+          // Split mode must still pass the cluster barriers below (with zeros).
+          if constexpr (!SPLIT) break;
+          have_acc = false;
+        }
+      }
+      dev::tc_fence_after_sync();
+      const int m0 = m_blk * S::BM;
+      const int n0 = n_blk * BN;
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16) + buf * BN;
+
+      // Split mode: gather the whole BN-wide row, reduce over the cluster.
+      uint32_t full_row[SPLIT ? BN : 1];
+      if constexpr (SPLIT) {
+#pragma unroll
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          if (have_acc) {
+            dev::tmem_ld_x16(t_row + c, v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0u;
+          }
+          dev::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) full_row[c + j] = v[j];
+        }
+        const uint32_t rank = dev::cluster_ctarank();
+        uint8_t* my_part = part_base + row_in_tile * S::PART_ROW;
+        if (rank != 0) {
+#pragma unroll
+          for (int c = 0; c < BN; c += 4)
+            dev::st_shared_v4(dev::smem_u32(my_part + c * 4), full_row[c], full_row[c + 1],
+                              full_row[c + 2], full_row[c + 3]);
+        }
+        dev::cluster_sync_all();  // partials visible cluster-wide
+        if (rank == 0) {
+          for (uint32_t p = 1; p < gridDim.x; ++p) {
+            const uint32_t peer = dev::map_shared_to_rank(dev::smem_u32(my_part), p);
+#pragma unroll
+            for (int c = 0; c < BN; c += 4) {
+              const uint4 v = dev::ld_dsmem_v4(peer + c * 4);
+              if constexpr (Op::kInt) {
+                full_row[c + 0] += v.x;
+                full_row[c + 1] += v.y;
+                full_row[c + 2] += v.z;
+                full_row[c + 3] += v.w;
+              } else {
+                full_row[c + 0] = __float_as_uint(__uint_as_float(full_row[c + 0]) + __uint_as_float(v.x));
+                full_row[c + 1] = __float_as_uint(__uint_as_float(full_row[c + 1]) + __uint_as_float(v.y));
+                full_row[c + 2] = __float_as_uint(__uint_as_float(full_row[c + 2]) + __uint_as_float(v.z));
+                full_row[c + 3] = __float_as_uint(__uint_as_float(full_row[c + 3]) + __uint_as_float(v.w));
+              }
+            }
+          }
+        }
+      }
+      const bool do_store = !SPLIT || dev::cluster_ctarank() == 0;
+
+      // Per-row epilogue constants.
+      float row_scale = 0.f;
+      int32_t row_corr = 0;
+      if (ep.mode == kEpiI8RowCol) row_scale = (row < M) ? ep.row_scale[row] : 0.f;
+      if ((ep.mode == kEpiI8Tensor || ep.mode == kEpiI32Raw) && ep.zb != 0 && row < M)
+        row_corr = static_cast<int32_t>(0u - static_cast<uint32_t>(ep.zb) *
+                                                 static_cast<uint32_t>(ep.row_sum[row]));
+
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += S::CHUNK) {
+        uint32_t v[S::CHUNK];
+        if constexpr (SPLIT) {
+#pragma unroll
+          for (int j = 0; j < S::CHUNK; ++j) v[j] = full_row[(c0 + j) % BN];
+        } else {
+#pragma unroll
+          for (int j = 0; j < S::CHUNK; j += 16) {
+            uint32_t t[16];
+            dev::tmem_ld_x16(t_row + c0 + j, t);
+            dev::tmem_ld_wait();
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+          }
+          if (c0 + S::CHUNK >= BN) {
+            // All of this accumulator buffer is in registers: hand it back to the MMA warp.
+            dev::tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) dev::mbar_arrive(&tempty[buf]);
+          }
+        }
+        if (!do_store) continue;
+
+        // Epilogue math -> 16-byte packets.
+        constexpr int PKTS = S::STG_ROW / 16;
+        uint32_t pk[PKTS][4];
+        const int ncol0 = n0 + c0;
+        if constexpr (OUT_BYTES == 2) {
+          float f[S::CHUNK];
+          if (ep.mode == kEpiF16AlphaBeta) {
+#pragma unroll
+            for (int j = 0; j < S::CHUNK; ++j) f[j] = ep.alpha * __uint_as_float(v[j]);
+            if (ep.beta != 0.f && row < M) {
+              const __half* crow = ep.c_in + static_cast<size_t>(row) * N;
+#pragma unroll
+              for (int j = 0; j < S::CHUNK; j += 8) {
+                if (ncol0 + j < N) {  // N % 8 == 0 on this path
+                  const uint4 cv = *reinterpret_cast<const uint4*>(crow + ncol0 + j);
+                  const __half2* h = reinterpret_cast<const __half2*>(&cv);
+#pragma unroll
+                  for (int u = 0; u < 4; ++u) {
+                    const float2 c2 = __half22float2(h[u]);
+                    f[j + 2 * u] += ep.beta * c2.x;
+                    f[j + 2 * u + 1] += ep.beta * c2.y;
+                  }
+                }
+              }
+            }
+          } else if (ep.mode == kEpiI8Tensor) {
+#pragma unroll
+            for (int j = 0; j < S::CHUNK; ++j) {
+              uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
+              if (ep.za != 0) {
+                const int n = min(ncol0 + j, N - 1);
+                a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+                a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
+                     static_cast<uint32_t>(ep.zb);
+              }
+              f[j] = static_cast<float>(static_cast<int32_t>(a)) * ep.scale;
+            }
+          } else {  // kEpiI8RowCol
+#pragma unroll
+            for (int j = 0; j < S::CHUNK; ++j) {
+              const int n = min(ncol0 + j, N - 1);
+              f[j] = (static_cast<float>(static_cast<int32_t>(v[j])) * row_scale) * ep.col_scale[n];
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < PKTS; ++p)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) pk[p][u] = dev::pack_half2(f[p * 8 + 2 * u], f[p * 8 + 2 * u + 1]);
+        } else {  // int32 raw accumulators
+#pragma unroll
+          for (int j = 0; j < S::CHUNK; ++j) {
+            uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
+            if (ep.za != 0) {
+              const int n = min(ncol0 + j, N - 1);
+              a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+              a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
+                   static_cast<uint32_t>(ep.zb);
+            }
+            pk[j / 4][j % 4] = a;
+          }
+        }
+
+        // Stage through swizzled smem and TMA-store this warp's 32-row slab.
+        uint8_t* stg = stg_base + (stg_count & 1u) * 4096;
+        if (lane == 0) dev::bulk_wait_group_read<1>();
+        __syncwarp();
+        const uint32_t stg_addr = dev::smem_u32(stg);
+#pragma unroll
+        for (int p = 0; p < PKTS; ++p) {
+          const uint32_t off = lane * S::STG_ROW + swz_chunk(lane, p, S::STG_ROW) * 16;
+          dev::st_shared_v4(stg_addr + off, pk[p][0], pk[p][1], pk[p][2], pk[p][3]);
+        }
+        dev::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          dev::tma_store_2d(&tmC, stg, ncol0, m0 + static_cast<int>(q) * 32);
+          dev::bulk_commit_group();
+        }
+        ++stg_count;
+      }
+      if constexpr (SPLIT) dev::cluster_sync_all();  // peers may now exit
+      if (*abort_flag) break;
+    }
+    if (lane == 0) dev::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  if constexpr (SPLIT) {
+    // Warps 0/1 (and epilogue warps that broke out early) must match the epilogue's
+    // two cluster barriers per tile; in split mode every CTA owns exactly one tile.
+    if (warp < 2) {
+      dev::cluster_sync_all();
+      dev::cluster_sync_all();
+    }
+  }
+
+  dev::tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after_sync();
+    dev::tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace kern
+}  // namespace clove

@@ -1,0 +1,120 @@
+// gemv_sm100.cu -- host launchers for the N <= 8 GEMV kernels (gemv_sm100.cuh).
+#include "gemv_sm100.cuh"
+#include "../runtime/internal.h"
+
+namespace clove {
+namespace rt {
+
+CLOVE_DEFINE_ERROR_READER(read_clear_error_gemv)
+
+namespace {
+
+// Enough CTAs to put every row pair in flight at once, at most 8 CTAs per SM.
+unsigned gemv_grid(int rows, const DeviceInfo& dev) {
+  const int warps_per_cta = kern::kGemvThreads / 32;
+  const long long row_pairs = (rows + kern::kGemvRowsPerWarp - 1) / kern::kGemvRowsPerWarp;
+  long long ctas = (row_pairs + warps_per_cta - 1) / warps_per_cta;
+  const long long cap = static_cast<long long>(dev.num_sms) * 8;
+  if (ctas > cap) ctas = cap;
+  if (ctas < 1) ctas = 1;
+  return static_cast<unsigned>(ctas);
+}
+
+template <typename KernelT>
+int prepare(KernelT kernel, size_t smem) {
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        reinterpret_cast<const void*>(kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(smem));
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemv smem)");
+  }
+  return CLOVE_OK;
+}
+
+template <int NC>
+int gemv_int4_nc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                 const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int K,
+                 long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col,
+                 const DeviceInfo& dev, cudaStream_t stream) {
+  const size_t smem = kern::gemv_int4_smem_bytes(NC, K);
+  int rc = prepare(kern::gemv_int4_kernel<NC>, smem);
+  if (rc) return rc;
+  kern::gemv_int4_kernel<NC><<<gemv_grid(rows, dev), kern::kGemvThreads, smem, stream>>>(
+      Aq, static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
+      static_cast<const __half*>(Bs), static_cast<const __half*>(Bz), static_cast<__half*>(C),
+      Gdbg, rows, K, ldc_row, ldc_col, ldg_row, ldg_col);
+  return check_cuda(cudaGetLastError(), "gemv_int4 launch");
+}
+
+template <int NC>
+int gemv_int8_nc(const int8_t* A, const int8_t* B, void* C, int rows, int K,
+                 const kern::GemvI8Epi& ep, const DeviceInfo& dev, cudaStream_t stream) {
+  const size_t smem = kern::gemv_int8_smem_bytes(NC, K);
+  int rc = prepare(kern::gemv_int8_kernel<NC>, smem);
+  if (rc) return rc;
+  kern::gemv_int8_kernel<NC><<<gemv_grid(rows, dev), kern::kGemvThreads, smem, stream>>>(
+      A, B, C, rows, K, ep);
+  return check_cuda(cudaGetLastError(), "gemv_int8 launch");
+}
+
+template <int NC>
+int gemv_f16_nc(const void* A, const void* B, void* C, int rows, int K, float alpha, float beta,
+                const DeviceInfo& dev, cudaStream_t stream) {
+  const size_t smem = kern::gemv_f16_smem_bytes(NC, K);
+  int rc = prepare(kern::gemv_f16_kernel<NC>, smem);
+  if (rc) return rc;
+  kern::gemv_f16_kernel<NC><<<gemv_grid(rows, dev), kern::kGemvThreads, smem, stream>>>(
+      static_cast<const __half*>(A), static_cast<const __half*>(B), static_cast<__half*>(C), rows,
+      K, alpha, beta);
+  return check_cuda(cudaGetLastError(), "gemv_f16 launch");
+}
+
+}  // namespace
+
+size_t gemv_int4_smem(int nc, int K) { return kern::gemv_int4_smem_bytes(nc, K); }
+size_t gemv_int8_smem(int nc, int K) { return kern::gemv_int8_smem_bytes(nc, K); }
+size_t gemv_f16_smem(int nc, int K) { return kern::gemv_f16_smem_bytes(nc, K); }
+
+#define CLOVE_NC_SWITCH(nc, CALL) \
+  switch (nc) {                   \
+    case 1: return CALL(1);       \
+    case 2: return CALL(2);       \
+    case 3: return CALL(3);       \
+    case 4: return CALL(4);       \
+    case 5: return CALL(5);       \
+    case 6: return CALL(6);       \
+    case 7: return CALL(7);       \
+    case 8: return CALL(8);       \
+    default: break;               \
+  }
+
+int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                     const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int nc,
+                     int K, long long ldc_row, long long ldc_col, long long ldg_row,
+                     long long ldg_col, const DeviceInfo& dev, cudaStream_t stream) {
+#define CALL(n)                                                                                  \
+  gemv_int4_nc<n>(Aq, As, Az, Bq, Bs, Bz, C, Gdbg, rows, K, ldc_row, ldc_col, ldg_row, ldg_col, \
+                  dev, stream)
+  CLOVE_NC_SWITCH(nc, CALL)
+#undef CALL
+  return fail(CLOVE_ERR_UNSUPPORTED, "gemv_int4: %d vectors (max 8)", nc);
+}
+
+int launch_gemv_int8(const int8_t* A, const int8_t* B, void* C, int rows, int nc, int K,
+                     const kern::GemvI8Epi& ep, const DeviceInfo& dev, cudaStream_t stream) {
+#define CALL(n) gemv_int8_nc<n>(A, B, C, rows, K, ep, dev, stream)
+  CLOVE_NC_SWITCH(nc, CALL)
+#undef CALL
+  return fail(CLOVE_ERR_UNSUPPORTED, "gemv_int8: %d columns (max 8)", nc);
+}
+
+int launch_gemv_f16(const void* A, const void* B, void* C, int rows, int nc, int K, float alpha,
+                    float beta, const DeviceInfo& dev, cudaStream_t stream) {
+#define CALL(n) gemv_f16_nc<n>(A, B, C, rows, K, alpha, beta, dev, stream)
+  CLOVE_NC_SWITCH(nc, CALL)
+#undef CALL
+  return fail(CLOVE_ERR_UNSUPPORTED, "gemv_f16: %d columns (max 8)", nc);
+}
+
+}  // namespace rt
+}  // namespace clove

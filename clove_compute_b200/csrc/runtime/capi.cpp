@@ -1,0 +1,440 @@
+// capi.cpp -- the extern "C" entry points of include/clove/capi.h: argument
+// validation, kernel-family dispatch, scratch management, error reporting.
+//
+// Reference behaviour kept: stateless, handle-free, asynchronous on the caller's
+// stream, caller-owned device buffers (src/kernels/gemm_fp16.cu:277-305,
+// gemm_int8.cu:119-137, gemm_int4.cu:195-216). Unlike the reference, failures
+// are returned as status codes instead of exit().
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../kernels/params.h"
+#include "internal.h"
+
+namespace clove {
+namespace rt {
+
+namespace {
+thread_local char g_last_error[512] = "no error";
+std::atomic<int> g_ov_path{0}, g_ov_bn{0}, g_ov_split{0};
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+DeviceInfo g_dev_cache[kMaxDevices];
+bool g_dev_valid[kMaxDevices] = {};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+inline bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return CLOVE_OK;
+  return fail(CLOVE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int current_device(DeviceInfo* out) {
+  int d = 0;
+  int rc = check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+  if (rc) return rc;
+  if (d < 0 || d >= kMaxDevices) return fail(CLOVE_ERR_DEVICE, "device ordinal %d", d);
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_dev_valid[d]) {
+      *out = g_dev_cache[d];
+      return CLOVE_OK;
+    }
+  }
+  DeviceInfo info;
+  info.device = d;
+  rc = check_cuda(cudaDeviceGetAttribute(&info.num_sms, cudaDevAttrMultiProcessorCount, d),
+                  "cudaDeviceGetAttribute(SMs)");
+  if (rc) return rc;
+  rc = check_cuda(cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, d),
+                  "cudaDeviceGetAttribute(cc)");
+  if (rc) return rc;
+  rc = check_cuda(cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, d),
+                  "cudaDeviceGetAttribute(cc)");
+  if (rc) return rc;
+  if (info.cc_major != 10)
+    return fail(CLOVE_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", d,
+                info.cc_major, info.cc_minor);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  g_dev_cache[d] = info;
+  g_dev_valid[d] = true;
+  *out = info;
+  return CLOVE_OK;
+}
+
+Override get_override() {
+  return Override{g_ov_path.load(), g_ov_bn.load(), g_ov_split.load()};
+}
+
+// ---------------------------------------------------------------------------
+// Tile-shape policy for the tensor-core kernels
+// ---------------------------------------------------------------------------
+struct TcPlan {
+  int bn;
+  int split;
+};
+
+// Per-tile time is roughly proportional to BN; narrower tiles pay extra for
+// re-reading A. Choose the BN that minimises waves x BN x penalty; when even
+// BN=64 leaves most SMs idle, split K over a cluster.
+TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
+  const Override ov = get_override();
+  const int bk = 128 / elem;
+  const int kb_total = (K + bk - 1) / bk;
+  const int tm = (M + 127) / 128;
+  TcPlan best{256, 1};
+  if (ov.bn != 0) {
+    best.bn = ov.bn;
+  } else {
+    double best_cost = 1e30;
+    const int cand[3] = {256, 128, 64};
+    const double penalty[3] = {1.0, 1.15, 1.45};
+    for (int i = 0; i < 3; ++i) {
+      const int bn = cand[i];
+      const long long tiles = static_cast<long long>(tm) * ((N + bn - 1) / bn);
+      const long long waves = (tiles + num_sms - 1) / num_sms;
+      const double cost = static_cast<double>(waves) * bn * penalty[i];
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best.bn = bn;
+      }
+    }
+  }
+  if (ov.split != 0) {
+    best.split = ov.split;
+  } else {
+    const long long tiles64 = static_cast<long long>(tm) * ((N + 63) / 64);
+    if (tiles64 * 2 <= num_sms && kb_total >= 4) {
+      // Few output tiles: narrow tiles split over K inside a cluster.
+      best.bn = (N <= 32 || tm * ((N + 63) / 64) * 4 <= num_sms) ? 32 : 64;
+      if (ov.bn != 0) best.bn = ov.bn;
+      const long long tiles = static_cast<long long>(tm) * ((N + best.bn - 1) / best.bn);
+      long long s = num_sms / std::max<long long>(tiles, 1);
+      s = std::min<long long>(s, 8);
+      s = std::min<long long>(s, kb_total / 2);
+      best.split = static_cast<int>(std::max<long long>(s, 1));
+    } else {
+      best.split = 1;
+    }
+  }
+  if (best.split > 1 && best.bn > 64) best.bn = 64;
+  return best;
+}
+
+}  // namespace rt
+}  // namespace clove
+
+using namespace clove;
+using namespace clove::rt;
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* clove_version(void) { return "clove-b200 0.1 (sm_100a, tcgen05)"; }
+
+const char* clove_last_error_string(void) { return g_last_error; }
+
+int clove_get_device_error(int* code) {
+  if (code == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "code is NULL");
+  int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (rc) return rc;
+  int v = 0;
+  const int readers[4] = {read_clear_error_tc(), read_clear_error_gemv(), read_clear_error_simt(),
+                          read_clear_error_int4()};
+  for (int r : readers) {
+    if (r < 0) return fail(CLOVE_ERR_CUDA, "reading the device error word failed");
+    if (v == 0 && r != 0) v = r;
+  }
+  *code = v;
+  return CLOVE_OK;
+}
+
+int clove_set_dispatch_override(int path, int bn, int split) {
+  g_ov_path.store(path);
+  g_ov_bn.store(bn);
+  g_ov_split.store(split);
+  return CLOVE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// FP16
+// ---------------------------------------------------------------------------
+static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                          float beta, cudaStream_t s, const char** chosen) {
+  if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
+  if (M == 0 || N == 0) return CLOVE_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
+    return fail(CLOVE_ERR_INVALID_ARG, "null matrix pointer");
+  if (!aligned2(A) || !aligned2(B) || !aligned2(C))
+    return fail(CLOVE_ERR_INVALID_ARG, "fp16 pointers must be 2-byte aligned");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  if (K == 0) {
+    if (chosen) *chosen = "scale";
+    return launch_scale_f16(C, static_cast<long long>(M) * N, beta, s);
+  }
+  const Override ov = get_override();
+  const bool tc_ok = K % 8 == 0 && N % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C);
+  const bool gemv_ok = N <= 8 && K % 8 == 0 && aligned16(A) && gemv_f16_smem(N, K) <= 200 * 1024;
+  int path = ov.path;
+  if (path == 1 && !tc_ok) path = 0;
+  if (path == 2 && !gemv_ok) path = 0;
+  if (path == 0) path = (gemv_ok && N < 16) ? 2 : (tc_ok ? 1 : 3);
+  if (path == 2) {
+    if (chosen) *chosen = "gemv_f16";
+    return launch_gemv_f16(A, B, C, M, N, K, alpha, beta, dev, s);
+  }
+  if (path == 3) {
+    if (chosen) *chosen = "simt_f16";
+    return launch_simt_f16(A, B, C, 1, M, N, K, alpha, beta, s);
+  }
+  const TcPlan plan = plan_tc(M, N, K, 2, dev.num_sms);
+  if (chosen) *chosen = plan.split > 1 ? "tc_f16_split" : "tc_f16";
+  kern::EpiParams ep{};
+  ep.mode = kern::kEpiF16AlphaBeta;
+  ep.alpha = alpha;
+  ep.beta = beta;
+  ep.c_in = static_cast<const __half*>(C);
+  return launch_gemm_tc(kTcF16, plan.bn, plan.split, 2, A, B, C, M, N, K, ep, dev, s);
+}
+
+int clove_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                    float beta, void* stream) {
+  return gemm_fp16_impl(A, B, C, M, N, K, alpha, beta, as_stream(stream), nullptr);
+}
+
+int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K,
+                            float alpha, float beta, void* stream) {
+  if (batch < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative batch");
+  if (batch == 0 || M == 0 || N == 0) return CLOVE_OK;
+  const size_t sa = static_cast<size_t>(M) * K * 2, sb = static_cast<size_t>(K) * N * 2,
+               sc = static_cast<size_t>(M) * N * 2;
+  for (int b = 0; b < batch; ++b) {
+    const int rc = gemm_fp16_impl(static_cast<const char*>(A) + b * sa,
+                                  static_cast<const char*>(B) + b * sb,
+                                  static_cast<char*>(C) + b * sc, M, N, K, alpha, beta,
+                                  as_stream(stream), nullptr);
+    if (rc) return rc;
+  }
+  return CLOVE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// INT8
+// ---------------------------------------------------------------------------
+// mode: 1 per-tensor, 2 row/col, 3 raw int32 accumulators.
+static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int N, int K, int mode,
+                          float scale, int za, int zb, const float* rs, const float* cs,
+                          cudaStream_t s, const char** chosen) {
+  if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
+  if (M == 0 || N == 0) return CLOVE_OK;
+  if (A == nullptr || B == nullptr || C == nullptr)
+    return fail(CLOVE_ERR_INVALID_ARG, "null matrix pointer");
+  if (mode == 2 && (rs == nullptr || cs == nullptr))
+    return fail(CLOVE_ERR_INVALID_ARG, "null scale vector");
+  const int out_bytes = mode == 3 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(C) & (out_bytes - 1)) != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "misaligned C");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  const Override ov = get_override();
+  const bool tc_ok = K > 0 && K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) &&
+                     aligned16(C);
+  const bool gemv_ok = K > 0 && N <= 8 && K % 16 == 0 && aligned16(A) &&
+                       gemv_int8_smem(N, K) <= 200 * 1024;
+  int path = ov.path;
+  if (path == 1 && !tc_ok) path = 0;
+  if (path == 2 && !gemv_ok) path = 0;
+  if (path == 0) path = gemv_ok ? 2 : (tc_ok ? 1 : 3);
+  if (path == 2) {
+    if (chosen) *chosen = "gemv_int8";
+    kern::GemvI8Epi ep{mode, scale, rs, cs, za, zb};
+    return launch_gemv_int8(A, B, C, M, N, K, ep, dev, s);
+  }
+  if (path == 3) {
+    if (chosen) *chosen = "simt_int8";
+    kern::SimtEpi ep{};
+    ep.mode = mode;
+    ep.scale = scale;
+    ep.row_scale = rs;
+    ep.col_scale = cs;
+    ep.za = za;
+    ep.zb = zb;
+    return launch_simt_i8(A, B, C, M, N, K, ep, s);
+  }
+  const TcPlan plan = plan_tc(M, N, K, 1, dev.num_sms);
+  if (chosen) *chosen = plan.split > 1 ? "tc_int8_split" : "tc_int8";
+  kern::EpiParams ep{};
+  ep.mode = mode == 1 ? kern::kEpiI8Tensor : mode == 2 ? kern::kEpiI8RowCol : kern::kEpiI32Raw;
+  ep.scale = scale;
+  ep.row_scale = rs;
+  ep.col_scale = cs;
+  ep.za = za;
+  ep.zb = zb;
+  // Zero points: row sums of A (zb != 0) and column sums of B (za != 0) in
+  // stream-ordered scratch.
+  int32_t* sums = nullptr;
+  if (za != 0 || zb != 0) {
+    rc = check_cuda(cudaMallocAsync(reinterpret_cast<void**>(&sums),
+                                    sizeof(int32_t) * (static_cast<size_t>(M) + N), s),
+                    "cudaMallocAsync(zero-point sums)");
+    if (rc) return rc;
+    if (zb != 0) rc = launch_int8_row_sums(A, sums, M, K, s);
+    if (!rc && za != 0) rc = launch_int8_col_sums(B, sums + M, K, N, s);
+    ep.row_sum = sums;
+    ep.col_sum = sums + M;
+  }
+  if (!rc) rc = launch_gemm_tc(kTcI8, plan.bn, plan.split, out_bytes, A, B, C, M, N, K, ep, dev, s);
+  if (sums != nullptr) {
+    const int rc2 = check_cuda(cudaFreeAsync(sums, s), "cudaFreeAsync(zero-point sums)");
+    if (!rc) rc = rc2;
+  }
+  return rc;
+}
+
+int clove_gemm_int8(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
+                    float A_scale, int8_t A_zero, float B_scale, int8_t B_zero, void* stream) {
+  return gemm_int8_impl(A_q, B_q, C, M, N, K, 1, A_scale * B_scale, A_zero, B_zero, nullptr,
+                        nullptr, as_stream(stream), nullptr);
+}
+
+int clove_gemm_int8_rowcol(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
+                           const float* A_row_scale, const float* B_col_scale, void* stream) {
+  return gemm_int8_impl(A_q, B_q, C, M, N, K, 2, 0.f, 0, 0, A_row_scale, B_col_scale,
+                        as_stream(stream), nullptr);
+}
+
+int clove_debug_int8_acc(const int8_t* A_q, const int8_t* B_q, int32_t* acc, int M, int N, int K,
+                         int8_t A_zero, int8_t B_zero, void* stream) {
+  return gemm_int8_impl(A_q, B_q, acc, M, N, K, 3, 0.f, A_zero, B_zero, nullptr, nullptr,
+                        as_stream(stream), nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// INT4
+// ---------------------------------------------------------------------------
+static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                          const void* Bs, const void* Bz, void* C, int32_t* G, int M, int N, int K,
+                          cudaStream_t s, const char** chosen) {
+  if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
+  if (M == 0 || N == 0) return CLOVE_OK;
+  if (K % CLOVE_INT4_GROUP_SIZE != 0)
+    return fail(CLOVE_ERR_UNSUPPORTED, "int4: K=%d is not a multiple of the group size 128", K);
+  if (Aq == nullptr || As == nullptr || Az == nullptr || Bq == nullptr || Bs == nullptr ||
+      Bz == nullptr || C == nullptr)
+    return fail(CLOVE_ERR_INVALID_ARG, "null pointer");
+  if (!aligned2(As) || !aligned2(Az) || !aligned2(Bs) || !aligned2(Bz) || !aligned2(C) ||
+      (G != nullptr && !aligned4(G)))
+    return fail(CLOVE_ERR_INVALID_ARG, "misaligned fp16 / int32 pointer");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  if (K == 0) return launch_scale_f16(C, static_cast<long long>(M) * N, 0.f, s);
+  const Override ov = get_override();
+  const int NG = K / 128;
+  const bool gemv_n_ok = N <= 8 && aligned16(Aq) && aligned4(Bq) && gemv_int4_smem(N, K) <= 200 * 1024;
+  const bool gemv_m_ok = M <= 8 && aligned16(Bq) && aligned4(Aq) && gemv_int4_smem(M, K) <= 200 * 1024;
+  const bool tc_ok = gemm_int4_tc_eligible(Aq, As, Az, Bq, Bs, Bz, C, M, N, K);
+  int path = ov.path;
+  if (path == 1 && !tc_ok) path = 0;
+  if (path == 2 && !(gemv_n_ok || gemv_m_ok)) path = 0;
+  if (path == 0) path = (gemv_n_ok || gemv_m_ok) ? 2 : (tc_ok ? 1 : 3);
+  if (path == 2) {
+    if (gemv_n_ok && (N <= M || !gemv_m_ok)) {
+      if (chosen) *chosen = "gemv_int4";
+      return launch_gemv_int4(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, N, 1,
+                              static_cast<long long>(N) * NG, NG, dev, s);
+    }
+    if (chosen) *chosen = "gemv_int4_t";
+    // Rows of B stream past the M (<= 8) vectors of A; C[m,n] at m*N + n.
+    return launch_gemv_int4(Bq, Bs, Bz, Aq, As, Az, C, G, N, M, K, 1, N, NG,
+                            static_cast<long long>(N) * NG, dev, s);
+  }
+  if (path == 1 && G == nullptr) {
+    if (chosen) *chosen = "tc_int4";
+    return launch_gemm_int4_tc(Aq, As, Az, Bq, Bs, Bz, C, M, N, K, dev, s);
+  }
+  if (chosen) *chosen = "simt_int4";
+  return launch_simt_i4(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, s);
+}
+
+int clove_gemm_int4(const uint8_t* A_q, const void* A_scale, const void* A_zero,
+                    const uint8_t* B_q, const void* B_scale, const void* B_zero, void* C, int M,
+                    int N, int K, void* stream) {
+  return gemm_int4_impl(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C, nullptr, M, N, K,
+                        as_stream(stream), nullptr);
+}
+
+int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const void* A_zero,
+                               const uint8_t* B_q, const void* B_scale, const void* B_zero,
+                               void* C, int32_t* G, int M, int N, int K, void* stream) {
+  if (G == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "G is NULL");
+  return gemm_int4_impl(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C, G, M, N, K,
+                        as_stream(stream), nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Introspection
+// ---------------------------------------------------------------------------
+int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t buflen) {
+  if (buf == nullptr || buflen == 0) return fail(CLOVE_ERR_INVALID_ARG, "null buffer");
+  DeviceInfo dev{0, 148, 10, 0};
+  DeviceInfo real;
+  if (current_device(&real) == CLOVE_OK) dev = real;
+  const Override ov = get_override();
+  const char* name = "?";
+  int bn = 0, split = 0;
+  if (M <= 0 || N <= 0) {
+    name = "noop";
+  } else if (dtype == 0) {
+    const bool gemv = N <= 8 && K % 8 == 0 && gemv_f16_smem(N, K) <= 200 * 1024;
+    const bool tc = K % 8 == 0 && N % 8 == 0 && K > 0;
+    int path = ov.path ? ov.path : ((gemv && N < 16) ? 2 : (tc ? 1 : 3));
+    name = path == 2 ? "gemv_f16" : path == 3 ? "simt_f16" : "tc_f16";
+    if (path == 1) {
+      const TcPlan p = plan_tc(M, N, K, 2, dev.num_sms);
+      bn = p.bn;
+      split = p.split;
+    }
+  } else if (dtype == 1) {
+    const bool gemv = N <= 8 && K % 16 == 0 && K > 0;
+    const bool tc = K % 16 == 0 && N % 16 == 0 && K > 0;
+    int path = ov.path ? ov.path : (gemv ? 2 : (tc ? 1 : 3));
+    name = path == 2 ? "gemv_int8" : path == 3 ? "simt_int8" : "tc_int8";
+    if (path == 1) {
+      const TcPlan p = plan_tc(M, N, K, 1, dev.num_sms);
+      bn = p.bn;
+      split = p.split;
+    }
+  } else {
+    const bool gemv = (N <= 8 || M <= 8) && K % 128 == 0;
+    name = gemv ? (N <= 8 && (N <= M || M > 8) ? "gemv_int4" : "gemv_int4_t") : "tc_int4";
+  }
+  snprintf(buf, buflen, "%s bn=%d split=%d", name, bn, split);
+  return CLOVE_OK;
+}
+
+}  // extern "C"

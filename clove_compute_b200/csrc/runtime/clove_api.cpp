@@ -1,0 +1,52 @@
+// clove_api.cpp -- the reference's C++ entry points (include/clove/kernels/gemm.cuh),
+// forwarding to the C ABI. As in the reference (CLOVE_CHECK_LAST, common.cuh:11-21)
+// a failure prints the reason and exits the process.
+#include <cstdio>
+#include <cstdlib>
+
+#include "clove/kernels/gemm.cuh"
+
+namespace clove {
+
+namespace {
+void die_on_error(int rc, const char* what) {
+  if (rc != CLOVE_OK) {
+    fprintf(stderr, "clove::%s failed (%d): %s\n", what, rc, clove_last_error_string());
+    exit(EXIT_FAILURE);
+  }
+}
+}  // namespace
+
+void gemm_fp16(const half* A, const half* B, half* C, int M, int N, int K, float alpha,
+               float beta, cudaStream_t stream) {
+  die_on_error(clove_gemm_fp16(A, B, C, M, N, K, alpha, beta, stream), "gemm_fp16");
+}
+
+void gemm_int8(const int8_t* A_q, const int8_t* B_q, half* C, int M, int N, int K, float A_scale,
+               int8_t A_zero, float B_scale, int8_t B_zero, cudaStream_t stream) {
+  die_on_error(clove_gemm_int8(A_q, B_q, C, M, N, K, A_scale, A_zero, B_scale, B_zero, stream),
+               "gemm_int8");
+}
+
+void gemm_int8_rowcol(const int8_t* A_q, const int8_t* B_q, half* C, int M, int N, int K,
+                      const float* A_row_scale, const float* B_col_scale, cudaStream_t stream) {
+  die_on_error(
+      clove_gemm_int8_rowcol(A_q, B_q, C, M, N, K, A_row_scale, B_col_scale, stream),
+      "gemm_int8_rowcol");
+}
+
+void gemm_int4(const uint8_t* A_q, const half* A_scale, const half* A_zero, const uint8_t* B_q,
+               const half* B_scale, const half* B_zero, half* C, int M, int N, int K,
+               cudaStream_t stream) {
+  die_on_error(
+      clove_gemm_int4(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C, M, N, K, stream),
+      "gemm_int4");
+}
+
+void gemm_fp16_batched(const half* A, const half* B, half* C, int batch, int M, int N, int K,
+                       float alpha, float beta, cudaStream_t stream) {
+  die_on_error(clove_gemm_fp16_batched(A, B, C, batch, M, N, K, alpha, beta, stream),
+               "gemm_fp16_batched");
+}
+
+}  // namespace clove

@@ -1,0 +1,88 @@
+// internal.h -- interfaces between the C-ABI layer (runtime/) and the kernel
+// translation units (kernels/). Not installed; not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "clove/capi.h"
+
+namespace clove {
+namespace kern {
+struct EpiParams;
+struct GemvI8Epi;
+struct SimtEpi;
+}  // namespace kern
+
+namespace rt {
+
+// Records a message for clove_last_error_string() (thread-local) and returns code.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to CLOVE_ERR_CUDA with a message; CLOVE_OK on cudaSuccess.
+int check_cuda(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+  int device;
+  int num_sms;
+  int cc_major, cc_minor;
+};
+// Current device's properties (cached per device). Fails unless cc 10.x.
+int current_device(DeviceInfo* out);
+
+// Dispatch override for tests (clove_set_dispatch_override).
+struct Override {
+  int path;   // 0 auto, 1 tensor core, 2 gemv, 3 simt
+  int bn;     // 0 auto
+  int split;  // 0 auto
+};
+Override get_override();
+
+// ---- tensor-core tile kernels (kernels/gemm_tc_sm100.cu)
+enum TcOp { kTcF16 = 0, kTcI8 = 1 };
+// bn in {32,64,128,256}; split in [1,8] (split > 1 requires bn <= 64);
+// out_bytes 2 (fp16 C) or 4 (int32 C, raw accumulators).
+int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
+                   void* C, int M, int N, int K, const kern::EpiParams& ep,
+                   const DeviceInfo& dev, cudaStream_t stream);
+// True when (op, bn, split, out_bytes) is an instantiated kernel.
+bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
+int read_clear_error_tc();
+
+// ---- GEMV kernels (kernels/gemv_sm100.cu)
+int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                     const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int nc,
+                     int K, long long ldc_row, long long ldc_col, long long ldg_row,
+                     long long ldg_col, const DeviceInfo& dev, cudaStream_t stream);
+size_t gemv_int4_smem(int nc, int K);
+int launch_gemv_int8(const int8_t* A, const int8_t* B, void* C, int rows, int nc, int K,
+                     const kern::GemvI8Epi& ep, const DeviceInfo& dev, cudaStream_t stream);
+size_t gemv_int8_smem(int nc, int K);
+int launch_gemv_f16(const void* A, const void* B, void* C, int rows, int nc, int K, float alpha,
+                    float beta, const DeviceInfo& dev, cudaStream_t stream);
+size_t gemv_f16_smem(int nc, int K);
+int read_clear_error_gemv();
+
+// ---- SIMT fallback + helpers (kernels/fallback_simt.cu)
+int launch_simt_f16(const void* A, const void* B, void* C, int batch, int M, int N, int K,
+                    float alpha, float beta, cudaStream_t stream);
+int launch_simt_i8(const int8_t* A, const int8_t* B, void* C, int M, int N, int K,
+                   const kern::SimtEpi& ep, cudaStream_t stream);
+int launch_simt_i4(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                   const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int M, int N, int K,
+                   cudaStream_t stream);
+int launch_int8_row_sums(const int8_t* A, int32_t* out, int M, int K, cudaStream_t stream);
+int launch_int8_col_sums(const int8_t* B, int32_t* out, int K, int N, cudaStream_t stream);
+int launch_scale_f16(void* C, long long n, float beta, cudaStream_t stream);
+int read_clear_error_simt();
+
+// ---- INT4 tensor-core kernel (kernels/gemm_int4_sm100.cu)
+int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                        const void* Bs, const void* Bz, void* C, int M, int N, int K,
+                        const DeviceInfo& dev, cudaStream_t stream);
+bool gemm_int4_tc_eligible(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                           const void* Bs, const void* Bz, const void* C, int M, int N, int K);
+int read_clear_error_int4();
+
+}  // namespace rt
+}  // namespace clove

@@ -1,0 +1,20 @@
+// tensor_map.h -- CUtensorMap encoding for the TMA-fed kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+namespace clove {
+namespace rt {
+
+// Encodes a 2D row-major tensor [outer, inner] (inner contiguous, rows
+// row_stride_bytes apart) for tiled TMA with a box of [box_outer, box_inner]
+// elements and the given swizzle width in bytes (0 = none, 32, 64, 128).
+// Out-of-bounds box elements read as zero and are clipped on store.
+// Returns CLOVE_OK or an error code with the message recorded.
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_outer, int swizzle_bytes);
+
+}  // namespace rt
+}  // namespace clove

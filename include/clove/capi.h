@@ -1,0 +1,153 @@
+/*
+ * clove/capi.h -- C ABI of the B200 (sm_100a) GEMM hot path.
+ *
+ * Plain pointers and sizes only. Every matrix is row-major and every pointer is
+ * a device pointer owned by the caller; fp16 data is IEEE binary16 passed as
+ * `void*`. Calls are asynchronous on `stream` (a cudaStream_t, NULL = legacy
+ * default stream) and never synchronise. Functions return CLOVE_OK or an error
+ * code; clove_last_error_string() describes the last failure on the calling
+ * thread. Nothing here calls exit().
+ *
+ * Entry points and the reference interfaces they replace (paths in the
+ * clove_compute tree):
+ *   clove_gemm_fp16        clove::gemm_fp16          include/clove/kernels/gemm.cuh:41-49,
+ *                                                    src/kernels/gemm_fp16.cu:277-305
+ *   clove_gemm_int8        clove::gemm_int8          gemm.cuh:57-65, gemm_int8.cu:119-137
+ *   clove_gemm_int8_rowcol (extension: per-row / per-column scales of gemm.cuh:55's formula)
+ *   clove_gemm_int4        clove::gemm_int4          gemm.cuh:77-87, gemm_int4.cu:195-216
+ *   clove_gemm_fp16_batched clove::gemm_fp16_batched gemm.cuh:93-101, gemm_fp16.cu:366-383
+ *   clove_debug_*          (test hooks: raw int32 accumulators for bit-exact checks)
+ *   clove_nsplit_*         (extension: N-split over the GPUs of one node, NCCL all-gather)
+ */
+#ifndef CLOVE_CAPI_H
+#define CLOVE_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define CLOVE_OK 0
+#define CLOVE_ERR_INVALID_ARG 1   /* null pointer, negative size, bad layout    */
+#define CLOVE_ERR_UNSUPPORTED 2   /* shape/alignment this build cannot run      */
+#define CLOVE_ERR_CUDA 3          /* a CUDA runtime/driver call failed          */
+#define CLOVE_ERR_NCCL 4          /* an NCCL call failed                        */
+#define CLOVE_ERR_DEVICE 5        /* device is not an sm_100 GPU                */
+#define CLOVE_ERR_TIMEOUT 6       /* a kernel's bounded wait expired            */
+
+/* INT4 quantisation group along K (gemm.cuh:72). */
+#define CLOVE_INT4_GROUP_SIZE 128
+
+/* Library version string and build architecture. */
+const char* clove_version(void);
+
+/* Description of the last error raised on the calling host thread. */
+const char* clove_last_error_string(void);
+
+/* Reads and clears the device-side error word of the current device (a kernel
+ * whose bounded wait expired sets it). Synchronises the device. *code = 0 when
+ * no kernel reported an error. */
+int clove_get_device_error(int* code);
+
+/* ------------------------------------------------------------------------- */
+/* FP16: C = alpha * A.B + beta * C.  A [M,K], B [K,N], C [M,N] binary16.       */
+/* fp32 accumulation (the reference WMMA kernel accumulates in fp16).          */
+/* beta == 0 never reads C; C may be the residual input when beta != 0.        */
+/* ------------------------------------------------------------------------- */
+int clove_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                    float beta, void* stream);
+
+/* Batched: A [batch,M,K], B [batch,K,N], C [batch,M,N], densely packed. */
+int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N,
+                            int K, float alpha, float beta, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* INT8 (reference signature): C = half( sum_k (A-A_zero)(B-B_zero) * A_scale*B_scale ) */
+/* A_q [M,K] int8, B_q [K,N] int8, C [M,N] binary16; int32 accumulation.        */
+/* ------------------------------------------------------------------------- */
+int clove_gemm_int8(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
+                    float A_scale, int8_t A_zero, float B_scale, int8_t B_zero, void* stream);
+
+/* INT8 with per-row A scales [M] and per-column B scales [N] (fp32, device),
+ * zero points 0: C[m,n] = half( float(acc) * A_row_scale[m] * B_col_scale[n] ). */
+int clove_gemm_int8_rowcol(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
+                           const float* A_row_scale, const float* B_col_scale, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* INT4, per-128-group scales and zero points on both operands, K-packed:       */
+/*   A_q [M,K/2], B_q [N,K/2] bytes; element 2j of a row in the HIGH nibble of   */
+/*   byte j, element 2j+1 in the low nibble; codes unsigned 0..15.              */
+/*   A_scale, A_zero [M,K/128]; B_scale, B_zero [N,K/128] binary16. Zero points */
+/*   hold integer codes (rounded to nearest).                                   */
+/*   G[m,n,g] = sum_{k in g} (a-za)(b-zb)   exact int32                         */
+/*   C[m,n]   = half( sum_g float(G) * sA[m,g] * sB[n,g] )  fp32 sum            */
+/* K must be a multiple of 128.                                                 */
+/* ------------------------------------------------------------------------- */
+int clove_gemm_int4(const uint8_t* A_q, const void* A_scale, const void* A_zero,
+                    const uint8_t* B_q, const void* B_scale, const void* B_zero, void* C, int M,
+                    int N, int K, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Test hooks: exact int32 accumulators through the same kernels.              */
+/* ------------------------------------------------------------------------- */
+/* acc[m,n] = sum_k (A-A_zero)(B-B_zero) (wrapping int32), acc [M,N]. */
+int clove_debug_int8_acc(const int8_t* A_q, const int8_t* B_q, int32_t* acc, int M, int N,
+                         int K, int8_t A_zero, int8_t B_zero, void* stream);
+/* G[m,n,g] as above, G [M,N,K/128]; also writes C like clove_gemm_int4. */
+int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const void* A_zero,
+                               const uint8_t* B_q, const void* B_scale, const void* B_zero,
+                               void* C, int32_t* G, int M, int N, int K, void* stream);
+
+/* Forces a kernel family for subsequent calls from any thread (tests only).
+ * path: 0 = automatic, 1 = tensor-core tiles, 2 = GEMV, 3 = SIMT fallback.
+ * bn: tensor-core N tile (0 = automatic; 32/64/128/256). split: cluster split-K
+ * factor (0 = automatic, 1 = none, 2..8). Returns CLOVE_OK. */
+int clove_set_dispatch_override(int path, int bn, int split);
+
+/* Describes the kernel the automatic dispatch picks for a shape:
+ * dtype 0 = fp16, 1 = int8, 2 = int4. Writes a short name into buf. */
+int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t buflen);
+
+/* ------------------------------------------------------------------------- */
+/* N-split over the GPUs of one node (one process per GPU).                    */
+/* Each rank holds all of A and a column shard of B / C: rank r owns columns    */
+/* [clove_nsplit_col_begin(N,P,r), clove_nsplit_col_begin(N,P,r+1)).            */
+/* The sharded calls compute C_r = A . B_r on this rank's GPU with the          */
+/* single-GPU kernels (no communication). With replicate_C = 1 they then        */
+/* all-gather every rank's C_r over NCCL into the full row-major C [M,N] on     */
+/* every rank. The communicator is created by clove_nsplit_init.                */
+/* ------------------------------------------------------------------------- */
+typedef struct clove_nsplit_ctx clove_nsplit_ctx;
+
+/* Column split: ranks get ceil/floor shares, first (N % P) ranks one extra. */
+int clove_nsplit_col_begin(int N, int nranks, int rank);
+
+/* 128-byte opaque NCCL unique id, produced on one rank and shared out of band. */
+int clove_nsplit_get_unique_id(uint8_t id_out[128]);
+int clove_nsplit_init(clove_nsplit_ctx** ctx, int nranks, int rank, const uint8_t id[128]);
+int clove_nsplit_destroy(clove_nsplit_ctx* ctx);
+int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
+
+/* B_shard [K, N_r] row-major; C_shard [M, N_r]; C_full [M,N] (only with
+ * replicate_C, may be NULL otherwise). */
+int clove_nsplit_gemm_fp16(clove_nsplit_ctx* ctx, const void* A, const void* B_shard,
+                           void* C_shard, void* C_full, int M, int N, int K, float alpha,
+                           int replicate_C, void* stream);
+/* INT4: B_q_shard [N_r, K/2], B_scale/zero_shard [N_r, K/128]. */
+int clove_nsplit_gemm_int4(clove_nsplit_ctx* ctx, const uint8_t* A_q, const void* A_scale,
+                           const void* A_zero, const uint8_t* B_q_shard,
+                           const void* B_scale_shard, const void* B_zero_shard, void* C_shard,
+                           void* C_full, int M, int N, int K, int replicate_C, void* stream);
+/* INT8 row/col: B_q_shard [K, N_r], B_col_scale_shard [N_r]. */
+int clove_nsplit_gemm_int8_rowcol(clove_nsplit_ctx* ctx, const int8_t* A_q,
+                                  const int8_t* B_q_shard, const float* A_row_scale,
+                                  const float* B_col_scale_shard, void* C_shard, void* C_full,
+                                  int M, int N, int K, int replicate_C, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CLOVE_CAPI_H */

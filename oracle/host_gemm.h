@@ -1,0 +1,106 @@
+/*
+ * host_gemm.h -- CPU oracle for the clove GEMM hot path (TEST INFRASTRUCTURE ONLY).
+ *
+ * This library is the parity checker and the timed CPU baseline. It is never
+ * linked into, loaded by or called from the product path (clove_compute_b200/).
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use it.
+ *
+ * It restates, in plain C with fp32 / int32 arithmetic, what the reference's
+ * GEMM entry points compute (reference paths relative to the clove_compute tree):
+ *
+ *   fp16  C = alpha*A.B + beta*C, fp32 accumulate     src/kernels/gemm_fp16.cu:241-270
+ *         (the naive kernel's math; the WMMA kernel :30-215 computes the same
+ *          product but accumulates in fp16, so it is only checked within tolerance)
+ *   int8  int32 sum (a-za)(b-zb), * A_scale*B_scale   src/kernels/gemm_int8.cu:87-114
+ *   int4  per-128-group int32 G = sum (a-za)(b-zb),   include/clove/kernels/gemm.cuh:67-87
+ *         C = sum_g sA*sB*G                           (documented intent; see
+ *                                                     clove_oracle_gemm_int4_refcompat
+ *                                                     for what gemm_int4.cu:45-193 does)
+ *
+ * Parity pinning: the reference ships no golden vectors or known-answer tests
+ * for any of these paths (its only check is cuBLAS with fp16 accumulation,
+ * tests/test_gemm.cu:64-93). The fp16 and int4-refcompat restatements are
+ * pinned against the reference kernels themselves run on a B200 (fixtures in
+ * tests/golden/). The int8 restatement is pinned only by known-answer tests
+ * written here: its reference kernel reads shared memory out of bounds
+ * (gemm_int8.cu:77,84) and is never run -- int8 parity is unpinned by the
+ * reference.
+ *
+ * All entry points compute only output rows [row_begin, row_end) so that the
+ * CPU baseline can time a bounded sample; nthreads <= 0 means "all cores".
+ * Every output element is produced by one thread in a fixed k / group order,
+ * so results do not depend on the thread count.
+ */
+#ifndef CLOVE_ORACLE_HOST_GEMM_H
+#define CLOVE_ORACLE_HOST_GEMM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* IEEE binary16 <-> binary32 (round to nearest even, like __float2half). */
+float clove_oracle_h2f(uint16_t h);
+uint16_t clove_oracle_f2h(float f);
+void clove_oracle_h2f_array(const uint16_t* in, float* out, int64_t n);
+void clove_oracle_f2h_array(const float* in, uint16_t* out, int64_t n);
+
+/* Number of threads the oracle uses when nthreads <= 0. */
+int clove_oracle_max_threads(void);
+
+/* fp16: C[m,n] = half(alpha * sum_k A[m,k]*B[k,n] + beta * C[m,n]), fp32 math.
+ * A [M,K], B [K,N], C [M,N], all row-major binary16. beta == 0 never reads C. */
+void clove_oracle_gemm_fp16(const uint16_t* A, const uint16_t* B, uint16_t* C,
+                            int M, int N, int K, float alpha, float beta,
+                            int row_begin, int row_end, int nthreads);
+
+/* int8: acc[m,n] = sum_k (A[m,k]-za)(B[k,n]-zb) in wrapping int32.
+ * A [M,K], B [K,N] row-major int8. */
+void clove_oracle_int8_acc(const int8_t* A, const int8_t* B, int32_t* acc,
+                           int M, int N, int K, int za, int zb,
+                           int row_begin, int row_end, int nthreads);
+
+/* int8, per-tensor (the reference signature): C = half(float(acc) * (sA*sB)). */
+void clove_oracle_gemm_int8(const int8_t* A, const int8_t* B, uint16_t* C,
+                            int M, int N, int K, float sA, int za, float sB, int zb,
+                            int row_begin, int row_end, int nthreads);
+
+/* int8, per-row A / per-column B fp32 scales, zero points 0:
+ * C = half(float(acc) * sA[m] * sB[n]). */
+void clove_oracle_gemm_int8_rowcol(const int8_t* A, const int8_t* B, uint16_t* C,
+                                   int M, int N, int K,
+                                   const float* sA_row, const float* sB_col,
+                                   int row_begin, int row_end, int nthreads);
+
+/* int4 group accumulators, K-packed layout on both operands:
+ *   Aq [M,K/2] bytes, element 2j in the high nibble of byte j, 2j+1 in the low;
+ *   Az [M,K/128], Bq [N,K/2], Bz [N,K/128] binary16 zero points (rounded to the
+ *   nearest integer);  G[m,n,g] = sum_{k in group g} (a-za)(b-zb), int32.
+ * K must be a multiple of 128. */
+void clove_oracle_int4_group_acc(const uint8_t* Aq, const uint16_t* Az,
+                                 const uint8_t* Bq, const uint16_t* Bz,
+                                 int32_t* G, int M, int N, int K,
+                                 int row_begin, int row_end, int nthreads);
+
+/* int4 GEMM: C[m,n] = half( sum_g float(G[m,n,g]) * (sA[m,g]*sB[n,g]) ), the
+ * fp32 sum taken in increasing g. Scales As [M,K/128], Bs [N,K/128] binary16. */
+void clove_oracle_gemm_int4(const uint8_t* Aq, const uint16_t* As, const uint16_t* Az,
+                            const uint8_t* Bq, const uint16_t* Bs, const uint16_t* Bz,
+                            uint16_t* C, int M, int N, int K,
+                            int row_begin, int row_end, int nthreads);
+
+/* What the reference int4 kernel computes (gemm_int4.cu:45-193): signed codes
+ * (nibble-8), zero points ignored, B packed along N as [K,N/2] (high nibble =
+ * even n), B scales [K/128,N], and the whole K-sum scaled by the scales of the
+ * LAST 64-wide K tile's group only. Used to explain the reference kernel's
+ * output, never as the product's semantics. */
+void clove_oracle_gemm_int4_refcompat(const uint8_t* Aq, const uint16_t* As,
+                                      const uint8_t* Bq_kn, const uint16_t* Bs_kn,
+                                      uint16_t* C, int M, int N, int K,
+                                      int row_begin, int row_end, int nthreads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,57 @@
+"""CPU checks of the product library: it loads, exports every entry point that
+include/clove/capi.h declares, and its pure host logic behaves (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    txt = open(os.path.join(ROOT, "include", "clove", "capi.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(clove_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_header_declares_expected_entry_points():
+    names = _declared_functions()
+    for n in ["clove_gemm_fp16", "clove_gemm_int8", "clove_gemm_int4", "clove_gemm_fp16_batched",
+              "clove_gemm_int8_rowcol", "clove_debug_int4_group_acc", "clove_last_error_string"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(clove_lib):
+    lib = ctypes.CDLL(clove_lib.library_path())
+    missing = [n for n in _declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header(clove_lib):
+    from clove_compute_b200._lib import SIGNATURES
+    assert set(_declared_functions()) <= set(SIGNATURES)
+
+
+def test_version_and_error_string(clove_lib):
+    lib = clove_lib.lib()
+    assert b"sm_100a" in lib.clove_version()
+    assert isinstance(lib.clove_last_error_string(), bytes)
+
+
+@pytest.mark.parametrize("N,P", [(2048, 8), (11008, 8), (7, 8), (0, 4), (13, 3), (1, 2)])
+def test_nsplit_column_partition(clove_lib, N, P):
+    bounds = [clove_lib.col_begin(N, P, r) for r in range(P + 1)]
+    assert bounds[0] == 0 and bounds[-1] == N
+    widths = [b - a for a, b in zip(bounds, bounds[1:])]
+    assert all(w >= 0 for w in widths)
+    assert max(widths) - min(widths) <= 1
+    assert widths == sorted(widths, reverse=True)  # extra columns go to the first ranks
+
+
+def test_dispatch_description_without_gpu(clove_lib):
+    d = clove_lib.describe_dispatch("fp16", 11008, 2048, 4096)
+    assert d.startswith("tc_f16")
+    assert clove_lib.describe_dispatch("int4", 4096, 1, 4096).startswith("gemv_int4")
+    assert clove_lib.describe_dispatch("int8", 4096, 32, 4096).startswith("tc_int8")
+    assert "split" in clove_lib.describe_dispatch("int8", 4096, 32, 4096)

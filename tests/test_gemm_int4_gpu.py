@@ -1,0 +1,76 @@
+"""INT4 parity on the GPU: per-group int32 accumulators G bit-exact against the
+oracle (clove_debug_int4_group_acc), C within the 1e-2 relative Frobenius
+contract of the fp32 oracle (tight bound 2e-3)."""
+import numpy as np
+import pytest
+
+from clove_compute_b200 import workloads as wl
+from tests.gpu_util import dev, host, rel_fro
+
+pytestmark = pytest.mark.gpu
+TOL_TIGHT = 2e-3
+
+
+@pytest.fixture(autouse=True)
+def _reset(clove_lib):
+    yield
+    clove_lib.set_dispatch_override(0, 0, 0)
+
+
+def _ops_dev(op):
+    return (dev(op.A_q), dev(op.A_scale), dev(op.A_zero), dev(op.B_q), dev(op.B_scale),
+            dev(op.B_zero))
+
+
+def _check(cc, oracle, M, N, K, path=0, seed=0, check_g=True):
+    op = wl.int4_operands(M, N, K, seed=seed)
+    cc.set_dispatch_override(path, 0, 0)
+    args = _ops_dev(op)
+    C = host(cc.gemm_int4(*args))
+    ref = oracle.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K)
+    err = rel_fro(C, ref)
+    assert err < 1e-2 and err < TOL_TIGHT, err
+    if check_g:
+        C2, G = cc.debug_int4_group_acc(*args)
+        Gref = oracle.int4_group_acc(op.A_q, op.A_zero, op.B_q, op.B_zero, K)
+        np.testing.assert_array_equal(host(G), Gref)
+        assert rel_fro(host(C2), ref) < TOL_TIGHT
+    assert cc.device_error() == 0
+
+
+def test_config2_decode_gemv(clove_lib, oracle_mod, cuda):
+    """weights A [4096, 4096] int4, activations B with N = 1."""
+    _check(clove_lib, oracle_mod, 4096, 1, 4096)
+
+
+@pytest.mark.parametrize("N", [2, 3, 4, 8])
+def test_gemv_small_n(clove_lib, oracle_mod, cuda, N):
+    _check(clove_lib, oracle_mod, 1000, N, 2048, seed=N)
+
+
+@pytest.mark.parametrize("K", [128, 384, 8192, 12288])
+def test_gemv_k_sizes(clove_lib, oracle_mod, cuda, K):
+    _check(clove_lib, oracle_mod, 300, 1, K, seed=K)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_gemv_small_m_transposed(clove_lib, oracle_mod, cuda, M):
+    _check(clove_lib, oracle_mod, M, 600, 1024, seed=M)
+
+
+def test_large_shape(clove_lib, oracle_mod, cuda):
+    _check(clove_lib, oracle_mod, 256, 192, 1024, seed=5)
+
+
+def test_simt_path(clove_lib, oracle_mod, cuda):
+    _check(clove_lib, oracle_mod, 40, 24, 512, path=3, seed=6)
+
+
+def test_k_not_multiple_of_group_rejected(clove_lib, cuda):
+    import torch
+    from clove_compute_b200 import CloveError
+    M, N, K = 4, 4, 192
+    z = lambda r: torch.zeros((r, 1), dtype=torch.float16, device="cuda")
+    with pytest.raises((CloveError, ValueError)):
+        clove_lib.gemm_int4(torch.zeros((M, K // 2), dtype=torch.uint8, device="cuda"), z(M), z(M),
+                            torch.zeros((N, K // 2), dtype=torch.uint8, device="cuda"), z(N), z(N))
