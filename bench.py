@@ -67,7 +67,7 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock",
     }
 
-    def __init__(self, index: int, period_s: float = 0.002):
+    def __init__(self, index: int, period_s: float = 0.0005):
         self.samples = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -89,7 +89,7 @@ class ClockSampler:
             try:
                 sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
                 rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
+                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0 if len(self.samples) % 8 == 0 else -1.0
                 self.samples.append((sm, rs, pw))
             except Exception:
                 pass
@@ -119,6 +119,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(s[0] for s in self.samples),
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
                 "power_w_max": round(max(s[2] for s in self.samples), 1),
+                "window": "warm-up and timed steps",
                 "samples": len(self.samples)}
 
 
@@ -213,16 +214,26 @@ def _secondary(cc, torch, peaks):
     stream = torch.cuda.current_stream()
 
     def timeit(fn, n_copies, reps, warm=3):
-        for i in range(warm):
+        """Seconds per call: the n_copies rotating calls are captured once in a CUDA
+        graph and replayed, so host launch overhead does not pace the GPU."""
+        for i in range(max(warm, n_copies)):
             fn(i % n_copies)
         torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n_copies):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
+        n_rep = max(2, reps // n_copies)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(reps):
-            fn(i % n_copies)
+        for _ in range(n_rep):
+            g.replay()
         e1.record(stream)
         e1.synchronize()
-        return e0.elapsed_time(e1) / reps * 1e-3  # seconds per call
+        del g
+        return e0.elapsed_time(e1) / (n_rep * n_copies) * 1e-3  # seconds per call
 
     # config 2: int4 decode GEMV, 4096x4096 weights, N = 1
     M, N, K = 4096, 1, 4096
@@ -336,11 +347,10 @@ def run_gpu(args):
         return float(t.item())
 
     # ---------------- device-resident timing, per-launch events
-    for _ in range(args.warmup):
-        step(X)
-    barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
     with ClockSampler(local) as clk:
+        for _ in range(args.warmup):
+            step(X)
         barrier()
         ev[0].record(stream)
         for s in range(args.steps):
@@ -354,6 +364,12 @@ def run_gpu(args):
     t_dn = sum(ev[2 * s + 1].elapsed_time(ev[2 * s + 2]) for s in range(args.steps)) * 1e-3
     t_max = max_over_ranks(t_dev)
     value = FLOP_STEP * args.steps * world / t_max / 1e12
+
+    if args.kernel_only:
+        # Profiling mode: the warm-up and timed FFN launches only.
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     # ---------------- end to end through the public API, host buffers
     X_pin = torch.from_numpy(X_h).pin_memory()
@@ -432,11 +448,13 @@ def run_gpu(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["clove", "reference"], default="clove")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="run only the warm-up and timed FFN GEMMs (for ncu), print nothing")
     ap.add_argument("--cpu-frac", type=int, default=32,
                     help="CPU sample = 1/cpu_frac of each GEMM's rows")
     args = ap.parse_args()
