@@ -88,11 +88,6 @@ Override get_override() {
 // ---------------------------------------------------------------------------
 // Tile-shape policy for the tensor-core kernels
 // ---------------------------------------------------------------------------
-struct TcPlan {
-  int bn;
-  int split;
-};
-
 // Per-tile time is roughly proportional to BN; narrower tiles pay extra for
 // re-reading A. Choose the BN that minimises waves x BN x penalty; when even
 // BN=64 leaves most SMs idle, split K over a cluster.

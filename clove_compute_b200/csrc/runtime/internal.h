@@ -38,6 +38,13 @@ struct Override {
 };
 Override get_override();
 
+// Tile shape chosen for a tensor-core call (capi.cpp).
+struct TcPlan {
+  int bn;
+  int split;
+};
+TcPlan plan_tc(int M, int N, int K, int elem, int num_sms);
+
 // ---- tensor-core tile kernels (kernels/gemm_tc_sm100.cu)
 enum TcOp { kTcF16 = 0, kTcI8 = 1 };
 // bn in {32,64,128,256}; split in [1,8] (split > 1 requires bn <= 64);

@@ -71,6 +71,22 @@ int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, in
 int clove_gemm_int8(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
                     float A_scale, int8_t A_zero, float B_scale, int8_t B_zero, void* stream);
 
+/* No-allocation variant of clove_gemm_int8 (same arguments and results). It has no
+ * counterpart in the reference. For callers that cannot let a library allocate
+ * device memory -- e.g. serving runtimes that reserve all of HBM for their own
+ * pools, where a stray allocation can fail mid-serving: the zero-point row /
+ * column sums that clove_gemm_int8 keeps in cudaMallocAsync scratch live here in
+ * a fixed array compiled into the library (CLOVE_NOALLOC_MAX_SUMS int32 entries,
+ * 256 KiB on every GPU that loads the library). Requires M + N <=
+ * CLOVE_NOALLOC_MAX_SUMS on the tensor-core path, else CLOVE_ERR_UNSUPPORTED.
+ * The first call on each device looks up the array's device address; make it
+ * before any stream capture. Calls share the array: calls that overlap on the
+ * GPU race. */
+#define CLOVE_NOALLOC_MAX_SUMS 65536
+int clove_gemm_int8_noalloc(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
+                            float A_scale, int8_t A_zero, float B_scale, int8_t B_zero,
+                            void* stream);
+
 /* INT8 with per-row A scales [M] and per-column B scales [N] (fp32, device),
  * zero points 0: C[m,n] = half( float(acc) * A_row_scale[m] * B_col_scale[n] ). */
 int clove_gemm_int8_rowcol(const int8_t* A_q, const int8_t* B_q, void* C, int M, int N, int K,
