@@ -238,6 +238,8 @@ def test_oracle_vs_reference_fp16_golden(oracle_mod, fname):
     # path accumulates in fp32 like the oracle.
     tol = float(d["tol"])
     assert oracle_mod.rel_frobenius(C, out) < tol
+    if "naive" in fname:  # same arithmetic as the oracle: bit for bit
+        assert np.array_equal(C.view(np.uint16), out.view(np.uint16))
 
 
 @pytest.mark.parametrize("fname", _golden_files("ref_int4_") or ["<none>"])
