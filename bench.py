@@ -126,6 +126,15 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU reference arm / baseline
 # ---------------------------------------------------------------------------
+def _host_threads() -> int:
+    """Every core this process may run on (torchrun exports OMP_NUM_THREADS=1, so
+    the oracle is given the thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def _cpu_ffn_sample(frac_div: int, min_seconds: float, max_reps: int):
     """Times the C oracle on rows [0, M/frac_div) of both FFN GEMMs, all cores."""
     import numpy as np
@@ -138,18 +147,19 @@ def _cpu_ffn_sample(frac_div: int, min_seconds: float, max_reps: int):
     ru = UP[0] // frac_div
     rd = DOWN[0] // frac_div
     flops = 2 * ru * UP[1] * UP[2] + 2 * rd * DOWN[1] * DOWN[2]
+    nt = _host_threads()
     times = []
     t_all = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        oracle.gemm_fp16(A_up, X, Cu, rows=(0, ru))
+        oracle.gemm_fp16(A_up, X, Cu, rows=(0, ru), nthreads=nt)
         # the down projection consumes the full C_up (only ru rows are fresh)
-        oracle.gemm_fp16(A_dn, Cu, rows=(0, rd))
+        oracle.gemm_fp16(A_dn, Cu, rows=(0, rd), nthreads=nt)
         times.append(time.perf_counter() - t0)
         if (time.perf_counter() - t_all >= min_seconds) or len(times) >= max_reps:
             break
     t = statistics.median(times)
-    return {"value": round(flops / t / 1e12, 5), "unit": "TFLOPS", "cores": oracle.max_threads(),
+    return {"value": round(flops / t / 1e12, 5), "unit": "TFLOPS", "cores": nt,
             "kind": "port",
             "sample": f"rows [0,{ru}) of the up GEMM and [0,{rd}) of the down GEMM "
                       f"(1/{frac_div} of the step, {flops / 1e9:.1f} GFLOP), median of {len(times)}",
@@ -171,9 +181,11 @@ def run_reference(args):
     ru, rd = UP[0] // frac, DOWN[0] // frac
     flops = 2 * ru * UP[1] * UP[2] + 2 * rd * DOWN[1] * DOWN[2]
 
+    nt = _host_threads()
+
     def step():
-        oracle.gemm_fp16(A_up, X, Cu, rows=(0, ru))
-        oracle.gemm_fp16(A_dn, Cu, rows=(0, rd))
+        oracle.gemm_fp16(A_up, X, Cu, rows=(0, ru), nthreads=nt)
+        oracle.gemm_fp16(A_dn, Cu, rows=(0, rd), nthreads=nt)
 
     for _ in range(args.warmup):
         step()
@@ -182,7 +194,7 @@ def run_reference(args):
         step()
     dt = time.perf_counter() - t0
     v = flops * args.steps / dt / 1e12
-    cores = oracle.max_threads()
+    cores = nt
     sample = (f"rows [0,{ru}) of the up GEMM and [0,{rd}) of the down GEMM per step "
               f"(1/{frac} of the FFN step, {flops / 1e9:.1f} GFLOP)")
     line = {
@@ -298,6 +310,33 @@ def _secondary(cc, torch, peaks):
             "TOPS": round(2 * n ** 3 / t / 1e12, 1),
             "frac_of_2x_bf16_peak": round(2 * n ** 3 / t / 1e12 / (2 * peaks["bf16_tflops"]), 4)}
     return out
+
+
+def run_case(args):
+    """Profiling mode (--case): a few plain launches of one secondary configuration,
+    no graphs, no output; the command line ncu captures."""
+    import numpy as np
+    import torch
+    import clove_compute_b200 as cc
+    from clove_compute_b200 import workloads as wl
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    if args.case == "int4_decode":
+        op = wl.int4_operands(4096, 1, 4096, seed=0)
+        t = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
+        fn = lambda: cc.gemm_int4(*t)
+    elif args.case == "int8_batch32":
+        A, B, sA, sB = wl.int8_operands(4096, 32, 4096, seed=0)
+        t = [dev(A), dev(B), dev(sA), dev(sB)]
+        fn = lambda: cc.gemm_int8_rowcol(*t)
+    elif args.case == "fp16_1024":
+        A, B = wl.fp16_operands(1024, 1024, 1024, seed=0)
+        t = [dev(A), dev(B)]
+        fn = lambda: cc.gemm_fp16(*t)
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
 
 
 def run_gpu(args):
@@ -453,6 +492,8 @@ def main():
     ap.add_argument("--impl", choices=["clove", "reference"], default="clove")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024"],
+                    help="profiling mode: warm-up + steps plain launches of one secondary config")
     ap.add_argument("--kernel-only", action="store_true",
                     help="run only the warm-up and timed FFN GEMMs (for ncu), print nothing")
     ap.add_argument("--cpu-frac", type=int, default=32,
@@ -460,7 +501,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -9,11 +9,11 @@ CLOVE_DEFINE_ERROR_READER(read_clear_error_gemv)
 
 namespace {
 
-// Enough CTAs to put every row pair in flight at once, at most 8 CTAs per SM.
-unsigned gemv_grid(int rows, const DeviceInfo& dev) {
+// Enough CTAs to put every row block in flight at once, at most 8 CTAs per SM.
+unsigned gemv_grid(int rows, const DeviceInfo& dev, int rows_per_warp = kern::kGemvRowsPerWarp) {
   const int warps_per_cta = kern::kGemvThreads / 32;
-  const long long row_pairs = (rows + kern::kGemvRowsPerWarp - 1) / kern::kGemvRowsPerWarp;
-  long long ctas = (row_pairs + warps_per_cta - 1) / warps_per_cta;
+  const long long row_blocks = (rows + rows_per_warp - 1) / rows_per_warp;
+  long long ctas = (row_blocks + warps_per_cta - 1) / warps_per_cta;
   const long long cap = static_cast<long long>(dev.num_sms) * 8;
   if (ctas > cap) ctas = cap;
   if (ctas < 1) ctas = 1;
@@ -31,15 +31,52 @@ int prepare(KernelT kernel, size_t smem) {
   return CLOVE_OK;
 }
 
+// Launch with programmatic stream serialisation: the kernel may be scheduled while
+// its predecessor on the stream drains; it orders every global access after
+// griddepcontrol.wait, so results are those of a plain launch.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), unsigned grid, size_t smem, cudaStream_t stream,
+               const char* what, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kern::kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args...), what);
+}
+
+template <int NC, int P>
+int gemv_int4_reg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                  const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int K,
+                  long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col,
+                  const DeviceInfo& dev, cudaStream_t stream) {
+  constexpr int R = 2;
+  return launch_pdl(kern::gemv_int4_reg_kernel<NC, P, R>, gemv_grid(rows, dev, R), 0, stream,
+                    "gemv_int4_reg launch", Aq, static_cast<const __half*>(As),
+                    static_cast<const __half*>(Az), Bq, static_cast<const __half*>(Bs),
+                    static_cast<const __half*>(Bz), static_cast<__half*>(C), Gdbg, rows, K,
+                    ldc_row, ldc_col, ldg_row, ldg_col);
+}
+
 template <int NC>
 int gemv_int4_nc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                  const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int K,
                  long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col,
                  const DeviceInfo& dev, cudaStream_t stream) {
   const size_t smem = kern::gemv_int4_smem_bytes(NC, K);
-  int rc = prepare(kern::gemv_int4_kernel<NC>, smem);
+  // One row per warp while every row still gets its own resident warp (the whole
+  // matrix in flight at once); two rows per warp beyond that.
+  const bool one = rows <= dev.num_sms * 32;
+  int rc = one ? prepare(kern::gemv_int4_kernel<NC, 1>, smem)
+               : prepare(kern::gemv_int4_kernel<NC, 2>, smem);
   if (rc) return rc;
-  kern::gemv_int4_kernel<NC><<<gemv_grid(rows, dev), kern::kGemvThreads, smem, stream>>>(
+  auto k = one ? kern::gemv_int4_kernel<NC, 1> : kern::gemv_int4_kernel<NC, 2>;
+  k<<<gemv_grid(rows, dev, one ? 1 : 2), kern::kGemvThreads, smem, stream>>>(
       Aq, static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
       static_cast<const __half*>(Bs), static_cast<const __half*>(Bz), static_cast<__half*>(C),
       Gdbg, rows, K, ldc_row, ldc_col, ldg_row, ldg_col);
@@ -92,6 +129,18 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
                      const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int nc,
                      int K, long long ldc_row, long long ldc_col, long long ldg_row,
                      long long ldg_col, const DeviceInfo& dev, cudaStream_t stream) {
+  // Register-resident B when this lane's share of the vectors fits (nc * P <= 8,
+  // P = 1024-element windows per row) and the 16-byte B loads are aligned.
+  const int P = (K + 1023) / 1024;
+  if (nc * P <= 8 && (reinterpret_cast<uintptr_t>(Bq) & 15u) == 0) {
+#define REG(n, p)                                                                          \
+  if (nc == n && P == p)                                                                    \
+    return gemv_int4_reg<n, p>(Aq, As, Az, Bq, Bs, Bz, C, Gdbg, rows, K, ldc_row, ldc_col, \
+                               ldg_row, ldg_col, dev, stream);
+    REG(1, 1) REG(1, 2) REG(1, 3) REG(1, 4) REG(1, 5) REG(1, 6) REG(1, 7) REG(1, 8)
+    REG(2, 1) REG(2, 2) REG(2, 3) REG(2, 4)
+#undef REG
+  }
 #define CALL(n)                                                                                  \
   gemv_int4_nc<n>(Aq, As, Az, Bq, Bs, Bz, C, Gdbg, rows, K, ldc_row, ldc_col, ldg_row, ldg_col, \
                   dev, stream)

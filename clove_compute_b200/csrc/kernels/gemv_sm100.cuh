@@ -48,7 +48,7 @@ __host__ __device__ constexpr size_t gemv_int4_smem_bytes(int nc, int K) {
   return static_cast<size_t>(nc) * (static_cast<size_t>(K) + 2 * 4 * (K / 128));
 }
 
-template <int NC>
+template <int NC, int R>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_int4_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
                      const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
@@ -59,20 +59,57 @@ __global__ void __launch_bounds__(kGemvThreads)
   const int NG = K >> 7;          // groups per row
   const int NCH = K >> 5;         // 16-byte chunks per row
   const int KB = K >> 1;          // bytes per row
-  uint32_t* bp = reinterpret_cast<uint32_t*>(smem);                    // [NC][NCH*8]
+  uint32_t* bp = reinterpret_cast<uint32_t*>(smem);                          // [NC][NCH*8]
   float* sb = reinterpret_cast<float*>(smem + static_cast<size_t>(NC) * K);  // [NC][NG]
   int* zs = reinterpret_cast<int*>(sb + NC * NG);                            // [NC][NG]
 
-  // ---- unpack the B vectors (tiny: NC * K/2 bytes)
+  const int lane = static_cast<int>(dev::lane_idx());
+  const int gwarp = static_cast<int>(blockIdx.x * (blockDim.x >> 5) + dev::warp_idx());
+  const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
+  const int passes = (NCH + 31) >> 5;  // 512-byte windows per row
+
+  // Loads of one 4-window slab (up to 2 KB of a row) for the R rows of a block.
+  uint4 v[R][4];
+  __half2 zsA[R][4];
+  auto load_slab = [&](int row_blk, int p0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m = row_blk + r;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int ch = (p0 + j) * 32 + lane;
+        if (m < rows && p0 + j < passes && ch < NCH) {
+          v[r][j] = dev::ld_nc_v4(Aq + static_cast<size_t>(m) * KB + static_cast<size_t>(ch) * 16);
+          const size_t gi = static_cast<size_t>(m) * NG + (ch >> 2);
+          zsA[r][j] = __halves2half2(Az[gi], As[gi]);
+        } else {
+          v[r][j] = make_uint4(0u, 0u, 0u, 0u);
+          zsA[r][j] = __halves2half2(__float2half(0.f), __float2half(0.f));
+        }
+      }
+    }
+  };
+
+  // The first slab of this warp's first rows is requested before the B vectors are
+  // touched, so its HBM latency overlaps the unpacking below.
+  const int first_row = gwarp * R;
+  load_slab(first_row, 0);
+
+  // ---- unpack the B vectors (tiny: NC * K/2 bytes). Word order per 16-byte chunk:
+  // word 2w = the 4 even-k codes (high nibbles) of A word w, 2w+1 the odd-k codes.
+  // The 32 consecutive words a warp produces per iteration are exactly one 128-code
+  // group (NC*NCH*8 and blockDim are multiples of 32), so the warp also reduces the
+  // group's sum of (b - zB) for the zero-point term.
   for (int idx = threadIdx.x; idx < NC * NCH * 8; idx += blockDim.x) {
     const int n = idx / (NCH * 8);
     const int r = idx - n * NCH * 8;
-    const int ch = r >> 3;         // chunk
-    const int w = (r >> 1) & 3;    // A word within the chunk
-    const int odd = r & 1;         // 0: high nibbles (even k), 1: low nibbles (odd k)
+    const int ch = r >> 3;
+    const int w = (r >> 1) & 3;
+    const int odd = r & 1;
     const int byte0 = ch * 16 + w * 4;
+    const int g = ch >> 2;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(Bq + static_cast<size_t>(n) * KB + byte0);
-    const int zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (byte0 * 2) / 128]);
+    const int zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + g]);
     uint32_t packed = 0;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -81,53 +118,25 @@ __global__ void __launch_bounds__(kGemvThreads)
       packed |= (static_cast<uint32_t>(code - zb) & 0xffu) << (8 * t);
     }
     bp[n * NCH * 8 + r] = packed;
-  }
-  for (int idx = threadIdx.x; idx < NC * NG; idx += blockDim.x) {
-    const int n = idx / NG;
-    const int g = idx - n * NG;
-    const uint8_t* row = Bq + static_cast<size_t>(n) * KB + g * 64;
-    const int zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + g]);
-    int s = 0;
-    for (int j = 0; j < 64; ++j) s += (row[j] >> 4) + (row[j] & 0xf);
-    zs[idx] = s - 128 * zb;
-    sb[idx] = __half2float(Bs[static_cast<size_t>(n) * NG + g]);
+    const int gsum = warp_sum_i32(__dp4a(static_cast<int>(packed), 0x01010101, 0));
+    if (lane == 0) {
+      zs[n * NG + g] = gsum;
+      sb[n * NG + g] = __half2float(Bs[static_cast<size_t>(n) * NG + g]);
+    }
   }
   __syncthreads();
 
-  const int lane = static_cast<int>(dev::lane_idx());
-  const int gwarp = static_cast<int>(blockIdx.x * (blockDim.x >> 5) + dev::warp_idx());
-  const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
-  const int passes = (NCH + 31) >> 5;  // 512-byte windows per row
-
-  for (int row0 = gwarp * kGemvRowsPerWarp; row0 < rows; row0 += nwarps * kGemvRowsPerWarp) {
-    float acc[kGemvRowsPerWarp][NC];
+  for (int row0 = first_row; row0 < rows; row0 += nwarps * R) {
+    float acc[R][NC];
 #pragma unroll
-    for (int r = 0; r < kGemvRowsPerWarp; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int n = 0; n < NC; ++n) acc[r][n] = 0.f;
 
     for (int p0 = 0; p0 < passes; p0 += 4) {
-      // Issue every load of this window for both rows first.
-      uint4 v[kGemvRowsPerWarp][4];
-      __half2 zsA[kGemvRowsPerWarp][4];
+      if (row0 != first_row || p0 != 0) load_slab(row0, p0);
 #pragma unroll
-      for (int r = 0; r < kGemvRowsPerWarp; ++r) {
-        const int m = row0 + r;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int ch = (p0 + j) * 32 + lane;
-          if (m < rows && p0 + j < passes && ch < NCH) {
-            v[r][j] = dev::ld_nc_v4(Aq + static_cast<size_t>(m) * KB + static_cast<size_t>(ch) * 16);
-            const size_t gi = static_cast<size_t>(m) * NG + (ch >> 2);
-            zsA[r][j] = __halves2half2(Az[gi], As[gi]);
-          } else {
-            v[r][j] = make_uint4(0u, 0u, 0u, 0u);
-            zsA[r][j] = __halves2half2(__float2half(0.f), __float2half(0.f));
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kGemvRowsPerWarp; ++r) {
+      for (int r = 0; r < R; ++r) {
         const int m = row0 + r;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -136,21 +145,26 @@ __global__ void __launch_bounds__(kGemvThreads)
           const bool valid = ch < NCH;
           const int chc = valid ? ch : 0;
           const uint32_t w[4] = {v[r][j].x, v[r][j].y, v[r][j].z, v[r][j].w};
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            hi[u] = (w[u] >> 4) & 0x0f0f0f0fu;
+            lo[u] = w[u] & 0x0f0f0f0fu;
+          }
 #pragma unroll
           for (int n = 0; n < NC; ++n) {
             const uint4* b4 = reinterpret_cast<const uint4*>(bp + n * NCH * 8 + chc * 8);
             const uint4 b0 = b4[0];
             const uint4 b1 = b4[1];
-            int d = 0;
-            d = __dp4a(static_cast<int>((w[0] >> 4) & 0x0f0f0f0fu), static_cast<int>(b0.x), d);
-            d = __dp4a(static_cast<int>(w[0] & 0x0f0f0f0fu), static_cast<int>(b0.y), d);
-            d = __dp4a(static_cast<int>((w[1] >> 4) & 0x0f0f0f0fu), static_cast<int>(b0.z), d);
-            d = __dp4a(static_cast<int>(w[1] & 0x0f0f0f0fu), static_cast<int>(b0.w), d);
-            d = __dp4a(static_cast<int>((w[2] >> 4) & 0x0f0f0f0fu), static_cast<int>(b1.x), d);
-            d = __dp4a(static_cast<int>(w[2] & 0x0f0f0f0fu), static_cast<int>(b1.y), d);
-            d = __dp4a(static_cast<int>((w[3] >> 4) & 0x0f0f0f0fu), static_cast<int>(b1.z), d);
-            d = __dp4a(static_cast<int>(w[3] & 0x0f0f0f0fu), static_cast<int>(b1.w), d);
-            if (!valid) d = 0;
+            int d0 = __dp4a(static_cast<int>(hi[0]), static_cast<int>(b0.x), 0);
+            int d1 = __dp4a(static_cast<int>(lo[0]), static_cast<int>(b0.y), 0);
+            d0 = __dp4a(static_cast<int>(hi[1]), static_cast<int>(b0.z), d0);
+            d1 = __dp4a(static_cast<int>(lo[1]), static_cast<int>(b0.w), d1);
+            d0 = __dp4a(static_cast<int>(hi[2]), static_cast<int>(b1.x), d0);
+            d1 = __dp4a(static_cast<int>(lo[2]), static_cast<int>(b1.y), d1);
+            d0 = __dp4a(static_cast<int>(hi[3]), static_cast<int>(b1.z), d0);
+            d1 = __dp4a(static_cast<int>(lo[3]), static_cast<int>(b1.w), d1);
+            int d = valid ? d0 + d1 : 0;
             // The 4 lanes of a group (lane & ~3 .. +3) hold its 4 chunks.
             d += __shfl_xor_sync(0xffffffffu, d, 1);
             d += __shfl_xor_sync(0xffffffffu, d, 2);
@@ -160,15 +174,140 @@ __global__ void __launch_bounds__(kGemvThreads)
               const int za = __half2int_rn(__low2half(zsA[r][j]));
               const int G = d - za * zs[n * NG + g];
               acc[r][n] += static_cast<float>(G) * (zsa.y * sb[n * NG + g]);
-              if (Gdbg != nullptr)
-                Gdbg[m * ldg_row + n * ldg_col + g] = G;
+              if (Gdbg != nullptr) Gdbg[m * ldg_row + n * ldg_col + g] = G;
             }
           }
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < kGemvRowsPerWarp; ++r) {
+    for (int r = 0; r < R; ++r) {
+      const int m = row0 + r;
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        const float s = warp_sum_f32(acc[r][n]);
+        if (lane == 0 && m < rows) C[m * ldc_row + n * ldc_col] = __float2half_rn(s);
+      }
+    }
+  }
+}
+
+// INT4, register-resident B (NC * P <= 8). Lane l of a warp always owns the
+// 16-byte chunks l, l+32, ..., l+32(P-1) of a row, so the (b - zB) codes, the
+// chunk sums of (b - zB) and the B scales for those chunks are built once per warp
+// in registers and reused for every row the warp streams: no shared memory, no
+// block barrier, no per-CTA preamble. Each lane forms its exact partial
+// d - zA * sum(b - zB) for its 32 codes; the 4 lanes of a group add them into the
+// group's exact G. R rows are streamed concurrently per warp.
+template <int NC, int P, int R>
+__global__ void __launch_bounds__(kGemvThreads)
+    gemv_int4_reg_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
+                         const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
+                         const __half* __restrict__ Bs, const __half* __restrict__ Bz,
+                         __half* __restrict__ C, int32_t* __restrict__ Gdbg, int rows, int K,
+                         long long ldc_row, long long ldc_col, long long ldg_row,
+                         long long ldg_col) {
+  dev::allow_dependent_launch();
+  const int NG = K >> 7;
+  const int NCH = K >> 5;
+  const int KB = K >> 1;
+  const int lane = static_cast<int>(dev::lane_idx());
+  const int gwarp = static_cast<int>(blockIdx.x * (blockDim.x >> 5) + dev::warp_idx());
+  const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
+
+  dev::grid_dependency_wait();
+
+  uint4 a[R][P];
+  __half2 zsa[R][P];
+  auto load_rows = [&](int row0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m = row0 + r;
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const int ch = p * 32 + lane;
+        if (m < rows && ch < NCH) {
+          a[r][p] = dev::ld_nc_v4(Aq + static_cast<size_t>(m) * KB + static_cast<size_t>(ch) * 16);
+          const size_t gi = static_cast<size_t>(m) * NG + (ch >> 2);
+          zsa[r][p] = __halves2half2(Az[gi], As[gi]);
+        } else {
+          a[r][p] = make_uint4(0u, 0u, 0u, 0u);
+          zsa[r][p] = __halves2half2(__float2half(0.f), __float2half(0.f));
+        }
+      }
+    }
+  };
+  int row0 = gwarp * R;
+  if (row0 < rows) load_rows(row0);
+
+  // (b - zB) codes of this lane's chunks: word 2u = even-k codes (high nibbles) of
+  // byte quad u, 2u+1 = odd-k codes; chunk sums of (b - zB); B group scales.
+  uint32_t bw[NC][P][8];
+  int bsum[NC][P];
+  float bsc[NC][P];
+#pragma unroll
+  for (int n = 0; n < NC; ++n)
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int ch = p * 32 + lane;
+      uint4 q = make_uint4(0u, 0u, 0u, 0u);
+      int zb = 0;
+      bsc[n][p] = 0.f;
+      if (ch < NCH) {
+        q = *reinterpret_cast<const uint4*>(Bq + static_cast<size_t>(n) * KB + static_cast<size_t>(ch) * 16);
+        zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (ch >> 2)]);
+        bsc[n][p] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
+      }
+      const uint32_t zq = static_cast<uint32_t>(zb & 0xff) * 0x01010101u;
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      int sum = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        bw[n][p][2 * u] = __vsub4((w[u] >> 4) & 0x0f0f0f0fu, zq);
+        bw[n][p][2 * u + 1] = __vsub4(w[u] & 0x0f0f0f0fu, zq);
+        sum = __dp4a(static_cast<int>(bw[n][p][2 * u]), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(bw[n][p][2 * u + 1]), 0x01010101, sum);
+      }
+      bsum[n][p] = ch < NCH ? sum : 0;
+    }
+
+  for (; row0 < rows; row0 += nwarps * R) {
+    float acc[R][NC];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int n = 0; n < NC; ++n) acc[r][n] = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int m = row0 + r;
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const int ch = p * 32 + lane;
+        const uint32_t w[4] = {a[r][p].x, a[r][p].y, a[r][p].z, a[r][p].w};
+        const int za = __half2int_rn(__low2half(zsa[r][p]));
+        const float sa = __high2float(zsa[r][p]);
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+          int d0 = 0, d1 = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            d0 = __dp4a(static_cast<int>((w[u] >> 4) & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u]), d0);
+            d1 = __dp4a(static_cast<int>(w[u] & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u + 1]), d1);
+          }
+          int g = d0 + d1 - za * bsum[n][p];
+          g += __shfl_xor_sync(0xffffffffu, g, 1);
+          g += __shfl_xor_sync(0xffffffffu, g, 2);
+          if ((lane & 3) == 0 && ch < NCH && m < rows) {
+            acc[r][n] += static_cast<float>(g) * (sa * bsc[n][p]);
+            if (Gdbg != nullptr) Gdbg[m * ldg_row + n * ldg_col + (ch >> 2)] = g;
+          }
+        }
+      }
+    }
+    const int next = row0 + nwarps * R;
+    if (next < rows) load_rows(next);  // next rows in flight during the reductions
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
       const int m = row0 + r;
 #pragma unroll
       for (int n = 0; n < NC; ++n) {

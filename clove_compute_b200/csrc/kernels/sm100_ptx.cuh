@@ -300,6 +300,21 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr) {
 }
 
 // ----------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialisation attribute may start before its predecessor on the stream
+// finishes; grid_dependency_wait() blocks until the predecessor has completed and
+// its memory is visible, so every global access placed after it is ordered as
+// with a plain launch. allow_dependent_launch() lets the next such kernel start.
+// Both are no-ops for kernels launched without the attribute.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------
 // Misc
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {

@@ -1,0 +1,78 @@
+"""N-split across two GPUs (one process per GPU, NCCL): every rank's shard GEMM and
+the replicated C gathered by clove_nsplit_gemm_* match the single-GPU oracle.
+Skipped on machines with fewer than two GPUs."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import clove_compute_b200 as cc
+        import oracle
+        from clove_compute_b200 import workloads as wl
+        ns = cc.NSplit(rank, world)
+        out = []
+        for (M, N, K) in [(512, 2048, 1024), (256, 1000, 512)]:
+            A, B = wl.fp16_operands(M, N, K, seed=1)
+            c0, c1 = ns.cols(N)
+            Ad = torch.from_numpy(A).cuda()
+            Bs = torch.from_numpy(np.ascontiguousarray(B[:, c0:c1])).cuda()
+            C = ns.gemm_fp16(Ad, Bs, N, replicate_C=True)
+            torch.cuda.synchronize()
+            ref = oracle.gemm_fp16(A, B)
+            d = C.cpu().numpy().astype(np.float64) - ref
+            out.append(float(np.linalg.norm(d) / np.linalg.norm(ref)))
+        # int4 with B rows sharded
+        M, N, K = 256, 512, 1024
+        op = wl.int4_operands(M, N, K, seed=2)
+        c0, c1 = ns.cols(N)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        C = ns.gemm_int4(t(op.A_q), t(op.A_scale), t(op.A_zero), t(op.B_q[c0:c1]),
+                         t(op.B_scale[c0:c1]), t(op.B_zero[c0:c1]), N, replicate_C=True)
+        torch.cuda.synchronize()
+        ref = oracle.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K)
+        d = C.cpu().numpy().astype(np.float64) - ref
+        out.append(float(np.linalg.norm(d) / np.linalg.norm(ref)))
+        ns.close()
+        q.put((rank, "ok", out))
+    except Exception as e:
+        q.put((rank, "error", repr(e)[:300]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nsplit_two_gpus(clove_lib, cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (k, v)) for r, k, v in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert res[r][0] == "ok", res[r]
+        assert all(e < 2e-3 for e in res[r][1]), res[r]
