@@ -299,6 +299,18 @@ def _secondary(cc, torch, peaks):
             "kernel": cc.describe_dispatch("fp16", n, n, n), "us_per_call": round(t * 1e6, 2),
             "TFLOPS": round(tf, 1), "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)}
         del Ad, Bd
+    # config 5: int4 8192^3 (both operands int4, per-group scales / zero points)
+    for n in (4096, 8192):
+        op = wl.int4_operands(n, n, n, seed=0)
+        t4 = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
+        C = torch.empty((n, n), dtype=torch.float16, device="cuda")
+        reps = max(5, min(100, int(4e13 // (2 * n ** 3))))
+        t = timeit(lambda i: cc.gemm_int4(*t4, C), 1, reps)
+        out[f"int4_square_{n}"] = {
+            "kernel": cc.describe_dispatch("int4", n, n, n), "us_per_call": round(t * 1e6, 2),
+            "TOPS": round(2 * n ** 3 / t / 1e12, 1),
+            "frac_of_2x_bf16_peak": round(2 * n ** 3 / t / 1e12 / (2 * peaks["bf16_tflops"]), 4)}
+        del t4
     for n in (4096, 8192):
         A8, B8, sA, sB = wl.int8_operands(n, n, n, seed=0)
         Ad, Bd, sAd, sBd = dev(A8), dev(B8), dev(sA), dev(sB)

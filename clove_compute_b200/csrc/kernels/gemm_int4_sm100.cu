@@ -1,22 +1,56 @@
-// gemm_int4_sm100.cu -- INT4 tensor-core GEMM (kind::i8 with in-smem nibble unpack).
-// Placeholder TU: the tensor-core path is not yet enabled, so every large INT4
-// shape reports ineligible and the dispatcher uses the GEMV or SIMT kernels.
-#include "sm100_ptx.cuh"
+// gemm_int4_sm100.cu -- host launcher of the INT4 tcgen05 kernel (gemm_int4_sm100.cuh).
+#include <atomic>
+
+#include "gemm_int4_sm100.cuh"
 #include "../runtime/internal.h"
+#include "../runtime/tensor_map.h"
 
 namespace clove {
 namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_int4)
 
-bool gemm_int4_tc_eligible(const uint8_t*, const void*, const void*, const uint8_t*, const void*,
-                           const void*, const void*, int, int, int) {
-  return false;
+namespace {
+std::atomic<uint64_t> g_attr_set{0};
+inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+// TMA needs 16-byte row strides: K/2 bytes of codes (K % 32) and K/128 fp16 of
+// scales / zero points (K % 1024); C rows of N fp16 (N % 8); aligned bases.
+bool gemm_int4_tc_eligible(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                           const void* Bs, const void* Bz, const void* C, int M, int N, int K) {
+  return M > 0 && N > 0 && K > 0 && K % 1024 == 0 && N % 8 == 0 && a16(Aq) && a16(Bq) &&
+         a16(As) && a16(Az) && a16(Bs) && a16(Bz) && a16(C);
 }
 
-int launch_gemm_int4_tc(const uint8_t*, const void*, const void*, const uint8_t*, const void*,
-                        const void*, void*, int, int, int, const DeviceInfo&, cudaStream_t) {
-  return fail(CLOVE_ERR_UNSUPPORTED, "int4 tensor-core kernel not built");
+int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                        const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int M, int N,
+                        int K, const DeviceInfo& dev, cudaStream_t stream) {
+  using S = kern::I4Shape;
+  const int NG = K / 128;
+  CUtensorMap tAq, tBq, tAs, tAz, tBs, tBz, tC;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int rc;
+  if ((rc = encode_tmap_2d(&tAq, U8, 1, Aq, K / 2, M, K / 2, 64, 128, 64))) return rc;
+  if ((rc = encode_tmap_2d(&tBq, U8, 1, Bq, K / 2, N, K / 2, 64, 128, 64))) return rc;
+  if ((rc = encode_tmap_2d(&tAs, F16, 2, As, NG, M, NG * 2ull, 8, 128, 0))) return rc;
+  if ((rc = encode_tmap_2d(&tAz, F16, 2, Az, NG, M, NG * 2ull, 8, 128, 0))) return rc;
+  if ((rc = encode_tmap_2d(&tBs, F16, 2, Bs, NG, N, NG * 2ull, 8, 128, 0))) return rc;
+  if ((rc = encode_tmap_2d(&tBz, F16, 2, Bz, NG, N, NG * 2ull, 8, 128, 0))) return rc;
+  if ((rc = encode_tmap_2d(&tC, F16, 2, C, N, M, N * 2ull, 64, 32, 128))) return rc;
+  const uint64_t bit = 1ull << (dev.device & 63);
+  if ((g_attr_set.load(std::memory_order_acquire) & bit) == 0) {
+    rc = check_cuda(cudaFuncSetAttribute(kern::gemm_int4_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES),
+                    "cudaFuncSetAttribute(int4 smem)");
+    if (rc) return rc;
+    g_attr_set.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const dim3 grid((N + S::BN - 1) / S::BN, (M + S::BM - 1) / S::BM, 1);
+  kern::gemm_int4_tc_kernel<<<grid, S::THREADS, S::SMEM_BYTES, stream>>>(tAq, tBq, tAs, tAz, tBs,
+                                                                         tBz, tC, M, N, K, Gdbg);
+  return check_cuda(cudaGetLastError(), "gemm_int4_tc launch");
 }
 
 }  // namespace rt

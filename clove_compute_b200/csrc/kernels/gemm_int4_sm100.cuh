@@ -1,0 +1,348 @@
+// gemm_int4_sm100.cuh -- INT4 group-wise GEMM on tcgen05 kind::i8 (sm_100a).
+//
+// Replaces the reference's SIMT kernel (src/kernels/gemm_int4.cu:45-193) with the
+// semantics its header documents (gemm.cuh:67-87): both operands K-packed,
+// A_q [M,K/2], B_q [N,K/2] (element 2j in the high nibble of byte j), per-128-group
+// fp16 scales and integer zero points [rows,K/128]; C[m,n] = sum_g sA sB G with
+//   G[m,n,g] = sum_{k in g} (a - zA)(b - zB)   exact in int32.
+//
+// One CTA computes a 128 x 128 tile of C; K advances one group (128 codes,
+// 64 packed bytes) at a time. 14 warps:
+//   warp 0      TMA producer: packed A / B boxes [128 rows x 64 B] (64B swizzle)
+//               into a 4-deep ring; every 8 groups, boxes [128 rows x 8 groups] of
+//               A/B scales and zero points into a 2-slot ring.
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
+//               group into one of two int32 TMEM buffers (a fresh accumulator per
+//               group), so every G leaves the tensor core exact.
+//   warps 2-5   transform: thread t unpacks row t of the A and of the B tile,
+//               subtracting the row's zero point, into a 128B-swizzled int8 stage
+//               (the MMA operand). Within a group both operands use the same K
+//               order (the high nibbles of a 4-byte word, then its low nibbles),
+//               which leaves the dot product unchanged. They also publish the
+//               group's B scales as fp32 for the epilogue.
+//   warps 6-13  epilogue: two warps per TMEM lane quarter, 64 columns each;
+//               acc += float(G) * (sA * sB) in fp32 registers while the tensor core
+//               computes the next group; finally fp16 through swizzled smem and a
+//               TMA store.
+// Zero points must be integer codes in [0, 15] (so a - zA fits int8).
+#pragma once
+
+#include "sm100_ptx.cuh"
+
+namespace clove {
+namespace kern {
+
+struct I4Shape {
+  static constexpr int BM = 128;
+  static constexpr int BN = 128;
+  static constexpr int GB = 64;                       // packed bytes per group per row
+  static constexpr int PK_STAGES = 4;
+  static constexpr int UN_STAGES = 3;
+  static constexpr int PK_A = BM * GB;                // 8 KB
+  static constexpr int PK_BYTES = (BM + BN) * GB;     // 16 KB
+  static constexpr int UN_A = BM * 128;               // 16 KB
+  static constexpr int UN_BYTES = (BM + BN) * 128;    // 32 KB
+  static constexpr int META_BOX = 128 * 16;           // 128 rows x 8 groups x fp16
+  static constexpr int META_BYTES = 4 * META_BOX;     // A scale, A zero, B scale, B zero
+  static constexpr int META_SLOTS = 2;
+  static constexpr int SBF_BYTES = 2 * BN * 4;        // fp32 B scales, 2 slots
+  static constexpr int EPI_BYTES = 8 * 4096;          // 8 warps x 32 rows x 128 B
+  static constexpr int THREADS = 14 * 32;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int OFF_UN = 0;                                      // 1024-aligned
+  static constexpr int OFF_PK = OFF_UN + UN_STAGES * UN_BYTES;
+  static constexpr int OFF_META = OFF_PK + PK_STAGES * PK_BYTES;
+  static constexpr int OFF_EPI = OFF_META + META_SLOTS * META_BYTES;
+  static constexpr int OFF_SBF = OFF_EPI + EPI_BYTES;
+  static constexpr int OFF_BAR = OFF_SBF + SBF_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
+  static_assert(SMEM_BYTES <= 232448, "smem budget");
+  static_assert(OFF_PK % 1024 == 0 && OFF_META % 1024 == 0 && OFF_EPI % 1024 == 0, "align");
+};
+
+// kind::i8, s32 accumulator, s8 x s8, both operands K-major, M = N = 128.
+constexpr uint32_t kI4Idesc = dev::make_idesc(2, 1, 1, 0, 0, I4Shape::BN, I4Shape::BM);
+
+__global__ void __launch_bounds__(I4Shape::THREADS, 1)
+    gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap tmAq,
+                        const __grid_constant__ CUtensorMap tmBq,
+                        const __grid_constant__ CUtensorMap tmAs,
+                        const __grid_constant__ CUtensorMap tmAz,
+                        const __grid_constant__ CUtensorMap tmBs,
+                        const __grid_constant__ CUtensorMap tmBz,
+                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+                        int32_t* __restrict__ Gdbg) {
+  using S = I4Shape;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* pk_full = bars;                        // [4]
+  uint64_t* pk_empty = bars + 4;                   // [4]
+  uint64_t* un_full = bars + 8;                    // [3]
+  uint64_t* un_empty = bars + 11;                  // [3]
+  uint64_t* acc_full = bars + 14;                  // [2]
+  uint64_t* acc_empty = bars + 16;                 // [2]
+  uint64_t* meta_full = bars + 18;                 // [2]
+  uint64_t* meta_empty = bars + 20;                // [2]
+  uint64_t* sb_full = bars + 22;                   // [2]
+  uint64_t* sb_empty = bars + 24;                  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sbf = reinterpret_cast<float*>(smem + S::OFF_SBF);
+
+  const uint32_t warp = dev::warp_idx();
+  const uint32_t lane = dev::lane_idx();
+  const int NG = K >> 7;
+  const int m0 = static_cast<int>(blockIdx.y) * S::BM;
+  const int n0 = static_cast<int>(blockIdx.x) * S::BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::PK_STAGES; ++i) {
+      dev::mbar_init(&pk_full[i], 1);
+      dev::mbar_init(&pk_empty[i], 4);
+    }
+    for (int i = 0; i < S::UN_STAGES; ++i) {
+      dev::mbar_init(&un_full[i], 4);
+      dev::mbar_init(&un_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      dev::mbar_init(&acc_full[i], 1);
+      dev::mbar_init(&acc_empty[i], 8);
+      dev::mbar_init(&meta_full[i], 1);
+      dev::mbar_init(&meta_empty[i], 12);
+      dev::mbar_init(&sb_full[i], 4);
+      dev::mbar_init(&sb_empty[i], 8);
+    }
+    *abort_flag = 0;
+    dev::fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&tmAq);
+    dev::prefetch_tmap(&tmBq);
+    dev::prefetch_tmap(&tmAs);
+    dev::prefetch_tmap(&tmAz);
+    dev::prefetch_tmap(&tmBs);
+    dev::prefetch_tmap(&tmBz);
+    dev::prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(tmem_slot, S::TMEM_COLS);
+    dev::tmem_relinquish_alloc_permit();
+  }
+  dev::tc_fence_before_sync();
+  __syncthreads();
+  dev::tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t armed = 0, armed_par = 0;  // packed stages with a load in flight
+      uint32_t meta_armed = 0, meta_par = 0;
+      for (int g = 0; g < NG; ++g) {
+        if ((g & 7) == 0) {
+          const int c = g >> 3;
+          const int slot = c & 1;
+          if (!dev::mbar_wait(&meta_empty[slot], ((c >> 1) & 1) ^ 1u, abort_flag)) break;
+          uint8_t* mt = smem + S::OFF_META + slot * S::META_BYTES;
+          dev::mbar_arrive_expect_tx(&meta_full[slot], S::META_BYTES);
+          dev::tma_load_2d(mt + 0 * S::META_BOX, &tmAs, &meta_full[slot], g, m0);
+          dev::tma_load_2d(mt + 1 * S::META_BOX, &tmAz, &meta_full[slot], g, m0);
+          dev::tma_load_2d(mt + 2 * S::META_BOX, &tmBs, &meta_full[slot], g, n0);
+          dev::tma_load_2d(mt + 3 * S::META_BOX, &tmBz, &meta_full[slot], g, n0);
+          meta_armed |= 1u << slot;
+          meta_par = (meta_par & ~(1u << slot)) | (static_cast<uint32_t>((c >> 1) & 1) << slot);
+        }
+        const int s = g % S::PK_STAGES;
+        const uint32_t use = static_cast<uint32_t>(g / S::PK_STAGES);
+        if (!dev::mbar_wait(&pk_empty[s], (use & 1u) ^ 1u, abort_flag)) break;
+        uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
+        dev::mbar_arrive_expect_tx(&pk_full[s], S::PK_BYTES);
+        dev::tma_load_2d(pk, &tmAq, &pk_full[s], g * S::GB, m0);
+        dev::tma_load_2d(pk + S::PK_A, &tmBq, &pk_full[s], g * S::GB, n0);
+        armed |= 1u << s;
+        armed_par = (armed_par & ~(1u << s)) | ((use & 1u) << s);
+      }
+      if (*abort_flag) {
+        volatile int no_abort = 0;
+        for (int s = 0; s < S::PK_STAGES; ++s)
+          if (armed & (1u << s)) dev::mbar_wait(&pk_full[s], (armed_par >> s) & 1u, &no_abort);
+        for (int s = 0; s < 2; ++s)
+          if (meta_armed & (1u << s)) dev::mbar_wait(&meta_full[s], (meta_par >> s) & 1u, &no_abort);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int g = 0; g < NG; ++g) {
+        const int u = g % S::UN_STAGES;
+        const int b = g & 1;
+        if (!dev::mbar_wait(&un_full[u], static_cast<uint32_t>(g / S::UN_STAGES) & 1u, abort_flag))
+          break;
+        if (!dev::mbar_wait(&acc_empty[b], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, abort_flag))
+          break;
+        dev::tc_fence_after_sync();
+        const uint32_t a_addr = dev::smem_u32(smem + S::OFF_UN + u * S::UN_BYTES);
+        const uint32_t b_addr = a_addr + S::UN_A;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(b) * S::BN;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = dev::make_smem_desc(a_addr + k * 32, 0, 1024, dev::kLayoutSw128);
+          const uint64_t bd = dev::make_smem_desc(b_addr + k * 32, 0, 1024, dev::kLayoutSw128);
+          dev::mma_i8_ss(d, ad, bd, kI4Idesc, k > 0 ? 1u : 0u);
+        }
+        dev::mma_commit(&un_empty[u]);
+        dev::mma_commit(&acc_full[b]);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ transform
+    const int t = static_cast<int>((warp - 2) * 32 + lane);  // row of the A and B tiles
+    for (int g = 0; g < NG; ++g) {
+      const int c = g >> 3;
+      const int mslot = c & 1;
+      const int s = g % S::PK_STAGES;
+      const int u = g % S::UN_STAGES;
+      const int sbs = g & 1;
+      bool ok = true;
+      if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&pk_full[s], static_cast<uint32_t>(g / S::PK_STAGES) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&un_empty[u], (static_cast<uint32_t>(g / S::UN_STAGES) & 1u) ^ 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+
+      const uint8_t* mt = smem + S::OFF_META + mslot * S::META_BYTES;
+      const __half* meta_az = reinterpret_cast<const __half*>(mt + 1 * S::META_BOX);
+      const __half* meta_bs = reinterpret_cast<const __half*>(mt + 2 * S::META_BOX);
+      const __half* meta_bz = reinterpret_cast<const __half*>(mt + 3 * S::META_BOX);
+      const int gi = g & 7;
+      const uint32_t za4 = static_cast<uint32_t>(__half2int_rn(meta_az[t * 8 + gi]) & 0xff) * 0x01010101u;
+      const uint32_t zb4 = static_cast<uint32_t>(__half2int_rn(meta_bz[t * 8 + gi]) & 0xff) * 0x01010101u;
+      sbf[sbs * S::BN + t] = __half2float(meta_bs[t * 8 + gi]);
+
+      const uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
+      uint8_t* un = smem + S::OFF_UN + u * S::UN_BYTES;
+#pragma unroll
+      for (int op = 0; op < 2; ++op) {
+        const uint8_t* src = pk + op * S::PK_A + t * 64;       // 64B-swizzled packed row
+        const uint32_t dst = dev::smem_u32(un + op * S::UN_A + t * 128);  // 128B-swizzled row
+        const uint32_t z4 = op == 0 ? za4 : zb4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 q = *reinterpret_cast<const uint4*>(src + ((j ^ ((t >> 1) & 3)) << 4));
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            o[2 * x] = __vsub4((w[x] >> 4) & 0x0f0f0f0fu, z4);
+            o[2 * x + 1] = __vsub4(w[x] & 0x0f0f0f0fu, z4);
+          }
+          const int c0 = 2 * j, c1 = 2 * j + 1;
+          dev::st_shared_v4(dst + ((c0 ^ (t & 7)) << 4), o[0], o[1], o[2], o[3]);
+          dev::st_shared_v4(dst + ((c1 ^ (t & 7)) << 4), o[4], o[5], o[6], o[7]);
+        }
+      }
+      dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+      __syncwarp();
+      if (lane == 0) {
+        dev::mbar_arrive(&un_full[u]);
+        dev::mbar_arrive(&sb_full[sbs]);
+        dev::mbar_arrive(&pk_empty[s]);
+        if (gi == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t q = warp & 3u;
+    const int h = static_cast<int>(warp - 6) >> 2;  // column half of the tile
+    const int row = static_cast<int>(q * 32 + lane);
+    float acc[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < NG && ok; ++g) {
+      const int c = g >> 3;
+      const int mslot = c & 1;
+      const int b = g & 1;
+      const int sbs = g & 1;
+      if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g >> 1) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g >> 1) & 1u, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      dev::tc_fence_after_sync();
+      const __half* meta_as = reinterpret_cast<const __half*>(smem + S::OFF_META + mslot * S::META_BYTES);
+      const float sa = __half2float(meta_as[row * 8 + (g & 7)]);
+      const float* sb = sbf + sbs * S::BN + h * 64;
+      const uint32_t taddr = tmem_base + ((q * 32u) << 16) + static_cast<uint32_t>(b) * S::BN + h * 64;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v0[16], v1[16];
+        dev::tmem_ld_x16(taddr + half * 32, v0);
+        dev::tmem_ld_x16(taddr + half * 32 + 16, v1);
+        dev::tmem_ld_wait();
+        if (half == 1) {
+          dev::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) dev::mbar_arrive(&acc_empty[b]);
+        }
+        if (Gdbg != nullptr && m0 + row < M) {  // test hook: exact group accumulators
+          const int nb = n0 + h * 64 + half * 32;
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < N)
+              Gdbg[(static_cast<size_t>(m0 + row) * N + nb + j) * NG + g] =
+                  static_cast<int32_t>(j < 16 ? v0[j] : v1[j - 16]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 s4 = *reinterpret_cast<const float4*>(sb + half * 32 + j);
+          const uint32_t* vv = j < 16 ? &v0[j] : &v1[j - 16];
+          acc[half * 32 + j + 0] += static_cast<float>(static_cast<int32_t>(vv[0])) * (sa * s4.x);
+          acc[half * 32 + j + 1] += static_cast<float>(static_cast<int32_t>(vv[1])) * (sa * s4.y);
+          acc[half * 32 + j + 2] += static_cast<float>(static_cast<int32_t>(vv[2])) * (sa * s4.z);
+          acc[half * 32 + j + 3] += static_cast<float>(static_cast<int32_t>(vv[3])) * (sa * s4.w);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        dev::mbar_arrive(&sb_empty[sbs]);
+        if ((g & 7) == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
+      }
+    }
+    if (ok) {
+      // fp16 into a 128B-swizzled staging tile, one TMA store per warp.
+      uint8_t* stg = smem + S::OFF_EPI + (warp - 6) * 4096;
+      const uint32_t sa_ = dev::smem_u32(stg);
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const uint32_t o0 = dev::pack_half2(acc[p * 8 + 0], acc[p * 8 + 1]);
+        const uint32_t o1 = dev::pack_half2(acc[p * 8 + 2], acc[p * 8 + 3]);
+        const uint32_t o2 = dev::pack_half2(acc[p * 8 + 4], acc[p * 8 + 5]);
+        const uint32_t o3 = dev::pack_half2(acc[p * 8 + 6], acc[p * 8 + 7]);
+        dev::st_shared_v4(sa_ + lane * 128 + ((p ^ (lane & 7)) << 4), o0, o1, o2, o3);
+      }
+      dev::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        dev::tma_store_2d(&tmC, stg, n0 + h * 64, m0 + static_cast<int>(q) * 32);
+        dev::bulk_commit_group();
+        dev::bulk_wait_group<0>();
+      }
+      __syncwarp();
+    }
+  }
+
+  dev::tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after_sync();
+    dev::tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace kern
+}  // namespace clove

@@ -368,9 +368,9 @@ static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, con
     return launch_gemv_int4(Bq, Bs, Bz, Aq, As, Az, C, G, N, M, K, 1, N, NG,
                             static_cast<long long>(N) * NG, dev, s);
   }
-  if (path == 1 && G == nullptr) {
+  if (path == 1) {
     if (chosen) *chosen = "tc_int4";
-    return launch_gemm_int4_tc(Aq, As, Az, Bq, Bs, Bz, C, M, N, K, dev, s);
+    return launch_gemm_int4_tc(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, dev, s);
   }
   if (chosen) *chosen = "simt_int4";
   return launch_simt_i4(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, s);
@@ -426,7 +426,10 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
     }
   } else {
     const bool gemv = (N <= 8 || M <= 8) && K % 128 == 0;
-    name = gemv ? (N <= 8 && (N <= M || M > 8) ? "gemv_int4" : "gemv_int4_t") : "tc_int4";
+    const bool tc = K % 1024 == 0 && N % 8 == 0;
+    int path = ov.path ? ov.path : (gemv ? 2 : (tc ? 1 : 3));
+    name = path == 2 ? (N <= 8 && (N <= M || M > 8) ? "gemv_int4" : "gemv_int4_t")
+                     : path == 1 ? "tc_int4" : "simt_int4";
   }
   snprintf(buf, buflen, "%s bn=%d split=%d", name, bn, split);
   return CLOVE_OK;

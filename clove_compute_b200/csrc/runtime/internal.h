@@ -84,9 +84,10 @@ int launch_scale_f16(void* C, long long n, float beta, cudaStream_t stream);
 int read_clear_error_simt();
 
 // ---- INT4 tensor-core kernel (kernels/gemm_int4_sm100.cu)
+// Gdbg (may be NULL): exact group accumulators G [M,N,K/128] for tests.
 int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
-                        const void* Bs, const void* Bz, void* C, int M, int N, int K,
-                        const DeviceInfo& dev, cudaStream_t stream);
+                        const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int M, int N,
+                        int K, const DeviceInfo& dev, cudaStream_t stream);
 bool gemm_int4_tc_eligible(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                            const void* Bs, const void* Bz, const void* C, int M, int N, int K);
 int read_clear_error_int4();

@@ -62,6 +62,31 @@ def test_large_shape(clove_lib, oracle_mod, cuda):
     _check(clove_lib, oracle_mod, 256, 192, 1024, seed=5)
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 128, 1024), (256, 384, 2048), (300, 136, 3072),
+                                   (1000, 200, 1024)])
+def test_tc_int4_exact_groups(clove_lib, oracle_mod, cuda, M, N, K):
+    """tcgen05 kind::i8 path: every group accumulator bit-exact, C within tolerance."""
+    assert clove_lib.describe_dispatch("int4", M, N, K).startswith("tc_int4")
+    _check(clove_lib, oracle_mod, M, N, K, seed=M + N)
+
+
+def test_tc_int4_config5_rows(clove_lib, oracle_mod, cuda):
+    """BASELINE config 5 shape (8192^3) on the tensor-core path, checked on a row sample
+    against the oracle (the full oracle product takes minutes on the host)."""
+    M = N = K = 8192
+    op = wl.int4_operands(M, N, K, seed=0)
+    C = host(clove_lib.gemm_int4(*_ops_dev(op)))
+    rows = (0, 64)
+    ref = oracle_mod.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K,
+                               rows=rows)
+    assert rel_fro(C[rows[0]:rows[1]], ref[rows[0]:rows[1]]) < TOL_TIGHT
+    last = (M - 64, M)
+    ref = oracle_mod.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K,
+                               rows=last)
+    assert rel_fro(C[last[0]:], ref[last[0]:]) < TOL_TIGHT
+    assert np.isfinite(C.astype(np.float32)).all()
+
+
 def test_simt_path(clove_lib, oracle_mod, cuda):
     _check(clove_lib, oracle_mod, 40, 24, 512, path=3, seed=6)
 
