@@ -340,6 +340,10 @@ def run_case(args):
         A, B, sA, sB = wl.int8_operands(4096, 32, 4096, seed=0)
         t = [dev(A), dev(B), dev(sA), dev(sB)]
         fn = lambda: cc.gemm_int8_rowcol(*t)
+    elif args.case == "int4_4096":
+        op = wl.int4_operands(4096, 4096, 4096, seed=0)
+        t = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
+        fn = lambda: cc.gemm_int4(*t)
     elif args.case == "fp16_1024":
         A, B = wl.fp16_operands(1024, 1024, 1024, seed=0)
         t = [dev(A), dev(B)]
@@ -504,7 +508,7 @@ def main():
     ap.add_argument("--impl", choices=["clove", "reference"], default="clove")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024"],
+    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096"],
                     help="profiling mode: warm-up + steps plain launches of one secondary config")
     ap.add_argument("--kernel-only", action="store_true",
                     help="run only the warm-up and timed FFN GEMMs (for ncu), print nothing")

@@ -11,7 +11,7 @@ namespace rt {
 CLOVE_DEFINE_ERROR_READER(read_clear_error_int4)
 
 namespace {
-std::atomic<uint64_t> g_attr_set{0};
+std::atomic<uint64_t> g_attr_set[2];
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
@@ -39,17 +39,19 @@ int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const
   if ((rc = encode_tmap_2d(&tBs, F16, 2, Bs, NG, N, NG * 2ull, 8, 128, 0))) return rc;
   if ((rc = encode_tmap_2d(&tBz, F16, 2, Bz, NG, N, NG * 2ull, 8, 128, 0))) return rc;
   if ((rc = encode_tmap_2d(&tC, F16, 2, C, N, M, N * 2ull, 64, 32, 128))) return rc;
+  const bool dbg = Gdbg != nullptr;
+  auto kernel = dbg ? kern::gemm_int4_tc_kernel<true> : kern::gemm_int4_tc_kernel<false>;
   const uint64_t bit = 1ull << (dev.device & 63);
-  if ((g_attr_set.load(std::memory_order_acquire) & bit) == 0) {
-    rc = check_cuda(cudaFuncSetAttribute(kern::gemm_int4_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES),
+  if ((g_attr_set[dbg].load(std::memory_order_acquire) & bit) == 0) {
+    rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         S::SMEM_BYTES),
                     "cudaFuncSetAttribute(int4 smem)");
     if (rc) return rc;
-    g_attr_set.fetch_or(bit, std::memory_order_acq_rel);
+    g_attr_set[dbg].fetch_or(bit, std::memory_order_acq_rel);
   }
   const dim3 grid((N + S::BN - 1) / S::BN, (M + S::BM - 1) / S::BM, 1);
-  kern::gemm_int4_tc_kernel<<<grid, S::THREADS, S::SMEM_BYTES, stream>>>(tAq, tBq, tAs, tAz, tBs,
-                                                                         tBz, tC, M, N, K, Gdbg);
+  kernel<<<grid, S::THREADS, S::SMEM_BYTES, stream>>>(tAq, tBq, tAs, tAz, tBs, tBz, tC, M, N, K,
+                                                      Gdbg);
   return check_cuda(cudaGetLastError(), "gemm_int4_tc launch");
 }
 

@@ -14,17 +14,23 @@
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
 //               group into one of two int32 TMEM buffers (a fresh accumulator per
 //               group), so every G leaves the tensor core exact.
-//   warps 2-5   transform: thread t unpacks row t of the A and of the B tile,
-//               subtracting the row's zero point, into a 128B-swizzled int8 stage
-//               (the MMA operand). Within a group both operands use the same K
-//               order (the high nibbles of a 4-byte word, then its low nibbles),
-//               which leaves the dot product unchanged. They also publish the
-//               group's B scales as fp32 for the epilogue.
-//   warps 6-13  epilogue: two warps per TMEM lane quarter, 64 columns each;
-//               acc += float(G) * (sA * sB) in fp32 registers while the tensor core
-//               computes the next group; finally fp16 through swizzled smem and a
-//               TMA store.
-// Zero points must be integer codes in [0, 15] (so a - zA fits int8).
+//   warps 2-5   transform: thread t unpacks row t of the A and of the B tile into
+//               a 128B-swizzled u8 stage (the MMA operand) holding the biased codes
+//               a'' = a - zA + 16 and b'' = b - zB + 16, both in [1, 31], formed with
+//               plain adds (no per-byte carries). Within a group both operands use
+//               the same K order (the high nibbles of a 4-byte word, then its low
+//               nibbles), which leaves the dot product unchanged. Per row they also
+//               sum the codes: with R = sum(a - zA), Cc = sum(b - zB),
+//                 G = D - 16 R - 16 Cc - 32768,   D = sum a'' b''  (u8 x u8 MMA).
+//               They publish, per group, the B scales (fp32), 16 Cc per column and
+//               0x4B400000 - 16 R - 32768 per row.
+//   warps 6-13  epilogue: two warps per TMEM lane quarter, 64 columns each. One
+//               3-input integer add turns D into the fp32 bit pattern of
+//               12582912 + G (exact: |G| < 2^22), one subtraction gives float(G);
+//               acc += float(G) * (sA * sB) with packed fp32x2 math, in registers,
+//               while the tensor core computes the next group; finally fp16 through
+//               swizzled smem and a TMA store.
+// Zero points must be integer codes in [0, 15].
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -37,7 +43,9 @@ struct I4Shape {
   static constexpr int BN = 128;
   static constexpr int GB = 64;                       // packed bytes per group per row
   static constexpr int PK_STAGES = 4;
-  static constexpr int UN_STAGES = 3;
+  static constexpr int UN_STAGES = 4;
+  static constexpr int ACC_BUFS = 4;                  // int32 TMEM accumulators
+  static constexpr int SB_SLOTS = 4;
   static constexpr int PK_A = BM * GB;                // 8 KB
   static constexpr int PK_BYTES = (BM + BN) * GB;     // 16 KB
   static constexpr int UN_A = BM * 128;               // 16 KB
@@ -45,25 +53,32 @@ struct I4Shape {
   static constexpr int META_BOX = 128 * 16;           // 128 rows x 8 groups x fp16
   static constexpr int META_BYTES = 4 * META_BOX;     // A scale, A zero, B scale, B zero
   static constexpr int META_SLOTS = 2;
-  static constexpr int SBF_BYTES = 2 * BN * 4;        // fp32 B scales, 2 slots
+  static constexpr int SBF_BYTES = SB_SLOTS * 3 * BN * 4;  // per slot: B scales, col/row terms
   static constexpr int EPI_BYTES = 8 * 4096;          // 8 warps x 32 rows x 128 B
   static constexpr int THREADS = 14 * 32;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int OFF_UN = 0;                                      // 1024-aligned
   static constexpr int OFF_PK = OFF_UN + UN_STAGES * UN_BYTES;
   static constexpr int OFF_META = OFF_PK + PK_STAGES * PK_BYTES;
-  static constexpr int OFF_EPI = OFF_META + META_SLOTS * META_BYTES;
-  static constexpr int OFF_SBF = OFF_EPI + EPI_BYTES;
+  // The output staging reuses the first unpacked stage: it is written only after
+  // the last MMA has completed (its accumulator was drained).
+  static constexpr int OFF_EPI = OFF_UN;
+  static constexpr int OFF_SBF = OFF_META + META_SLOTS * META_BYTES;
   static constexpr int OFF_BAR = OFF_SBF + SBF_BYTES;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
   static_assert(SMEM_BYTES <= 232448, "smem budget");
   static_assert(OFF_PK % 1024 == 0 && OFF_META % 1024 == 0 && OFF_EPI % 1024 == 0, "align");
+  static_assert(EPI_BYTES <= UN_BYTES, "staging alias");
+  static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
-// kind::i8, s32 accumulator, s8 x s8, both operands K-major, M = N = 128.
-constexpr uint32_t kI4Idesc = dev::make_idesc(2, 1, 1, 0, 0, I4Shape::BN, I4Shape::BM);
+// kind::i8, s32 accumulator, u8 x u8, both operands K-major, M = N = 128.
+constexpr uint32_t kI4Idesc = dev::make_idesc(2, 0, 0, 0, 0, I4Shape::BN, I4Shape::BM);
+constexpr int32_t kF32Magic = 0x4B400000;  // bit pattern of 12582912.0f = 1.5 * 2^23
 
+// DBG instantiation writes every exact group accumulator to Gdbg [M,N,K/128].
+template <bool DBG>
 __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap tmAq,
                         const __grid_constant__ CUtensorMap tmBq,
@@ -80,15 +95,15 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   uint64_t* pk_full = bars;                        // [4]
   uint64_t* pk_empty = bars + 4;                   // [4]
-  uint64_t* un_full = bars + 8;                    // [3]
-  uint64_t* un_empty = bars + 11;                  // [3]
-  uint64_t* acc_full = bars + 14;                  // [2]
-  uint64_t* acc_empty = bars + 16;                 // [2]
-  uint64_t* meta_full = bars + 18;                 // [2]
-  uint64_t* meta_empty = bars + 20;                // [2]
-  uint64_t* sb_full = bars + 22;                   // [2]
-  uint64_t* sb_empty = bars + 24;                  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  uint64_t* un_full = bars + 8;                    // [4]
+  uint64_t* un_empty = bars + 12;                  // [4]
+  uint64_t* acc_full = bars + 16;                  // [4]
+  uint64_t* acc_empty = bars + 20;                 // [4]
+  uint64_t* meta_full = bars + 24;                 // [2]
+  uint64_t* meta_empty = bars + 26;                // [2]
+  uint64_t* sb_full = bars + 28;                   // [4]
+  uint64_t* sb_empty = bars + 32;                  // [4]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 36);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbf = reinterpret_cast<float*>(smem + S::OFF_SBF);
 
@@ -107,13 +122,17 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       dev::mbar_init(&un_full[i], 4);
       dev::mbar_init(&un_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < S::ACC_BUFS; ++i) {
       dev::mbar_init(&acc_full[i], 1);
       dev::mbar_init(&acc_empty[i], 8);
-      dev::mbar_init(&meta_full[i], 1);
-      dev::mbar_init(&meta_empty[i], 12);
+    }
+    for (int i = 0; i < S::SB_SLOTS; ++i) {
       dev::mbar_init(&sb_full[i], 4);
       dev::mbar_init(&sb_empty[i], 8);
+    }
+    for (int i = 0; i < 2; ++i) {
+      dev::mbar_init(&meta_full[i], 1);
+      dev::mbar_init(&meta_empty[i], 12);
     }
     *abort_flag = 0;
     dev::fence_mbarrier_init();
@@ -145,7 +164,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         if ((g & 7) == 0) {
           const int c = g >> 3;
           const int slot = c & 1;
-          if (!dev::mbar_wait(&meta_empty[slot], ((c >> 1) & 1) ^ 1u, abort_flag)) break;
+          if (!dev::mbar_wait<true>(&meta_empty[slot], ((c >> 1) & 1) ^ 1u, abort_flag)) break;
           uint8_t* mt = smem + S::OFF_META + slot * S::META_BYTES;
           dev::mbar_arrive_expect_tx(&meta_full[slot], S::META_BYTES);
           dev::tma_load_2d(mt + 0 * S::META_BOX, &tmAs, &meta_full[slot], g, m0);
@@ -157,7 +176,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         }
         const int s = g % S::PK_STAGES;
         const uint32_t use = static_cast<uint32_t>(g / S::PK_STAGES);
-        if (!dev::mbar_wait(&pk_empty[s], (use & 1u) ^ 1u, abort_flag)) break;
+        if (!dev::mbar_wait<true>(&pk_empty[s], (use & 1u) ^ 1u, abort_flag)) break;
         uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
         dev::mbar_arrive_expect_tx(&pk_full[s], S::PK_BYTES);
         dev::tma_load_2d(pk, &tmAq, &pk_full[s], g * S::GB, m0);
@@ -179,10 +198,11 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     if (lane == 0) {
       for (int g = 0; g < NG; ++g) {
         const int u = g % S::UN_STAGES;
-        const int b = g & 1;
+        const int b = g % S::ACC_BUFS;
         if (!dev::mbar_wait(&un_full[u], static_cast<uint32_t>(g / S::UN_STAGES) & 1u, abort_flag))
           break;
-        if (!dev::mbar_wait(&acc_empty[b], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, abort_flag))
+        if (!dev::mbar_wait(&acc_empty[b], (static_cast<uint32_t>(g / S::ACC_BUFS) & 1u) ^ 1u,
+                            abort_flag))
           break;
         dev::tc_fence_after_sync();
         const uint32_t a_addr = dev::smem_u32(smem + S::OFF_UN + u * S::UN_BYTES);
@@ -207,12 +227,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const int mslot = c & 1;
       const int s = g % S::PK_STAGES;
       const int u = g % S::UN_STAGES;
-      const int sbs = g & 1;
+      const int sbs = g % S::SB_SLOTS;
       bool ok = true;
       if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&pk_full[s], static_cast<uint32_t>(g / S::PK_STAGES) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&un_empty[u], (static_cast<uint32_t>(g / S::UN_STAGES) & 1u) ^ 1u, abort_flag);
-      ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g / S::SB_SLOTS) & 1u) ^ 1u, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
 
       const uint8_t* mt = smem + S::OFF_META + mslot * S::META_BYTES;
@@ -220,17 +240,20 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const __half* meta_bs = reinterpret_cast<const __half*>(mt + 2 * S::META_BOX);
       const __half* meta_bz = reinterpret_cast<const __half*>(mt + 3 * S::META_BOX);
       const int gi = g & 7;
-      const uint32_t za4 = static_cast<uint32_t>(__half2int_rn(meta_az[t * 8 + gi]) & 0xff) * 0x01010101u;
-      const uint32_t zb4 = static_cast<uint32_t>(__half2int_rn(meta_bz[t * 8 + gi]) & 0xff) * 0x01010101u;
-      sbf[sbs * S::BN + t] = __half2float(meta_bs[t * 8 + gi]);
+      const int za = __half2int_rn(meta_az[t * 8 + gi]);
+      const int zb = __half2int_rn(meta_bz[t * 8 + gi]);
+      float* slot = sbf + sbs * 3 * S::BN;  // [B scale][16 Cc][row term]
+      slot[t] = __half2float(meta_bs[t * 8 + gi]);
 
       const uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
       uint8_t* un = smem + S::OFF_UN + u * S::UN_BYTES;
 #pragma unroll
       for (int op = 0; op < 2; ++op) {
-        const uint8_t* src = pk + op * S::PK_A + t * 64;       // 64B-swizzled packed row
+        const uint8_t* src = pk + op * S::PK_A + t * 64;                 // 64B-swizzled packed row
         const uint32_t dst = dev::smem_u32(un + op * S::UN_A + t * 128);  // 128B-swizzled row
-        const uint32_t z4 = op == 0 ? za4 : zb4;
+        const int z = op == 0 ? za : zb;
+        const uint32_t bias4 = static_cast<uint32_t>(16 - z) * 0x01010101u;
+        uint32_t hs = 0, ls = 0;  // byte lanes: sums of 16 nibbles each (<= 240, no carries)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint4 q = *reinterpret_cast<const uint4*>(src + ((j ^ ((t >> 1) & 3)) << 4));
@@ -238,13 +261,23 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
           uint32_t o[8];
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
-            o[2 * x] = __vsub4((w[x] >> 4) & 0x0f0f0f0fu, z4);
-            o[2 * x + 1] = __vsub4(w[x] & 0x0f0f0f0fu, z4);
+            const uint32_t hi = (w[x] >> 4) & 0x0f0f0f0fu;
+            const uint32_t lo = w[x] & 0x0f0f0f0fu;
+            hs += hi;
+            ls += lo;
+            o[2 * x] = hi + bias4;      // bytes code + 16 - z in [1, 31]: no carries
+            o[2 * x + 1] = lo + bias4;
           }
           const int c0 = 2 * j, c1 = 2 * j + 1;
           dev::st_shared_v4(dst + ((c0 ^ (t & 7)) << 4), o[0], o[1], o[2], o[3]);
           dev::st_shared_v4(dst + ((c1 ^ (t & 7)) << 4), o[4], o[5], o[6], o[7]);
         }
+        const int codes = static_cast<int>(__dp4a(hs, 0x01010101u, __dp4a(ls, 0x01010101u, 0u)));
+        const int r = codes - 128 * z;  // sum over the group of (code - z)
+        if (op == 0)
+          reinterpret_cast<int*>(slot)[2 * S::BN + t] = kF32Magic - 16 * r - 32768;
+        else
+          reinterpret_cast<int*>(slot)[S::BN + t] = 16 * r;
       }
       dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
       __syncwarp();
@@ -260,24 +293,29 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     const uint32_t q = warp & 3u;
     const int h = static_cast<int>(warp - 6) >> 2;  // column half of the tile
     const int row = static_cast<int>(q * 32 + lane);
-    float acc[64];
+    float2 acc[32];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.f, 0.f);
     bool ok = true;
     for (int g = 0; g < NG && ok; ++g) {
       const int c = g >> 3;
       const int mslot = c & 1;
-      const int b = g & 1;
-      const int sbs = g & 1;
+      const int b = g % S::ACC_BUFS;
+      const int sbs = g % S::SB_SLOTS;
       if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
-      ok = ok && dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g >> 1) & 1u, abort_flag);
-      ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g >> 1) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g / S::ACC_BUFS) & 1u, abort_flag);
+      ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g / S::SB_SLOTS) & 1u, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       dev::tc_fence_after_sync();
       const __half* meta_as = reinterpret_cast<const __half*>(smem + S::OFF_META + mslot * S::META_BYTES);
       const float sa = __half2float(meta_as[row * 8 + (g & 7)]);
-      const float* sb = sbf + sbs * S::BN + h * 64;
+      const float* slot = sbf + sbs * 3 * S::BN;
+      const float* sb = slot + h * 64;
+      const int* colt = reinterpret_cast<const int*>(slot) + S::BN + h * 64;
+      const int rowt = reinterpret_cast<const int*>(slot)[2 * S::BN + row];
+      const float2 sa2 = make_float2(sa, sa);
+      const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + static_cast<uint32_t>(b) * S::BN + h * 64;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -290,21 +328,31 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
           __syncwarp();
           if (lane == 0) dev::mbar_arrive(&acc_empty[b]);
         }
-        if (Gdbg != nullptr && m0 + row < M) {  // test hook: exact group accumulators
-          const int nb = n0 + h * 64 + half * 32;
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < N)
-              Gdbg[(static_cast<size_t>(m0 + row) * N + nb + j) * NG + g] =
-                  static_cast<int32_t>(j < 16 ? v0[j] : v1[j - 16]);
-        }
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 s4 = *reinterpret_cast<const float4*>(sb + half * 32 + j);
+          const int4 c4 = *reinterpret_cast<const int4*>(colt + half * 32 + j);
           const uint32_t* vv = j < 16 ? &v0[j] : &v1[j - 16];
-          acc[half * 32 + j + 0] += static_cast<float>(static_cast<int32_t>(vv[0])) * (sa * s4.x);
-          acc[half * 32 + j + 1] += static_cast<float>(static_cast<int32_t>(vv[1])) * (sa * s4.y);
-          acc[half * 32 + j + 2] += static_cast<float>(static_cast<int32_t>(vv[2])) * (sa * s4.z);
-          acc[half * 32 + j + 3] += static_cast<float>(static_cast<int32_t>(vv[3])) * (sa * s4.w);
+          // fp32 bit patterns of 12582912 + G: one 3-input add each.
+          const int f0 = static_cast<int>(vv[0]) + rowt - c4.x;
+          const int f1 = static_cast<int>(vv[1]) + rowt - c4.y;
+          const int f2 = static_cast<int>(vv[2]) + rowt - c4.z;
+          const int f3 = static_cast<int>(vv[3]) + rowt - c4.w;
+          const float2 g01 = __fadd2_rn(make_float2(__int_as_float(f0), __int_as_float(f1)), neg_magic);
+          const float2 g23 = __fadd2_rn(make_float2(__int_as_float(f2), __int_as_float(f3)), neg_magic);
+          const float2 s01 = __fmul2_rn(sa2, make_float2(s4.x, s4.y));
+          const float2 s23 = __fmul2_rn(sa2, make_float2(s4.z, s4.w));
+          const int a = (half * 32 + j) >> 1;
+          acc[a] = __ffma2_rn(g01, s01, acc[a]);
+          acc[a + 1] = __ffma2_rn(g23, s23, acc[a + 1]);
+          if (DBG && m0 + row < M) {  // test hook: exact group accumulators
+            const int nb = n0 + h * 64 + half * 32 + j;
+            const int fs[4] = {f0, f1, f2, f3};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (nb + e < N)
+                Gdbg[(static_cast<size_t>(m0 + row) * N + nb + e) * NG + g] = fs[e] - kF32Magic;
+          }
         }
       }
       __syncwarp();
@@ -319,10 +367,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const uint32_t sa_ = dev::smem_u32(stg);
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
-        const uint32_t o0 = dev::pack_half2(acc[p * 8 + 0], acc[p * 8 + 1]);
-        const uint32_t o1 = dev::pack_half2(acc[p * 8 + 2], acc[p * 8 + 3]);
-        const uint32_t o2 = dev::pack_half2(acc[p * 8 + 4], acc[p * 8 + 5]);
-        const uint32_t o3 = dev::pack_half2(acc[p * 8 + 6], acc[p * 8 + 7]);
+        const uint32_t o0 = dev::pack_half2(acc[p * 4 + 0].x, acc[p * 4 + 0].y);
+        const uint32_t o1 = dev::pack_half2(acc[p * 4 + 1].x, acc[p * 4 + 1].y);
+        const uint32_t o2 = dev::pack_half2(acc[p * 4 + 2].x, acc[p * 4 + 2].y);
+        const uint32_t o3 = dev::pack_half2(acc[p * 4 + 3].x, acc[p * 4 + 3].y);
         dev::st_shared_v4(sa_ + lane * 128 + ((p ^ (lane & 7)) << 4), o0, o1, o2, o3);
       }
       dev::fence_proxy_async_smem();

@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         bool ok = true;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
-          if (!dev::mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          if (!dev::mbar_wait<true>(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(192, 1)
         // Error unwinding: let every load still in flight land before the CTA exits.
         volatile int no_abort = 0;
         for (int s = 0; s < S::STAGES; ++s)
-          if (armed & (1u << s)) dev::mbar_wait(&full[s], (armed_parity >> s) & 1u, &no_abort);
+          if (armed & (1u << s)) dev::mbar_wait<true>(&full[s], (armed_parity >> s) & 1u, &no_abort);
       }
     }
     __syncwarp();
@@ -228,11 +228,11 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = tile_first; tile < num_tiles && ok; tile += tile_stride, ++it) {
         const uint32_t buf = static_cast<uint32_t>(it) & (S::ACC_BUFS - 1);
         const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
-        if (!dev::mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag)) break;
+        if (!dev::mbar_wait<true>(&tempty[buf], (use & 1u) ^ 1u, abort_flag)) break;
         dev::tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
-          if (!dev::mbar_wait(&full[stage], phase, abort_flag)) {
+          if (!dev::mbar_wait<true>(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
       bool have_acc = kb_end > kb_begin;
       if (have_acc) {
-        const bool got = __all_sync(0xffffffffu, dev::mbar_wait(&tfull[buf], use & 1u, abort_flag));
+        const bool got = __all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag));
         if (!got) {
           // Split mode must still pass the cluster barriers below (with zeros).
           if constexpr (!SPLIT) break;

@@ -77,27 +77,45 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// With SLEEP, a waiting thread may be suspended up to kTryWaitSuspendNs inside one
+// try_wait (it resumes as soon as the phase completes), so warps that wait long
+// (an epilogue waiting for a whole tile) do not compete for issue slots. Waits on
+// short hand-offs use the plain form.
+constexpr uint32_t kTryWaitSuspendNs = 1000000u;
+
+template <bool SLEEP = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred P1;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, P1;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if constexpr (SLEEP) {
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitSuspendNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
 // Waits for the phase with the given parity to complete. Gives up (returns
 // false) when *abort becomes non-zero or after kWaitTimeoutNs; on a timeout it
 // records the error and raises *abort so that the CTA's other roles unwind too.
+template <bool SLEEP = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<SLEEP>(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if (mbar_try_wait<SLEEP>(bar, parity)) return true;
+    if ((i & (SLEEP ? 3u : 63u)) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
         record_error(kDevErrWaitTimeout);
