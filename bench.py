@@ -257,6 +257,9 @@ def _secondary(cc, torch, peaks):
     Bq, Bs, Bz = dev(op.B_q), dev(op.B_scale), dev(op.B_zero)
     C = torch.empty((M, N), dtype=torch.float16, device="cuda")
     t = timeit(lambda i: cc.gemm_int4(Aq[i], As[i], Az[i], Bq, Bs, Bz, C), copies, 400)
+    cc.set_weight_prefetch(True)
+    t_pf = timeit(lambda i: cc.gemm_int4(Aq[i], As[i], Az[i], Bq, Bs, Bz, C), copies, 400)
+    cc.set_weight_prefetch(False)
     nbytes = M * K // 2 + 2 * 2 * M * K // 128 + N * K // 2 + 2 * 2 * N * K // 128 + 2 * M * N
     out["int4_decode_4096x1x4096"] = {
         "kernel": cc.describe_dispatch("int4", M, N, K), "us_per_call": round(t * 1e6, 3),
@@ -264,7 +267,12 @@ def _secondary(cc, torch, peaks):
         "roofline": {"bound": "hbm", "achieved": round(nbytes / t / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 4)},
-        "working_set_MB": round(copies * nbytes / 1e6, 1)}
+        "working_set_MB": round(copies * nbytes / 1e6, 1),
+        "weight_prefetch": {
+            "us_per_call": round(t_pf * 1e6, 3), "GBps": round(nbytes / t_pf / 1e9, 1),
+            "frac": round(nbytes / t_pf / 1e9 / peaks["hbm_gbs"], 4),
+            "note": "clove_set_weight_prefetch(1): each call streams its (distinct) weight "
+                    "matrix while the previous call drains"}}
     del Aq, As, Az
 
     # config 3: int8 batch-32 with per-row / per-column scales

@@ -181,6 +181,12 @@ def set_dispatch_override(path: int = 0, bn: int = 0, split: int = 0) -> None:
     check(lib().clove_set_dispatch_override(int(path), int(bn), int(split)))
 
 
+def set_weight_prefetch(enable: bool) -> None:
+    """Let decode kernels stream the weight operand before the previous kernel on the
+    stream finishes (only when no in-flight kernel writes that operand)."""
+    check(lib().clove_set_weight_prefetch(int(bool(enable))))
+
+
 def describe_dispatch(dtype: str, M: int, N: int, K: int) -> str:
     code = {"fp16": 0, "int8": 1, "int4": 2}[dtype]
     buf = ctypes.create_string_buffer(128)

@@ -51,6 +51,42 @@ int launch_pdl(void (*kernel)(KArgs...), unsigned grid, size_t smem, cudaStream_
 }
 
 template <int NC, int P>
+int gemv_int4_ws(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                 const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
+                 long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
+  int grid = dev.num_sms;
+  if (rows < grid * 8) grid = (rows + 7) / 8;
+  const int per_cta = (rows + grid - 1) / grid;
+  const int chunks = (per_cta + kern::kWsChunkRows - 1) / kern::kWsChunkRows;
+  const int chunk_bytes = kern::gemv_ws_chunk_bytes(K);
+  // <= ~100 KB so that the next kernel's CTA fits beside this one (overlap under PDL).
+  int slots = (100 * 1024) / (chunk_bytes + 16);
+  if (slots > chunks) slots = chunks;
+  if (slots < 2) slots = 2;  // two chunks are consumed per pass
+  const size_t smem = static_cast<size_t>(slots) * (chunk_bytes + 16);
+  auto kernel = kern::gemv_int4_ws_kernel<NC, P>;
+  int rc = prepare(kernel, smem);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kern::kWsThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int early = weight_prefetch_enabled() ? 1 : 0;
+  return check_cuda(
+      cudaLaunchKernelEx(&cfg, kernel, Aq, static_cast<const __half*>(As),
+                         static_cast<const __half*>(Az), Bq, static_cast<const __half*>(Bs),
+                         static_cast<const __half*>(Bz), static_cast<__half*>(C), rows, K, ldc_row,
+                         ldc_col, slots, early),
+      "gemv_int4_ws launch");
+}
+
+template <int NC, int P>
 int gemv_int4_reg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                   const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int K,
                   long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col,
@@ -132,6 +168,18 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
   // Register-resident B when this lane's share of the vectors fits (nc * P <= 8,
   // P = 1024-element windows per row) and the 16-byte B loads are aligned.
   const int P = (K + 1023) / 1024;
+  // Warp-specialised bulk-copy kernel: whole 1024-element windows, 16-byte aligned
+  // rows of codes, scales and zero points (K % 1024 == 0), no debug output.
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (Gdbg == nullptr && K % 1024 == 0 && K <= 24576 && nc * P <= 8 && a16(Aq) && a16(As) &&
+      a16(Az) && a16(Bq) && !ws_disabled()) {
+#define WS(n, p)                                                                            \
+  if (nc == n && P == p)                                                                     \
+    return gemv_int4_ws<n, p>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
+    WS(1, 1) WS(1, 2) WS(1, 3) WS(1, 4) WS(1, 5) WS(1, 6) WS(1, 7) WS(1, 8)
+    WS(2, 1) WS(2, 2) WS(2, 3) WS(2, 4)
+#undef WS
+  }
   if (nc * P <= 8 && (reinterpret_cast<uintptr_t>(Bq) & 15u) == 0) {
 #define REG(n, p)                                                                          \
   if (nc == n && P == p)                                                                    \

@@ -318,6 +318,186 @@ __global__ void __launch_bounds__(kGemvThreads)
   }
 }
 
+// INT4 decode, warp-specialised: one CTA per SM owns a contiguous block of rows.
+// Warp 8 (one thread) moves the block into a shared-memory ring in chunks of 8
+// rows -- three cp.async.bulk copies per chunk (codes, scales, zero points; the
+// rows of a chunk are contiguous in each of the three row-major arrays), so a
+// chunk costs three copy operations rather than three per row -- and issues every
+// chunk that fits in the ring at once. Warps 0-7 take one row of each chunk; each
+// lane holds the (b - zB) codes of its fixed 16-byte chunks in registers (as in
+// gemv_int4_reg_kernel). With weights_early the copies are issued before
+// griddepcontrol.wait, i.e. while the previous kernel on the stream drains (only
+// valid when no in-flight kernel writes A).
+constexpr int kWsConsumerWarps = 8;
+constexpr int kWsThreads = (kWsConsumerWarps + 1) * 32;
+constexpr int kWsChunkRows = kWsConsumerWarps;
+
+// Shared bytes of one chunk: codes [8][K/2], then scales [8][K/128], zeros [8][K/128].
+__host__ __device__ constexpr int gemv_ws_chunk_bytes(int K) {
+  return kWsChunkRows * (K / 2 + 4 * (K / 128));
+}
+
+template <int NC, int P>
+__global__ void __launch_bounds__(kWsThreads)
+    gemv_int4_ws_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
+                        const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
+                        const __half* __restrict__ Bs, const __half* __restrict__ Bz,
+                        __half* __restrict__ C, int rows, int K, long long ldc_row,
+                        long long ldc_col, int slots, int weights_early) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int NG = K >> 7;
+  const int NCH = K >> 5;
+  const int KB = K >> 1;
+  const int chunk_bytes = gemv_ws_chunk_bytes(K);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(slots) * chunk_bytes);
+  uint64_t* empty = full + slots;
+  __shared__ int abort_s;
+  volatile int* abort_flag = &abort_s;
+
+  const int warp = static_cast<int>(dev::warp_idx());
+  const int lane = static_cast<int>(dev::lane_idx());
+  const int per_cta = (rows + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * per_cta;
+  const int nrows = max(0, min(rows, r0 + per_cta) - r0);
+  const int nchunks = (nrows + kWsChunkRows - 1) / kWsChunkRows;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < slots; ++i) {
+      dev::mbar_init(&full[i], 1);
+      dev::mbar_init(&empty[i], kWsConsumerWarps);
+    }
+    abort_s = 0;
+    dev::fence_mbarrier_init();
+  }
+  __syncthreads();
+  dev::allow_dependent_launch();
+
+  if (warp == kWsConsumerWarps) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      if (!weights_early) dev::grid_dependency_wait();
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % slots;
+        const uint32_t use = static_cast<uint32_t>(c / slots);
+        if (use > 0 && !dev::mbar_wait(&empty[s], (use & 1u) ^ 1u, abort_flag)) break;
+        const int cr = min(kWsChunkRows, nrows - c * kWsChunkRows);
+        const size_t m = static_cast<size_t>(r0 + c * kWsChunkRows);
+        uint8_t* dst = smem + static_cast<size_t>(s) * chunk_bytes;
+        dev::mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(cr * (KB + 4 * NG)));
+        dev::bulk_load_1d(dst, Aq + m * KB, static_cast<uint32_t>(cr * KB), &full[s]);
+        dev::bulk_load_1d(dst + kWsChunkRows * KB, As + m * NG, static_cast<uint32_t>(cr * 2 * NG),
+                          &full[s]);
+        dev::bulk_load_1d(dst + kWsChunkRows * (KB + 2 * NG), Az + m * NG,
+                          static_cast<uint32_t>(cr * 2 * NG), &full[s]);
+      }
+      if (*abort_flag) {  // let copies still in flight land before the CTA exits
+        volatile int no_abort = 0;
+        for (int c = max(0, nchunks - slots); c < nchunks; ++c)
+          dev::mbar_wait(&full[c % slots], static_cast<uint32_t>(c / slots) & 1u, &no_abort);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  dev::grid_dependency_wait();  // B and C may belong to the previous kernel
+  uint32_t bw[NC][P][8];
+  int bsum[NC][P];
+  float bsc[NC][P];
+#pragma unroll
+  for (int n = 0; n < NC; ++n)
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int ch = p * 32 + lane;
+      uint4 q = make_uint4(0u, 0u, 0u, 0u);
+      int zb = 0;
+      bsc[n][p] = 0.f;
+      if (ch < NCH) {
+        q = *reinterpret_cast<const uint4*>(Bq + static_cast<size_t>(n) * KB + static_cast<size_t>(ch) * 16);
+        zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (ch >> 2)]);
+        bsc[n][p] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
+      }
+      const uint32_t zq = static_cast<uint32_t>(zb & 0xff) * 0x01010101u;
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      int sum = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        bw[n][p][2 * u] = __vsub4((w[u] >> 4) & 0x0f0f0f0fu, zq);
+        bw[n][p][2 * u + 1] = __vsub4(w[u] & 0x0f0f0f0fu, zq);
+        sum = __dp4a(static_cast<int>(bw[n][p][2 * u]), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(bw[n][p][2 * u + 1]), 0x01010101, sum);
+      }
+      bsum[n][p] = ch < NCH ? sum : 0;
+    }
+
+  // Two chunks per pass: this warp's rows of both are reduced together (ILP).
+  for (int c0 = 0; c0 < nchunks; c0 += 2) {
+    const int nc2 = min(2, nchunks - c0);
+    bool ok = true;
+    for (int k = 0; k < nc2; ++k) {
+      const int c = c0 + k;
+      ok = ok && dev::mbar_wait(&full[c % slots], static_cast<uint32_t>(c / slots) & 1u, abort_flag);
+    }
+    if (!__all_sync(0xffffffffu, ok)) break;
+    float acc[2][NC];
+    const uint8_t* rowp[2];
+    const __half* ras[2];
+    const __half* raz[2];
+    bool live[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int c = c0 + (k < nc2 ? k : 0);
+      const uint8_t* base = smem + static_cast<size_t>(c % slots) * chunk_bytes;
+      rowp[k] = base + warp * KB;
+      ras[k] = reinterpret_cast<const __half*>(base + kWsChunkRows * KB) + warp * NG;
+      raz[k] = reinterpret_cast<const __half*>(base + kWsChunkRows * (KB + 2 * NG)) + warp * NG;
+      live[k] = k < nc2 && (c0 + k) * kWsChunkRows + warp < nrows;
+#pragma unroll
+      for (int n = 0; n < NC; ++n) acc[k][n] = 0.f;
+    }
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int ch = p * 32 + lane;
+      const bool valid = ch < NCH;
+      const int chc = valid ? ch : 0;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint4 a = *reinterpret_cast<const uint4*>(rowp[k] + chc * 16);
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+        const int za = __half2int_rn(raz[k][chc >> 2]);
+        const float sa = __half2float(ras[k][chc >> 2]);
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+          int d0 = 0, d1 = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            d0 = __dp4a(static_cast<int>((w[u] >> 4) & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u]), d0);
+            d1 = __dp4a(static_cast<int>(w[u] & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u + 1]), d1);
+          }
+          int g = valid ? d0 + d1 - za * bsum[n][p] : 0;
+          g += __shfl_xor_sync(0xffffffffu, g, 1);
+          g += __shfl_xor_sync(0xffffffffu, g, 2);
+          if ((lane & 3) == 0 && valid) acc[k][n] += static_cast<float>(g) * (sa * bsc[n][p]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+#pragma unroll
+      for (int n = 0; n < NC; ++n) {
+        const float t = warp_sum_f32(acc[k][n]);
+        const int m = r0 + (c0 + k) * kWsChunkRows + warp;
+        if (lane == 0 && live[k]) C[m * ldc_row + n * ldc_col] = __float2half_rn(t);
+      }
+    }
+    __syncwarp();
+    if (lane == 0)
+      for (int k = 0; k < nc2; ++k)
+        if (c0 + k + slots < nchunks) dev::mbar_arrive(&empty[(c0 + k) % slots]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // INT8: A int8 [rows, K] streamed, B int8 [K, NC] row-major (reference layout).
 // ---------------------------------------------------------------------------

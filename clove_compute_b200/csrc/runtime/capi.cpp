@@ -23,6 +23,7 @@ namespace rt {
 namespace {
 thread_local char g_last_error[512] = "no error";
 std::atomic<int> g_ov_path{0}, g_ov_bn{0}, g_ov_split{0};
+std::atomic<int> g_weight_prefetch{0};
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
@@ -84,6 +85,9 @@ int current_device(DeviceInfo* out) {
 Override get_override() {
   return Override{g_ov_path.load(), g_ov_bn.load(), g_ov_split.load()};
 }
+
+bool weight_prefetch_enabled() { return g_weight_prefetch.load() != 0; }
+bool ws_disabled() { return g_ov_path.load() == 2 && g_ov_bn.load() == 1; }
 
 // ---------------------------------------------------------------------------
 // Tile-shape policy for the tensor-core kernels
@@ -162,6 +166,11 @@ int clove_get_device_error(int* code) {
     if (v == 0 && r != 0) v = r;
   }
   *code = v;
+  return CLOVE_OK;
+}
+
+int clove_set_weight_prefetch(int enable) {
+  g_weight_prefetch.store(enable ? 1 : 0);
   return CLOVE_OK;
 }
 

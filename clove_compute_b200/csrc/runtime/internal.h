@@ -38,6 +38,13 @@ struct Override {
 };
 Override get_override();
 
+// clove_set_weight_prefetch: decode kernels may stream their weight operand before
+// the previous kernel on the stream has finished.
+bool weight_prefetch_enabled();
+// Test hook: path 2 with bn == 1 forces the register GEMV instead of the
+// warp-specialised one.
+bool ws_disabled();
+
 // Tile shape chosen for a tensor-core call (capi.cpp).
 struct TcPlan {
   int bn;

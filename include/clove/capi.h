@@ -123,6 +123,14 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
  * factor (0 = automatic, 1 = none, 2..8). Returns CLOVE_OK. */
 int clove_set_dispatch_override(int path, int bn, int split);
 
+/* Decode kernels (N <= 8 or M <= 8) start streaming their large operand -- the
+ * weight matrix -- before the previous kernel on the stream has finished, which
+ * hides the launch and first-byte latency of back-to-back decode GEMMs (programmatic
+ * dependent launch). Only valid when no kernel still running on the stream writes
+ * that operand, as for model weights in a decode loop; the small operand and C are
+ * always accessed after the previous kernel completes. Process-wide; default off. */
+int clove_set_weight_prefetch(int enable);
+
 /* Describes the kernel the automatic dispatch picks for a shape:
  * dtype 0 = fp16, 1 = int8, 2 = int4. Writes a short name into buf. */
 int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t buflen);

@@ -24,7 +24,8 @@ def _ops_dev(op):
 
 def _check(cc, oracle, M, N, K, path=0, seed=0, check_g=True):
     op = wl.int4_operands(M, N, K, seed=seed)
-    cc.set_dispatch_override(path, 0, 0)
+    if path != 2:
+        cc.set_dispatch_override(path, 0, 0)
     args = _ops_dev(op)
     C = host(cc.gemm_int4(*args))
     ref = oracle.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K)
@@ -99,3 +100,36 @@ def test_k_not_multiple_of_group_rejected(clove_lib, cuda):
     with pytest.raises((CloveError, ValueError)):
         clove_lib.gemm_int4(torch.zeros((M, K // 2), dtype=torch.uint8, device="cuda"), z(M), z(M),
                             torch.zeros((N, K // 2), dtype=torch.uint8, device="cuda"), z(N), z(N))
+
+
+@pytest.mark.parametrize("prefetch", [False, True])
+def test_decode_back_to_back_ordering(clove_lib, oracle_mod, cuda, prefetch):
+    """Consecutive decode calls on one stream with programmatic dependent launch:
+    each call must see the activation vector the preceding kernel just wrote, and
+    each output must match the oracle (with and without weight prefetch)."""
+    import torch
+    M, K = 4096, 4096
+    ops = [wl.int4_operands(M, 1, K, seed=s) for s in range(4)]
+    Ad = [(dev(o.A_q), dev(o.A_scale), dev(o.A_zero)) for o in ops]
+    Bsrc = [(dev(o.B_q), dev(o.B_scale), dev(o.B_zero)) for o in ops]
+    Bq = torch.empty_like(Bsrc[0][0]); Bs = torch.empty_like(Bsrc[0][1]); Bz = torch.empty_like(Bsrc[0][2])
+    outs = [torch.empty((M, 1), dtype=torch.float16, device="cuda") for _ in ops]
+    clove_lib.set_weight_prefetch(prefetch)
+    try:
+        for rep in range(3):
+            for i in range(len(ops)):
+                Bq.copy_(Bsrc[i][0]); Bs.copy_(Bsrc[i][1]); Bz.copy_(Bsrc[i][2])
+                clove_lib.gemm_int4(*Ad[i], Bq, Bs, Bz, outs[i])
+        torch.cuda.synchronize()
+    finally:
+        clove_lib.set_weight_prefetch(False)
+    for i, o in enumerate(ops):
+        ref = oracle_mod.gemm_int4(o.A_q, o.A_scale, o.A_zero, o.B_q, o.B_scale, o.B_zero, K)
+        assert rel_fro(host(outs[i]), ref) < TOL_TIGHT
+    assert clove_lib.device_error() == 0
+
+
+def test_register_gemv_path(clove_lib, oracle_mod, cuda):
+    """The register-resident GEMV (used when the bulk-copy kernel does not apply)."""
+    clove_lib.set_dispatch_override(2, 1, 0)
+    _check(clove_lib, oracle_mod, 4096, 1, 4096, path=2, seed=3, check_g=False)
