@@ -1,0 +1,252 @@
+// gemm_tc2_sm100.cuh -- CTA-pair tcgen05 GEMM (cta_group::2), 256 x 256 tiles.
+//
+// Same operands, layouts and epilogues as gemm_tc_kernel (A row-major [M,K]
+// K-major, B row-major [K,N] MN-major, C row-major fp16), for the large prefill
+// shapes. A cluster of two CTAs on two SMs computes one 256 x 256 tile of C:
+//   * each CTA TMA-loads its own 128 rows of A and its own 128 columns of B for a
+//     K block (32 KB per stage instead of 48 KB for a 128 x 256 tile on one SM,
+//     so the pair pulls a third less L2 data per FLOP and fits 6 stages); the
+//     loads' transaction bytes complete on the leader CTA's full barrier;
+//   * the leader's MMA thread issues tcgen05.mma.cta_group::2 (M = 256, N = 256):
+//     the tensor cores of both SMs read A from their own CTA and B from both, and
+//     each SM's TMEM receives its 128 rows x 256 fp32 accumulator columns;
+//     tcgen05.commit multicasts stage-free and accumulator-ready arrivals to both
+//     CTAs (a commit multicast, not a TMA multicast);
+//   * each CTA's 4 epilogue warps drain their own TMEM (two 256-column buffers)
+//     and arrive on the leader's accumulator-free barrier, remotely for the peer.
+// No TMA load in this kernel uses .multicast::cluster.
+#pragma once
+
+#include "gemm_tc_sm100.cuh"
+
+namespace clove {
+namespace kern {
+
+template <class Op>
+struct Tc2Shape {
+  static constexpr int BM = 128;        // rows per CTA (256 per pair)
+  static constexpr int BN = 256;        // accumulator columns (the pair's N tile)
+  static constexpr int BNH = 128;       // columns of B loaded by each CTA
+  static constexpr int ELEM = Op::kElemBytes;
+  static constexpr int BK = 128 / ELEM;
+  static constexpr int UMMA_K = 32 / ELEM;
+  static constexpr int KSTEPS = BK / UMMA_K;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int BH_BYTES = BNH * ELEM;        // bytes of one B row (this CTA's half)
+  static constexpr int B_SW = 128;
+  static constexpr int B_ATOMS = BH_BYTES / B_SW;
+  static constexpr int B_ATOM_ELEMS = B_SW / ELEM;
+  static constexpr int B_BYTES = BK * BH_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int CHUNK = 64;                    // fp16 output columns per store
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int STAGES_FIT = (kSmemLimit - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(B_ATOMS >= 1 && BH_BYTES % B_SW == 0, "B half in whole 128-byte atoms");
+  static_assert(STAGES >= 3 && SMEM_BYTES <= kSmemLimit, "smem budget");
+  static_assert(TMEM_COLS <= 512, "TMEM");
+};
+
+template <class Op>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep) {
+  using S = Tc2Shape<Op>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  uint8_t* epi_base = smem + S::STAGES * S::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_base + S::EPI_BYTES);
+  uint64_t* full = bars;                    // leader's used (both CTAs' bytes)
+  uint64_t* empty = bars + S::STAGES;       // both CTAs (commit multicast)
+  uint64_t* tfull = bars + 2 * S::STAGES;   // both CTAs (commit multicast)
+  uint64_t* tempty = tfull + 2;             // leader's used (4 local + 4 remote arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = dev::warp_idx();
+  const uint32_t lane = dev::lane_idx();
+  const uint32_t rank = dev::cluster_ctarank();  // 0 = leader of the pair
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      dev::mbar_init(&full[s], 1);
+      dev::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      dev::mbar_init(&tfull[b], 1);
+      dev::mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    dev::fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    dev::prefetch_tmap(&tmA);
+    dev::prefetch_tmap(&tmB);
+    dev::prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    dev::tmem_relinquish_alloc_permit_pair();
+  }
+  dev::tc_fence_before_sync();
+  dev::cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA use
+  dev::tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + 2 * S::BM - 1) / (2 * S::BM);
+  const int tiles_n = (N + S::BN - 1) / S::BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kb_total = (K + S::BK - 1) / S::BK;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      for (int tile = pair; tile < num_tiles; tile += pairs) {
+        int m_blk, n_blk;
+        tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+        const int my_m = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
+        const int my_n = n_blk * S::BN + static_cast<int>(rank) * S::BNH;
+        bool ok = true;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!dev::mbar_wait<true>(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) dev::mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+          uint8_t* a_dst = stage_base + stage * S::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + S::A_BYTES;
+          dev::tma_load_2d_pair(a_dst, &tmA, &full[stage], kb * S::BK, my_m);
+#pragma unroll
+          for (int a = 0; a < S::B_ATOMS; ++a)
+            dev::tma_load_2d_pair(b_dst + a * (S::BK * S::B_SW), &tmB, &full[stage],
+                                  my_n + a * S::B_ATOM_ELEMS, kb * S::BK);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const uint32_t idesc = Op::kInt ? dev::make_idesc(2, 1, 1, 0, 1, S::BN, 2 * S::BM)
+                                      : dev::make_idesc(1, 0, 0, 0, 1, S::BN, 2 * S::BM);
+      uint32_t stage = 0, phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs, ++it) {
+        const uint32_t buf = static_cast<uint32_t>(it) & 1u;
+        const uint32_t use = static_cast<uint32_t>(it) >> 1;
+        if (!dev::mbar_wait<true>(&tempty[buf], (use & 1u) ^ 1u, abort_flag)) break;
+        dev::tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + buf * S::BN;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!dev::mbar_wait<true>(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after_sync();
+          const uint32_t a_addr = dev::smem_u32(stage_base + stage * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < S::KSTEPS; ++k) {
+            const uint64_t adesc = dev::make_smem_desc(a_addr + k * 32, 0, 1024, dev::kLayoutSw128);
+            const uint64_t bdesc = dev::make_smem_desc(b_addr + k * S::UMMA_K * S::B_SW,
+                                                       S::BK * S::B_SW, 8 * S::B_SW,
+                                                       dev::kLayoutSw128);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (Op::kInt)
+              dev::mma_i8_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
+            else
+              dev::mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
+          }
+          dev::mma_commit_pair(&empty[stage], 0x3);  // frees the stage in both CTAs
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        dev::mma_commit_pair(&tfull[buf], 0x3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const uint32_t q = warp & 3u;
+    const int row_in_tile = static_cast<int>(q * 32 + lane);
+    uint8_t* stg_base = epi_base + (warp - 2) * (2 * 4096);
+    uint32_t stg_count = 0;
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += pairs, ++it) {
+      int m_blk, n_blk;
+      tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+      const uint32_t buf = static_cast<uint32_t>(it) & 1u;
+      const uint32_t use = static_cast<uint32_t>(it) >> 1;
+      if (!__all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag))) break;
+      dev::tc_fence_after_sync();
+      const int m0 = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
+      const int n0 = n_blk * S::BN;
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16) + buf * S::BN;
+
+      float row_scale = 0.f;
+      int32_t row_corr = 0;
+      if (ep.mode == kEpiI8RowCol) row_scale = (row < M) ? ep.row_scale[row] : 0.f;
+      if ((ep.mode == kEpiI8Tensor || ep.mode == kEpiI32Raw) && ep.zb != 0 && row < M)
+        row_corr = static_cast<int32_t>(0u - static_cast<uint32_t>(ep.zb) *
+                                                 static_cast<uint32_t>(ep.row_sum[row]));
+#pragma unroll 1
+      for (int c0 = 0; c0 < S::BN; c0 += S::CHUNK) {
+        uint32_t v[S::CHUNK];
+#pragma unroll
+        for (int j = 0; j < S::CHUNK; j += 16) {
+          uint32_t t[16];
+          dev::tmem_ld_x16(t_row + c0 + j, t);
+          dev::tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+        }
+        if (c0 + S::CHUNK >= S::BN) {
+          // Accumulator drained: release it to the leader's MMA thread.
+          dev::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader)
+              dev::mbar_arrive(&tempty[buf]);
+            else
+              dev::mbar_arrive_remote(&tempty[buf], 0);
+          }
+        }
+        store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
+                                     stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32);
+      }
+      if (*abort_flag) break;
+    }
+    if (lane == 0) dev::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // No CTA leaves while its pair may still touch its shared memory or TMEM.
+  dev::tc_fence_before_sync();
+  dev::cluster_sync_all();
+  if (warp == 1) {
+    dev::tc_fence_after_sync();
+    dev::tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace kern
+}  // namespace clove

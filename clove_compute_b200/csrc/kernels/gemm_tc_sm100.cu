@@ -4,6 +4,7 @@
 
 #include <atomic>
 
+#include "gemm_tc2_sm100.cuh"
 #include "gemm_tc_sm100.cuh"
 #include "../runtime/internal.h"
 #include "../runtime/tensor_map.h"
@@ -159,6 +160,66 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
     cfg.numAttrs = 0;
   }
   return check_cuda(cudaLaunchKernelExC(&cfg, e->fn, args), "gemm_tc launch");
+}
+
+}  // namespace rt
+}  // namespace clove
+
+namespace clove {
+namespace rt {
+
+namespace {
+std::atomic<uint64_t> g_tc2_attr[2];
+}
+
+// CTA-pair 256 x 256 tile kernel (fp16 C only).
+int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
+                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream) {
+  using SF = kern::Tc2Shape<kern::OpF16>;
+  using SI = kern::Tc2Shape<kern::OpI8>;
+  const bool f16 = op == kTcF16;
+  const void* fn = f16 ? reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpF16>)
+                       : reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpI8>);
+  const int smem = f16 ? SF::SMEM_BYTES : SI::SMEM_BYTES;
+  const int bk = f16 ? SF::BK : SI::BK;
+  const int b_atom = f16 ? SF::B_ATOM_ELEMS : SI::B_ATOM_ELEMS;
+  const int elem = f16 ? 2 : 1;
+  const CUtensorMapDataType in_dt =
+      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap tmA, tmB, tmC;
+  int rc = encode_tmap_2d(&tmA, in_dt, elem, A, K, M, static_cast<uint64_t>(K) * elem, bk, 128, 128);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tmB, in_dt, elem, B, N, K, static_cast<uint64_t>(N) * elem, b_atom, bk, 128);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, N, M,
+                      static_cast<uint64_t>(N) * 2, 64, 32, 128);
+  if (rc) return rc;
+  const uint64_t bit = 1ull << (dev.device & 63);
+  std::atomic<uint64_t>& attr = g_tc2_attr[f16 ? 0 : 1];
+  if ((attr.load(std::memory_order_acquire) & bit) == 0) {
+    rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                    "cudaFuncSetAttribute(tc2 smem)");
+    if (rc) return rc;
+    attr.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  int pairs = dev.num_sms / 2;
+  if (pairs > tiles) pairs = tiles;
+  kern::EpiParams epv = ep;
+  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "gemm_tc2 launch");
 }
 
 }  // namespace rt

@@ -105,6 +105,95 @@ __device__ __forceinline__ uint32_t swz_chunk(uint32_t row, uint32_t chunk, uint
   return chunk ^ (((row * row_bytes) >> 7) & mask);
 }
 
+// Epilogue of one CHUNK-column slice of a 32-row warp slab: fp16 (or raw int32)
+// math on this thread's row, swizzled staging, TMA store of the warp's slab.
+template <class Op, int OUT_BYTES, int CHUNK>
+__device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const EpiParams& ep,
+                                            int row, int ncol0, int M, int N, int K,
+                                            float row_scale, int32_t row_corr, uint32_t lane,
+                                            uint8_t* stg_base, uint32_t& stg_count,
+                                            const CUtensorMap* tmC, int store_row0) {
+  // Epilogue math -> 16-byte packets.
+  constexpr int STG_ROW = CHUNK * OUT_BYTES;
+  constexpr int PKTS = STG_ROW / 16;
+  uint32_t pk[PKTS][4];
+  if constexpr (OUT_BYTES == 2) {
+    float f[CHUNK];
+    if (ep.mode == kEpiF16AlphaBeta) {
+#pragma unroll
+      for (int j = 0; j < CHUNK; ++j) f[j] = ep.alpha * __uint_as_float(v[j]);
+      if (ep.beta != 0.f && row < M) {
+        const __half* crow = ep.c_in + static_cast<size_t>(row) * N;
+#pragma unroll
+        for (int j = 0; j < CHUNK; j += 8) {
+          if (ncol0 + j < N) {  // N % 8 == 0 on this path
+            const uint4 cv = *reinterpret_cast<const uint4*>(crow + ncol0 + j);
+            const __half2* h = reinterpret_cast<const __half2*>(&cv);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float2 c2 = __half22float2(h[u]);
+              f[j + 2 * u] += ep.beta * c2.x;
+              f[j + 2 * u + 1] += ep.beta * c2.y;
+            }
+          }
+        }
+      }
+    } else if (ep.mode == kEpiI8Tensor) {
+#pragma unroll
+      for (int j = 0; j < CHUNK; ++j) {
+        uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
+        if (ep.za != 0) {
+          const int n = min(ncol0 + j, N - 1);
+          a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+          a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
+               static_cast<uint32_t>(ep.zb);
+        }
+        f[j] = static_cast<float>(static_cast<int32_t>(a)) * ep.scale;
+      }
+    } else {  // kEpiI8RowCol
+#pragma unroll
+      for (int j = 0; j < CHUNK; ++j) {
+        const int n = min(ncol0 + j, N - 1);
+        f[j] = (static_cast<float>(static_cast<int32_t>(v[j])) * row_scale) * ep.col_scale[n];
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < PKTS; ++p)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) pk[p][u] = dev::pack_half2(f[p * 8 + 2 * u], f[p * 8 + 2 * u + 1]);
+  } else {  // int32 raw accumulators
+#pragma unroll
+    for (int j = 0; j < CHUNK; ++j) {
+      uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
+      if (ep.za != 0) {
+        const int n = min(ncol0 + j, N - 1);
+        a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+        a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
+             static_cast<uint32_t>(ep.zb);
+      }
+      pk[j / 4][j % 4] = a;
+    }
+  }
+
+  // Stage through swizzled smem and TMA-store this warp's 32-row slab.
+  uint8_t* stg = stg_base + (stg_count & 1u) * 4096;
+  if (lane == 0) dev::bulk_wait_group_read<1>();
+  __syncwarp();
+  const uint32_t stg_addr = dev::smem_u32(stg);
+#pragma unroll
+  for (int p = 0; p < PKTS; ++p) {
+    const uint32_t off = lane * STG_ROW + swz_chunk(lane, p, STG_ROW) * 16;
+    dev::st_shared_v4(stg_addr + off, pk[p][0], pk[p][1], pk[p][2], pk[p][3]);
+  }
+  dev::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    dev::tma_store_2d(tmC, stg, ncol0, store_row0);
+    dev::bulk_commit_group();
+  }
+  ++stg_count;
+}
+
 template <class Op, int BN, bool SPLIT, int OUT_BYTES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -375,85 +464,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (!do_store) continue;
 
-        // Epilogue math -> 16-byte packets.
-        constexpr int PKTS = S::STG_ROW / 16;
-        uint32_t pk[PKTS][4];
-        const int ncol0 = n0 + c0;
-        if constexpr (OUT_BYTES == 2) {
-          float f[S::CHUNK];
-          if (ep.mode == kEpiF16AlphaBeta) {
-#pragma unroll
-            for (int j = 0; j < S::CHUNK; ++j) f[j] = ep.alpha * __uint_as_float(v[j]);
-            if (ep.beta != 0.f && row < M) {
-              const __half* crow = ep.c_in + static_cast<size_t>(row) * N;
-#pragma unroll
-              for (int j = 0; j < S::CHUNK; j += 8) {
-                if (ncol0 + j < N) {  // N % 8 == 0 on this path
-                  const uint4 cv = *reinterpret_cast<const uint4*>(crow + ncol0 + j);
-                  const __half2* h = reinterpret_cast<const __half2*>(&cv);
-#pragma unroll
-                  for (int u = 0; u < 4; ++u) {
-                    const float2 c2 = __half22float2(h[u]);
-                    f[j + 2 * u] += ep.beta * c2.x;
-                    f[j + 2 * u + 1] += ep.beta * c2.y;
-                  }
-                }
-              }
-            }
-          } else if (ep.mode == kEpiI8Tensor) {
-#pragma unroll
-            for (int j = 0; j < S::CHUNK; ++j) {
-              uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
-              if (ep.za != 0) {
-                const int n = min(ncol0 + j, N - 1);
-                a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
-                a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
-                     static_cast<uint32_t>(ep.zb);
-              }
-              f[j] = static_cast<float>(static_cast<int32_t>(a)) * ep.scale;
-            }
-          } else {  // kEpiI8RowCol
-#pragma unroll
-            for (int j = 0; j < S::CHUNK; ++j) {
-              const int n = min(ncol0 + j, N - 1);
-              f[j] = (static_cast<float>(static_cast<int32_t>(v[j])) * row_scale) * ep.col_scale[n];
-            }
-          }
-#pragma unroll
-          for (int p = 0; p < PKTS; ++p)
-#pragma unroll
-            for (int u = 0; u < 4; ++u) pk[p][u] = dev::pack_half2(f[p * 8 + 2 * u], f[p * 8 + 2 * u + 1]);
-        } else {  // int32 raw accumulators
-#pragma unroll
-          for (int j = 0; j < S::CHUNK; ++j) {
-            uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
-            if (ep.za != 0) {
-              const int n = min(ncol0 + j, N - 1);
-              a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
-              a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
-                   static_cast<uint32_t>(ep.zb);
-            }
-            pk[j / 4][j % 4] = a;
-          }
-        }
-
-        // Stage through swizzled smem and TMA-store this warp's 32-row slab.
-        uint8_t* stg = stg_base + (stg_count & 1u) * 4096;
-        if (lane == 0) dev::bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t stg_addr = dev::smem_u32(stg);
-#pragma unroll
-        for (int p = 0; p < PKTS; ++p) {
-          const uint32_t off = lane * S::STG_ROW + swz_chunk(lane, p, S::STG_ROW) * 16;
-          dev::st_shared_v4(stg_addr + off, pk[p][0], pk[p][1], pk[p][2], pk[p][3]);
-        }
-        dev::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          dev::tma_store_2d(&tmC, stg, ncol0, m0 + static_cast<int>(q) * 32);
-          dev::bulk_commit_group();
-        }
-        ++stg_count;
+        store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
+                                             stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32);
       }
       if constexpr (SPLIT) dev::cluster_sync_all();  // peers may now exit
       if (*abort_flag) break;

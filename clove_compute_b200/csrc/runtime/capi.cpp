@@ -100,7 +100,7 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
   const int bk = 128 / elem;
   const int kb_total = (K + bk - 1) / bk;
   const int tm = (M + 127) / 128;
-  TcPlan best{256, 1};
+  TcPlan best{256, 1, false};
   if (ov.bn != 0) {
     best.bn = ov.bn;
   } else {
@@ -136,6 +136,15 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
     }
   }
   if (best.split > 1 && best.bn > 64) best.bn = 64;
+  // CTA pairs (256 x 256 tiles) when the one-SM plan is 128 x 256 tiles and the
+  // pair tiles fill at least one wave of SM pairs.
+  const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
+  if (ov.path == 4) {
+    best.pair = true;
+  } else if (ov.path == 0 && best.split == 1 && best.bn == 256 && N % 8 == 0 &&
+             pair_tiles * 2 >= num_sms) {
+    best.pair = true;
+  }
   return best;
 }
 
@@ -203,7 +212,7 @@ static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, i
   const bool tc_ok = K % 8 == 0 && N % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C);
   const bool gemv_ok = N <= 8 && K % 8 == 0 && aligned16(A) && gemv_f16_smem(N, K) <= 200 * 1024;
   int path = ov.path;
-  if (path == 1 && !tc_ok) path = 0;
+  if ((path == 1 || path == 4) && !tc_ok) path = 0;
   if (path == 2 && !gemv_ok) path = 0;
   if (path == 0) path = (gemv_ok && N < 16) ? 2 : (tc_ok ? 1 : 3);
   if (path == 2) {
@@ -215,12 +224,13 @@ static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, i
     return launch_simt_f16(A, B, C, 1, M, N, K, alpha, beta, s);
   }
   const TcPlan plan = plan_tc(M, N, K, 2, dev.num_sms);
-  if (chosen) *chosen = plan.split > 1 ? "tc_f16_split" : "tc_f16";
+  if (chosen) *chosen = plan.pair ? "tc2_f16" : plan.split > 1 ? "tc_f16_split" : "tc_f16";
   kern::EpiParams ep{};
   ep.mode = kern::kEpiF16AlphaBeta;
   ep.alpha = alpha;
   ep.beta = beta;
   ep.c_in = static_cast<const __half*>(C);
+  if (plan.pair) return launch_gemm_tc2(kTcF16, A, B, C, M, N, K, ep, dev, s);
   return launch_gemm_tc(kTcF16, plan.bn, plan.split, 2, A, B, C, M, N, K, ep, dev, s);
 }
 
@@ -270,7 +280,7 @@ static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int 
   const bool gemv_ok = K > 0 && N <= 8 && K % 16 == 0 && aligned16(A) &&
                        gemv_int8_smem(N, K) <= 200 * 1024;
   int path = ov.path;
-  if (path == 1 && !tc_ok) path = 0;
+  if ((path == 1 || path == 4) && !tc_ok) path = 0;
   if (path == 2 && !gemv_ok) path = 0;
   if (path == 0) path = gemv_ok ? 2 : (tc_ok ? 1 : 3);
   if (path == 2) {
@@ -290,7 +300,7 @@ static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int 
     return launch_simt_i8(A, B, C, M, N, K, ep, s);
   }
   const TcPlan plan = plan_tc(M, N, K, 1, dev.num_sms);
-  if (chosen) *chosen = plan.split > 1 ? "tc_int8_split" : "tc_int8";
+  if (chosen) *chosen = (plan.pair && out_bytes == 2) ? "tc2_int8" : plan.split > 1 ? "tc_int8_split" : "tc_int8";
   kern::EpiParams ep{};
   ep.mode = mode == 1 ? kern::kEpiI8Tensor : mode == 2 ? kern::kEpiI8RowCol : kern::kEpiI32Raw;
   ep.scale = scale;
@@ -311,7 +321,12 @@ static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int 
     ep.row_sum = sums;
     ep.col_sum = sums + M;
   }
-  if (!rc) rc = launch_gemm_tc(kTcI8, plan.bn, plan.split, out_bytes, A, B, C, M, N, K, ep, dev, s);
+  if (!rc) {
+    if (plan.pair && out_bytes == 2)
+      rc = launch_gemm_tc2(kTcI8, A, B, C, M, N, K, ep, dev, s);
+    else
+      rc = launch_gemm_tc(kTcI8, plan.bn, plan.split, out_bytes, A, B, C, M, N, K, ep, dev, s);
+  }
   if (sums != nullptr) {
     const int rc2 = check_cuda(cudaFreeAsync(sums, s), "cudaFreeAsync(zero-point sums)");
     if (!rc) rc = rc2;
@@ -418,20 +433,22 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
     const bool tc = K % 8 == 0 && N % 8 == 0 && K > 0;
     int path = ov.path ? ov.path : ((gemv && N < 16) ? 2 : (tc ? 1 : 3));
     name = path == 2 ? "gemv_f16" : path == 3 ? "simt_f16" : "tc_f16";
-    if (path == 1) {
+    if (path == 1 || path == 4) {
       const TcPlan p = plan_tc(M, N, K, 2, dev.num_sms);
       bn = p.bn;
       split = p.split;
+      if (p.pair) name = "tc2_f16";
     }
   } else if (dtype == 1) {
     const bool gemv = N <= 8 && K % 16 == 0 && K > 0;
     const bool tc = K % 16 == 0 && N % 16 == 0 && K > 0;
     int path = ov.path ? ov.path : (gemv ? 2 : (tc ? 1 : 3));
     name = path == 2 ? "gemv_int8" : path == 3 ? "simt_int8" : "tc_int8";
-    if (path == 1) {
+    if (path == 1 || path == 4) {
       const TcPlan p = plan_tc(M, N, K, 1, dev.num_sms);
       bn = p.bn;
       split = p.split;
+      if (p.pair) name = "tc2_int8";
     }
   } else {
     const bool gemv = (N <= 8 || M <= 8) && K % 128 == 0;

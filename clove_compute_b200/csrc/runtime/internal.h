@@ -32,7 +32,7 @@ int current_device(DeviceInfo* out);
 
 // Dispatch override for tests (clove_set_dispatch_override).
 struct Override {
-  int path;   // 0 auto, 1 tensor core, 2 gemv, 3 simt
+  int path;   // 0 auto, 1 tensor core (one SM per tile), 2 gemv, 3 simt, 4 CTA-pair tiles
   int bn;     // 0 auto
   int split;  // 0 auto
 };
@@ -49,6 +49,7 @@ bool ws_disabled();
 struct TcPlan {
   int bn;
   int split;
+  bool pair;  // CTA-pair 256 x 256 kernel
 };
 TcPlan plan_tc(int M, int N, int K, int elem, int num_sms);
 
@@ -59,6 +60,9 @@ enum TcOp { kTcF16 = 0, kTcI8 = 1 };
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
                    const DeviceInfo& dev, cudaStream_t stream);
+// CTA-pair kernel: 256 x 256 tiles on two SMs (fp16 C).
+int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
+                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream);
 // True when (op, bn, split, out_bytes) is an instantiated kernel.
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();

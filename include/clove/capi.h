@@ -118,7 +118,8 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
                                void* C, int32_t* G, int M, int N, int K, void* stream);
 
 /* Forces a kernel family for subsequent calls from any thread (tests only).
- * path: 0 = automatic, 1 = tensor-core tiles, 2 = GEMV, 3 = SIMT fallback.
+ * path: 0 = automatic, 1 = tensor-core tiles on one SM, 2 = GEMV, 3 = SIMT
+ * fallback, 4 = tensor-core 256 x 256 tiles on CTA pairs.
  * bn: tensor-core N tile (0 = automatic; 32/64/128/256). split: cluster split-K
  * factor (0 = automatic, 1 = none, 2..8). Returns CLOVE_OK. */
 int clove_set_dispatch_override(int path, int bn, int split);

@@ -54,6 +54,23 @@ def test_tc_cluster_split_k(clove_lib, oracle_mod, cuda, bn, split):
     _run(clove_lib, oracle_mod, 256, 96, 4096, path=1, bn=bn, split=split, seed=split)
 
 
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (1024, 1024, 2048), (384, 520, 200),
+                                   (128, 256, 64), (640, 776, 1000)])
+def test_tc_cta_pair(clove_lib, oracle_mod, cuda, M, N, K):
+    """256 x 256 tiles on CTA pairs (tcgen05 cta_group::2), ragged M / N / K included
+    (M = 128 and 384 leave one CTA of a pair entirely outside A)."""
+    _run(clove_lib, oracle_mod, M, N, K, path=4, seed=M + K)
+
+
+def test_tc_cta_pair_alpha_beta(clove_lib, oracle_mod, cuda):
+    _run(clove_lib, oracle_mod, 768, 512, 256, path=4, alpha=0.5, beta=1.0, seed=2)
+
+
+def test_ffn_shapes_choose_cta_pairs(clove_lib, cuda):
+    assert clove_lib.describe_dispatch("fp16", 11008, 2048, 4096).startswith("tc2_f16")
+    assert clove_lib.describe_dispatch("fp16", 4096, 2048, 11008).startswith("tc2_f16")
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 1024, 1024), (16, 4096, 1024)])
 def test_small_m_decode(clove_lib, oracle_mod, cuda, M, N, K):
     _run(clove_lib, oracle_mod, M, N, K)

@@ -71,3 +71,17 @@ def test_per_tensor_reference_signature(clove_lib, oracle_mod, cuda):
         ref = oracle_mod.gemm_int8(A, B, 0.01, za, 0.02, zb)
         assert rel_fro(C, ref) < 1e-3
     assert clove_lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 272, 512)])
+def test_tc_cta_pair_rowcol(clove_lib, oracle_mod, cuda, M, N, K):
+    """int8 on CTA pairs (kind::i8, cta_group::2): C bit-identical in practice."""
+    A, B, sA, sB = wl.int8_operands(M, N, K, seed=M)
+    clove_lib.set_dispatch_override(4, 0, 0)
+    C = host(clove_lib.gemm_int8_rowcol(dev(A), dev(B), dev(sA), dev(sB)))
+    ref = oracle_mod.gemm_int8_rowcol(A, B, sA, sB)
+    assert rel_fro(C, ref) < 1e-3
+    assert (C.view(np.uint16) != ref.view(np.uint16)).mean() < 1e-3
+    C = host(clove_lib.gemm_int8(dev(A), dev(B), 0.01, 3, 0.02, -4))
+    assert rel_fro(C, oracle_mod.gemm_int8(A, B, 0.01, 3, 0.02, -4)) < 1e-3
+    assert clove_lib.device_error() == 0
