@@ -461,7 +461,7 @@ def run_gpu(args):
     line = None
     if rank == 0:
         ach = FLOP_STEP * args.steps / (t_up + t_dn) / 1e12
-        traffic = _profile_traffic("tc_f16_ffn_up")
+        traffic = _profile_traffic("tc2_f16_ffn_up")
         line = {
             "metric": "GEMM TFLOPS (fp16 FFN prefill, Llama-7B shapes)",
             "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,

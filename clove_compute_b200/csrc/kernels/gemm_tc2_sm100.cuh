@@ -22,6 +22,10 @@
 namespace clove {
 namespace kern {
 
+// Pair tiles are 256 rows tall: bands of 8 keep the band of A that concurrently
+// running pairs share as tall as the one-SM kernel's 16 x 128 rows.
+constexpr int kPairGroupM = 8;
+
 template <class Op>
 struct Tc2Shape {
   static constexpr int BM = 128;        // rows per CTA (256 per pair)
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t stage = 0, phase = 0;
       for (int tile = pair; tile < num_tiles; tile += pairs) {
         int m_blk, n_blk;
-        tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+        tile_coords<kPairGroupM>(tile, tiles_m, tiles_n, m_blk, n_blk);
         const int my_m = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
         const int my_n = n_blk * S::BN + static_cast<int>(rank) * S::BNH;
         bool ok = true;
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(192, 1)
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += pairs, ++it) {
       int m_blk, n_blk;
-      tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+      tile_coords<kPairGroupM>(tile, tiles_m, tiles_n, m_blk, n_blk);
       const uint32_t buf = static_cast<uint32_t>(it) & 1u;
       const uint32_t use = static_cast<uint32_t>(it) >> 1;
       if (!__all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag))) break;

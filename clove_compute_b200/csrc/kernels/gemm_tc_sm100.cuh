@@ -84,11 +84,11 @@ struct TcShape {
   static_assert(!SPLIT || BN <= 64, "split mode keeps the whole tile in registers");
 };
 
-// Grouped rasterisation: bands of 16 M-tiles, N-tiles walked inside a band so
-// that concurrently running CTAs share A rows and B columns in L2.
+// Grouped rasterisation: bands of kGroupM M-tiles, N-tiles walked inside a band
+// so that concurrently running CTAs share A rows and B columns in L2.
+template <int kGroupM = 16>
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& m_blk,
                                             int& n_blk) {
-  constexpr int kGroupM = 16;
   const int per_group = kGroupM * tiles_n;
   const int g = tile / per_group;
   const int first_m = g * kGroupM;
