@@ -14,6 +14,20 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_tc)
 
+}  // namespace rt
+}  // namespace clove
+
+#ifdef CLOVE_TRACE
+// Development builds only: copies the tile kernel's trace slots to the host.
+extern "C" int clove_trace_read_tc(unsigned long long* out, int n) {
+  return static_cast<int>(
+      cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * (n < 64 ? n : 64)));
+}
+#endif
+
+namespace clove {
+namespace rt {
+
 namespace {
 
 using kern::EpiParams;

@@ -215,6 +215,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const uint32_t warp = dev::warp_idx();
   const uint32_t lane = dev::lane_idx();
+  if (threadIdx.x == 0) CLOVE_TRACE_POINT(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -241,6 +242,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   dev::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) CLOVE_TRACE_POINT(1);
 
   const int tiles_m = (M + S::BM - 1) / S::BM;
   const int tiles_n = (N + BN - 1) / BN;
@@ -282,6 +284,7 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           dev::mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          if (kb == kb_begin) CLOVE_TRACE_POINT(2);
           uint8_t* a_dst = stage_base + stage * S::STAGE_BYTES;
           uint8_t* b_dst = a_dst + S::A_BYTES;
           dev::tma_load_2d(a_dst, &tmA, &full[stage], kb * S::BK, m_blk * S::BM);
@@ -325,6 +328,7 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
+          if (kb == kb_begin) CLOVE_TRACE_POINT(3);
           dev::tc_fence_after_sync();
           const uint32_t a_addr = dev::smem_u32(stage_base + stage * S::STAGE_BYTES);
           const uint32_t b_addr = a_addr + S::A_BYTES;
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (!ok) break;
         dev::mma_commit(&tfull[buf]);
+        CLOVE_TRACE_POINT(4);
       }
     }
     __syncwarp();
@@ -379,6 +384,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       dev::tc_fence_after_sync();
+      if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(5);
       const int m0 = m_blk * S::BM;
       const int n0 = n_blk * BN;
       const int row = m0 + row_in_tile;
@@ -409,6 +415,7 @@ __global__ void __launch_bounds__(192, 1)
                               full_row[c + 2], full_row[c + 3]);
         }
         dev::cluster_sync_all();  // partials visible cluster-wide
+        if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(6);
         if (rank == 0) {
           for (uint32_t p = 1; p < gridDim.x; ++p) {
             const uint32_t peer = dev::map_shared_to_rank(dev::smem_u32(my_part), p);
@@ -467,10 +474,12 @@ __global__ void __launch_bounds__(192, 1)
         store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
                                              stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32);
       }
+      if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);
       if constexpr (SPLIT) dev::cluster_sync_all();  // peers may now exit
       if (*abort_flag) break;
     }
     if (lane == 0) dev::bulk_wait_group<0>();
+    if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(8);
     __syncwarp();
   }
 
@@ -488,6 +497,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     dev::tc_fence_after_sync();
     dev::tmem_dealloc(tmem_base, S::TMEM_COLS);
+    if (lane == 0) CLOVE_TRACE_POINT(9);
   }
 }
 

@@ -7,6 +7,22 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_gemv)
 
+}  // namespace rt
+}  // namespace clove
+
+#ifdef CLOVE_TRACE
+// Development builds only: trace slots of the decode kernels.
+extern "C" int clove_trace_read_gemv(unsigned long long* out) {
+  return static_cast<int>(cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * 256));
+}
+extern "C" int clove_trace_write_gemv(const unsigned long long* in) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_clove_trace, in, sizeof(unsigned long long) * 256));
+}
+#endif
+
+namespace clove {
+namespace rt {
+
 namespace {
 
 // Enough CTAs to put every row block in flight at once, at most 8 CTAs per SM.
@@ -50,10 +66,10 @@ int launch_pdl(void (*kernel)(KArgs...), unsigned grid, size_t smem, cudaStream_
   return check_cuda(cudaLaunchKernelEx(&cfg, kernel, args...), what);
 }
 
-template <int NC, int P>
-int gemv_int4_ws(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
-                 const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
-                 long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
+template <int NC, int PW>
+int gemv_int4_ws2(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                  const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
+                  long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
   int grid = dev.num_sms;
   if (rows < grid * 8) grid = (rows + 7) / 8;
   const int per_cta = (rows + grid - 1) / grid;
@@ -62,9 +78,10 @@ int gemv_int4_ws(const uint8_t* Aq, const void* As, const void* Az, const uint8_
   // <= ~100 KB so that the next kernel's CTA fits beside this one (overlap under PDL).
   int slots = (100 * 1024) / (chunk_bytes + 16);
   if (slots > chunks) slots = chunks;
-  if (slots < 2) slots = 2;  // two chunks are consumed per pass
-  const size_t smem = static_cast<size_t>(slots) * (chunk_bytes + 16);
-  auto kernel = kern::gemv_int4_ws_kernel<NC, P>;
+  if (slots < 1) slots = 1;
+  const size_t part_bytes = static_cast<size_t>(per_cta) * kern::kWs2WindowGroups * NC * sizeof(float);
+  const size_t smem = static_cast<size_t>(slots) * (chunk_bytes + 16) + part_bytes;
+  auto kernel = kern::gemv_int4_ws2_kernel<NC, PW>;
   int rc = prepare(kernel, smem);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -72,7 +89,7 @@ int gemv_int4_ws(const uint8_t* Aq, const void* As, const void* Az, const uint8_
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(kern::kWsThreads, 1, 1);
+  cfg.blockDim = dim3(kern::kWs2Threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -83,7 +100,7 @@ int gemv_int4_ws(const uint8_t* Aq, const void* As, const void* Az, const uint8_
                          static_cast<const __half*>(Az), Bq, static_cast<const __half*>(Bs),
                          static_cast<const __half*>(Bz), static_cast<__half*>(C), rows, K, ldc_row,
                          ldc_col, slots, early),
-      "gemv_int4_ws launch");
+      "gemv_int4_ws2 launch");
 }
 
 template <int NC, int P>
@@ -92,11 +109,12 @@ int gemv_int4_reg(const uint8_t* Aq, const void* As, const void* Az, const uint8
                   long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col,
                   const DeviceInfo& dev, cudaStream_t stream) {
   constexpr int R = 2;
+  const int early = weight_prefetch_enabled() ? 1 : 0;
   return launch_pdl(kern::gemv_int4_reg_kernel<NC, P, R>, gemv_grid(rows, dev, R), 0, stream,
                     "gemv_int4_reg launch", Aq, static_cast<const __half*>(As),
                     static_cast<const __half*>(Az), Bq, static_cast<const __half*>(Bs),
                     static_cast<const __half*>(Bz), static_cast<__half*>(C), Gdbg, rows, K,
-                    ldc_row, ldc_col, ldg_row, ldg_col);
+                    ldc_row, ldc_col, ldg_row, ldg_col, early);
 }
 
 template <int NC>
@@ -173,12 +191,12 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (Gdbg == nullptr && K % 1024 == 0 && K <= 24576 && nc * P <= 8 && a16(Aq) && a16(As) &&
       a16(Az) && a16(Bq) && !ws_disabled()) {
-#define WS(n, p)                                                                            \
-  if (nc == n && P == p)                                                                     \
-    return gemv_int4_ws<n, p>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
-    WS(1, 1) WS(1, 2) WS(1, 3) WS(1, 4) WS(1, 5) WS(1, 6) WS(1, 7) WS(1, 8)
-    WS(2, 1) WS(2, 2) WS(2, 3) WS(2, 4)
-#undef WS
+    const int PW = (P + kern::kWs2WindowGroups - 1) / kern::kWs2WindowGroups;
+#define WS2(n, pw)                                                                            \
+  if (nc == n && PW == pw)                                                                     \
+    return gemv_int4_ws2<n, pw>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
+    WS2(1, 1) WS2(1, 2) WS2(2, 1)
+#undef WS2
   }
   if (nc * P <= 8 && (reinterpret_cast<uintptr_t>(Bq) & 15u) == 0) {
 #define REG(n, p)                                                                          \

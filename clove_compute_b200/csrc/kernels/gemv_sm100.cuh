@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(kGemvThreads)
                      const __half* __restrict__ Bs, const __half* __restrict__ Bz,
                      __half* __restrict__ C, int32_t* __restrict__ Gdbg, int rows, int K,
                      long long ldc_row, long long ldc_col, long long ldg_row, long long ldg_col) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   const int NG = K >> 7;          // groups per row
   const int NCH = K >> 5;         // 16-byte chunks per row
   const int KB = K >> 1;          // bytes per row
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kGemvThreads)
                          const __half* __restrict__ Bs, const __half* __restrict__ Bz,
                          __half* __restrict__ C, int32_t* __restrict__ Gdbg, int rows, int K,
                          long long ldc_row, long long ldc_col, long long ldg_row,
-                         long long ldg_col) {
+                         long long ldg_col, int weights_early) {
   dev::allow_dependent_launch();
   const int NG = K >> 7;
   const int NCH = K >> 5;
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kGemvThreads)
   const int gwarp = static_cast<int>(blockIdx.x * (blockDim.x >> 5) + dev::warp_idx());
   const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
 
-  dev::grid_dependency_wait();
+  if (!weights_early) dev::grid_dependency_wait();
 
   uint4 a[R][P];
   __half2 zsa[R][P];
@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(kGemvThreads)
   };
   int row0 = gwarp * R;
   if (row0 < rows) load_rows(row0);
+  // With weights_early the first rows of A were requested before the previous
+  // kernel finished; B, C and Gdbg are touched only after it has.
+  if (weights_early) dev::grid_dependency_wait();
 
   // (b - zB) codes of this lane's chunks: word 2u = even-k codes (high nibbles) of
   // byte quad u, 2u+1 = odd-k codes; chunk sums of (b - zB); B group scales.
@@ -318,39 +321,48 @@ __global__ void __launch_bounds__(kGemvThreads)
   }
 }
 
-// INT4 decode, warp-specialised: one CTA per SM owns a contiguous block of rows.
-// Warp 8 (one thread) moves the block into a shared-memory ring in chunks of 8
-// rows -- three cp.async.bulk copies per chunk (codes, scales, zero points; the
-// rows of a chunk are contiguous in each of the three row-major arrays), so a
-// chunk costs three copy operations rather than three per row -- and issues every
-// chunk that fits in the ring at once. Warps 0-7 take one row of each chunk; each
-// lane holds the (b - zB) codes of its fixed 16-byte chunks in registers (as in
-// gemv_int4_reg_kernel). With weights_early the copies are issued before
-// griddepcontrol.wait, i.e. while the previous kernel on the stream drains (only
-// valid when no in-flight kernel writes A).
-constexpr int kWsConsumerWarps = 8;
-constexpr int kWsThreads = (kWsConsumerWarps + 1) * 32;
-constexpr int kWsChunkRows = kWsConsumerWarps;
+constexpr int kWsChunkRows = 8;  // rows moved per ring slot
 
 // Shared bytes of one chunk: codes [8][K/2], then scales [8][K/128], zeros [8][K/128].
 __host__ __device__ constexpr int gemv_ws_chunk_bytes(int K) {
   return kWsChunkRows * (K / 2 + 4 * (K / 128));
 }
 
-template <int NC, int P>
-__global__ void __launch_bounds__(kWsThreads)
-    gemv_int4_ws_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
-                        const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
-                        const __half* __restrict__ Bs, const __half* __restrict__ Bz,
-                        __half* __restrict__ C, int rows, int K, long long ldc_row,
-                        long long ldc_col, int slots, int weights_early) {
+// INT4 decode, warp-specialised: one CTA per SM owns a contiguous block of rows.
+// The producer warp (one thread) moves the block into a shared-memory ring in
+// chunks of 8 rows -- three cp.async.bulk copies per chunk (codes, scales, zero
+// points; a chunk's rows are contiguous in each of the three row-major arrays) --
+// and issues every chunk that fits in the ring at once. With weights_early the
+// copies are issued before griddepcontrol.wait, i.e. while the previous kernel on
+// the stream drains (only valid when no in-flight kernel writes A). Consumer warp
+// w = 4 * rg + wg reads rows rg and rg + 4 of every chunk and only the
+// 1024-element windows p = wg, wg + 4, ... of each row, so a lane keeps just PW
+// windows of (b - zB) codes in registers (56 registers: two CTAs of consecutive
+// launches fit on one SM) and 16 warps hide shared-memory and shuffle latency. A lane forms the exact int32 partial d - zA * sum(b - zB) of its 32
+// codes and adds float(partial) * sA * sB to the row's fp32 sum; one 5-shuffle
+// butterfly reduces a warp's two rows, the four window partials of a row are
+// added in fixed order (deterministic results) and stored once every chunk is done.
+constexpr int kWs2RowGroups = 4;
+constexpr int kWs2WindowGroups = 4;
+constexpr int kWs2ConsumerWarps = kWs2RowGroups * kWs2WindowGroups;
+constexpr int kWs2Threads = (kWs2ConsumerWarps + 1) * 32;
+static_assert(kWsChunkRows == 2 * kWs2RowGroups, "two rows of a chunk per consumer warp");
+
+template <int NC, int PW>
+__global__ void __launch_bounds__(kWs2Threads, 2)
+    gemv_int4_ws2_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
+                         const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
+                         const __half* __restrict__ Bs, const __half* __restrict__ Bz,
+                         __half* __restrict__ C, int rows, int K, long long ldc_row,
+                         long long ldc_col, int slots, int weights_early) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int NG = K >> 7;
-  const int NCH = K >> 5;
+  const int P = K >> 10;
   const int KB = K >> 1;
   const int chunk_bytes = gemv_ws_chunk_bytes(K);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(slots) * chunk_bytes);
   uint64_t* empty = full + slots;
+  float* part = reinterpret_cast<float*>(empty + slots);  // [rows of this CTA][4][NC]
   __shared__ int abort_s;
   volatile int* abort_flag = &abort_s;
 
@@ -360,19 +372,26 @@ __global__ void __launch_bounds__(kWsThreads)
   const int r0 = blockIdx.x * per_cta;
   const int nrows = max(0, min(rows, r0 + per_cta) - r0);
   const int nchunks = (nrows + kWsChunkRows - 1) / kWsChunkRows;
+#ifdef CLOVE_TRACE
+  __shared__ int trace_k;
+  CLOVE_TRACE_SEQ_BEGIN(trace_k);
+#endif
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < slots; ++i) {
       dev::mbar_init(&full[i], 1);
-      dev::mbar_init(&empty[i], kWsConsumerWarps);
+      dev::mbar_init(&empty[i], kWs2ConsumerWarps);
     }
     abort_s = 0;
     dev::fence_mbarrier_init();
   }
   __syncthreads();
   dev::allow_dependent_launch();
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 0);
+#endif
 
-  if (warp == kWsConsumerWarps) {
+  if (warp == kWs2ConsumerWarps) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       if (!weights_early) dev::grid_dependency_wait();
@@ -390,6 +409,9 @@ __global__ void __launch_bounds__(kWsThreads)
         dev::bulk_load_1d(dst + kWsChunkRows * (KB + 2 * NG), Az + m * NG,
                           static_cast<uint32_t>(cr * 2 * NG), &full[s]);
       }
+#ifdef CLOVE_TRACE
+      CLOVE_TRACE_SEQ_POINT(trace_k, 7);
+#endif
       if (*abort_flag) {  // let copies still in flight land before the CTA exits
         volatile int no_abort = 0;
         for (int c = max(0, nchunks - slots); c < nchunks; ++c)
@@ -402,105 +424,123 @@ __global__ void __launch_bounds__(kWsThreads)
 
   // ------------------------------------------------------------------ consumers
   dev::grid_dependency_wait();  // B and C may belong to the previous kernel
-  uint32_t bw[NC][P][8];
-  int bsum[NC][P];
-  float bsc[NC][P];
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 2);
+#endif
+  const int rg = warp >> 2;
+  const int wg = warp & 3;
+  uint32_t bw[NC][PW][8];
+  int bsum[NC][PW];
+  float bsc[NC][PW];
 #pragma unroll
   for (int n = 0; n < NC; ++n)
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
+    for (int pw = 0; pw < PW; ++pw) {
+      const int p = wg + kWs2WindowGroups * pw;
       const int ch = p * 32 + lane;
       uint4 q = make_uint4(0u, 0u, 0u, 0u);
       int zb = 0;
-      bsc[n][p] = 0.f;
-      if (ch < NCH) {
+      bsc[n][pw] = 0.f;
+      if (p < P) {
         q = *reinterpret_cast<const uint4*>(Bq + static_cast<size_t>(n) * KB + static_cast<size_t>(ch) * 16);
         zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (ch >> 2)]);
-        bsc[n][p] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
+        bsc[n][pw] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
       }
       const uint32_t zq = static_cast<uint32_t>(zb & 0xff) * 0x01010101u;
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
       int sum = 0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        bw[n][p][2 * u] = __vsub4((w[u] >> 4) & 0x0f0f0f0fu, zq);
-        bw[n][p][2 * u + 1] = __vsub4(w[u] & 0x0f0f0f0fu, zq);
-        sum = __dp4a(static_cast<int>(bw[n][p][2 * u]), 0x01010101, sum);
-        sum = __dp4a(static_cast<int>(bw[n][p][2 * u + 1]), 0x01010101, sum);
+        bw[n][pw][2 * u] = __vsub4((w[u] >> 4) & 0x0f0f0f0fu, zq);
+        bw[n][pw][2 * u + 1] = __vsub4(w[u] & 0x0f0f0f0fu, zq);
+        sum = __dp4a(static_cast<int>(bw[n][pw][2 * u]), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(bw[n][pw][2 * u + 1]), 0x01010101, sum);
       }
-      bsum[n][p] = ch < NCH ? sum : 0;
+      bsum[n][pw] = p < P ? sum : 0;
     }
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0 && bsum[0][0] != 0x7fffffff) CLOVE_TRACE_SEQ_POINT(trace_k, 3);
+#endif
 
-  // Two chunks per pass: this warp's rows of both are reduced together (ILP).
-  for (int c0 = 0; c0 < nchunks; c0 += 2) {
-    const int nc2 = min(2, nchunks - c0);
-    bool ok = true;
-    for (int k = 0; k < nc2; ++k) {
-      const int c = c0 + k;
-      ok = ok && dev::mbar_wait(&full[c % slots], static_cast<uint32_t>(c / slots) & 1u, abort_flag);
-    }
+  for (int c = 0; c < nchunks; ++c) {
+    const int s = c % slots;
+    const bool ok = dev::mbar_wait(&full[s], static_cast<uint32_t>(c / slots) & 1u, abort_flag);
     if (!__all_sync(0xffffffffu, ok)) break;
+#ifdef CLOVE_TRACE
+    if (threadIdx.x == 0 && c == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 4);
+#endif
+    const uint8_t* base = smem + static_cast<size_t>(s) * chunk_bytes;
     float acc[2][NC];
-    const uint8_t* rowp[2];
-    const __half* ras[2];
-    const __half* raz[2];
-    bool live[2];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int c = c0 + (k < nc2 ? k : 0);
-      const uint8_t* base = smem + static_cast<size_t>(c % slots) * chunk_bytes;
-      rowp[k] = base + warp * KB;
-      ras[k] = reinterpret_cast<const __half*>(base + kWsChunkRows * KB) + warp * NG;
-      raz[k] = reinterpret_cast<const __half*>(base + kWsChunkRows * (KB + 2 * NG)) + warp * NG;
-      live[k] = k < nc2 && (c0 + k) * kWsChunkRows + warp < nrows;
+    for (int h = 0; h < 2; ++h) {
+      const int rr = rg + kWs2RowGroups * h;
 #pragma unroll
-      for (int n = 0; n < NC; ++n) acc[k][n] = 0.f;
-    }
+      for (int n = 0; n < NC; ++n) acc[h][n] = 0.f;
+      if (c * kWsChunkRows + rr >= nrows) continue;  // warp-uniform: row not loaded
+      const uint8_t* rowp = base + rr * KB;
+      const __half* ras = reinterpret_cast<const __half*>(base + kWsChunkRows * KB) + rr * NG;
+      const __half* raz = reinterpret_cast<const __half*>(base + kWsChunkRows * (KB + 2 * NG)) + rr * NG;
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const int ch = p * 32 + lane;
-      const bool valid = ch < NCH;
-      const int chc = valid ? ch : 0;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const uint4 a = *reinterpret_cast<const uint4*>(rowp[k] + chc * 16);
+      for (int pw = 0; pw < PW; ++pw) {
+        const int p = wg + kWs2WindowGroups * pw;
+        if (p >= P) continue;  // warp-uniform
+        const int ch = p * 32 + lane;
+        const uint4 a = *reinterpret_cast<const uint4*>(rowp + ch * 16);
         const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-        const int za = __half2int_rn(raz[k][chc >> 2]);
-        const float sa = __half2float(ras[k][chc >> 2]);
+        const int za = __half2int_rn(raz[ch >> 2]);
+        const float sa = __half2float(ras[ch >> 2]);
 #pragma unroll
         for (int n = 0; n < NC; ++n) {
-          int d0 = 0, d1 = 0;
+          // High nibbles are used in place (16 x code as unsigned bytes); their
+          // sum is a multiple of 16 and is shifted back exactly.
+          int dh = 0, dl = 0;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            d0 = __dp4a(static_cast<int>((w[u] >> 4) & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u]), d0);
-            d1 = __dp4a(static_cast<int>(w[u] & 0x0f0f0f0fu), static_cast<int>(bw[n][p][2 * u + 1]), d1);
+            dh = dev::dp4a_u8s8(w[u] & 0xf0f0f0f0u, bw[n][pw][2 * u], dh);
+            dl = __dp4a(static_cast<int>(w[u] & 0x0f0f0f0fu), static_cast<int>(bw[n][pw][2 * u + 1]), dl);
           }
-          int g = valid ? d0 + d1 - za * bsum[n][p] : 0;
-          g += __shfl_xor_sync(0xffffffffu, g, 1);
-          g += __shfl_xor_sync(0xffffffffu, g, 2);
-          if ((lane & 3) == 0 && valid) acc[k][n] += static_cast<float>(g) * (sa * bsc[n][p]);
+          const int d = dl + (dh >> 4) - za * bsum[n][pw];
+          acc[h][n] = fmaf(static_cast<float>(d), sa * bsc[n][pw], acc[h][n]);
         }
       }
     }
+    // Butterfly over the warp's two rows: lanes 0-15 end with row rg, 16-31 with rg + 4.
+    const bool upper = (lane & 16) != 0;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int n = 0; n < NC; ++n) {
+      const float send = upper ? acc[0][n] : acc[1][n];
+      float keep = upper ? acc[1][n] : acc[0][n];
+      keep += __shfl_xor_sync(0xffffffffu, send, 16);
 #pragma unroll
-      for (int n = 0; n < NC; ++n) {
-        const float t = warp_sum_f32(acc[k][n]);
-        const int m = r0 + (c0 + k) * kWsChunkRows + warp;
-        if (lane == 0 && live[k]) C[m * ldc_row + n * ldc_col] = __float2half_rn(t);
-      }
+      for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+      const int row_local = c * kWsChunkRows + rg + (upper ? kWs2RowGroups : 0);
+      if ((lane & 15) == 0 && row_local < nrows) part[(row_local * kWs2WindowGroups + wg) * NC + n] = keep;
     }
     __syncwarp();
-    if (lane == 0)
-      for (int k = 0; k < nc2; ++k)
-        if (c0 + k + slots < nchunks) dev::mbar_arrive(&empty[(c0 + k) % slots]);
+    if (lane == 0 && c + slots < nchunks) dev::mbar_arrive(&empty[s]);
   }
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 9);
+#endif
+
+  // Every consumer warp has written its partials: add the four windows of each row.
+  asm volatile("bar.sync 1, %0;" ::"n"(kWs2ConsumerWarps * 32) : "memory");
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 11);
+#endif
+  if (*abort_flag) return;
+  for (int i = static_cast<int>(threadIdx.x); i < nrows * NC; i += kWs2ConsumerWarps * 32) {
+    const int r = i / NC;
+    const int n = i - r * NC;
+    const float* pr = part + r * kWs2WindowGroups * NC + n;
+    const float t = ((pr[0] + pr[NC]) + pr[2 * NC]) + pr[3 * NC];
+    C[static_cast<long long>(r0 + r) * ldc_row + n * ldc_col] = __float2half_rn(t);
+  }
+#ifdef CLOVE_TRACE
+  if (threadIdx.x == 0) CLOVE_TRACE_SEQ_POINT(trace_k, 6);
+#endif
 }
 
-// ---------------------------------------------------------------------------
-// INT8: A int8 [rows, K] streamed, B int8 [K, NC] row-major (reference layout).
-// ---------------------------------------------------------------------------
 __host__ __device__ constexpr size_t gemv_int8_smem_bytes(int nc, int K) {
   return static_cast<size_t>(nc) * K + 4 * 8;
 }
@@ -509,7 +549,7 @@ template <int NC>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_int8_kernel(const int8_t* __restrict__ A, const int8_t* __restrict__ B,
                      void* __restrict__ Cout, int rows, int K, GemvI8Epi ep) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   int8_t* bt = reinterpret_cast<int8_t*>(smem);                            // [NC][K]
   int* colsum = reinterpret_cast<int*>(smem + static_cast<size_t>(NC) * K);  // [NC]
   for (int idx = threadIdx.x; idx < NC * K; idx += blockDim.x) {
@@ -618,7 +658,7 @@ template <int NC>
 __global__ void __launch_bounds__(kGemvThreads)
     gemv_f16_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
                     __half* __restrict__ C, int rows, int K, float alpha, float beta) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   __half* bt = reinterpret_cast<__half*>(smem);  // [NC][K]
   for (int idx = threadIdx.x; idx < NC * K; idx += blockDim.x) {
     const int n = idx / K;

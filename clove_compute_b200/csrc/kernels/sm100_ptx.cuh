@@ -426,6 +426,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// dot product of four unsigned bytes of a with four signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_u8s8(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -433,6 +440,60 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 }  // namespace dev
 }  // namespace clove
+
+// Timeline tracing for kernel development: with -DCLOVE_TRACE, CLOVE_TRACE_POINT(i)
+// stores %globaltimer into slot i of a per-TU device array when executed by the
+// first CTA; without it the macro expands to nothing (the product build).
+#ifdef CLOVE_TRACE
+static __device__ unsigned long long g_clove_trace[256];
+#define CLOVE_TRACE_POINT(i)                                                      \
+  do {                                                                            \
+    if (blockIdx.x == 0 && blockIdx.y == 0) g_clove_trace[(i)] = clove::dev::globaltimer_ns(); \
+  } while (0)
+// Earliest / latest time any CTA reaches a point (slots reset by the host).
+#define CLOVE_TRACE_MIN(i) atomicMin(&g_clove_trace[(i)], clove::dev::globaltimer_ns())
+#define CLOVE_TRACE_MAX(i) atomicMax(&g_clove_trace[(i)], clove::dev::globaltimer_ns())
+// Start time of each launch, in launch order: slots 32..63, counter in slot 31.
+#define CLOVE_TRACE_SEQ()                                                         \
+  do {                                                                            \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {                                    \
+      const unsigned long long k_ = atomicAdd(&g_clove_trace[31], 1ull);          \
+      g_clove_trace[32 + (k_ & 31)] = clove::dev::globaltimer_ns();               \
+    }                                                                             \
+  } while (0)
+// Per-launch timelines of the first CTA: launch k (in start order, counter in
+// slot 63) writes point j to slot 64 + 16 * (k % 12) + j.
+#define CLOVE_TRACE_SEQ_BEGIN(shared_k)                                           \
+  do {                                                                            \
+    if (threadIdx.x == 0)                                                         \
+      shared_k = blockIdx.x == 0                                                  \
+                     ? static_cast<int>(atomicAdd(&g_clove_trace[63], 1ull) % 12ull) \
+                     : 0;                                                         \
+  } while (0)
+#define CLOVE_TRACE_SEQ_POINT(shared_k, j)                                        \
+  do {                                                                            \
+    if (blockIdx.x == 0) g_clove_trace[64 + 16 * (shared_k) + (j)] = clove::dev::globaltimer_ns(); \
+  } while (0)
+#else
+#define CLOVE_TRACE_SEQ_BEGIN(shared_k) \
+  do {                                  \
+  } while (0)
+#define CLOVE_TRACE_SEQ_POINT(shared_k, j) \
+  do {                                     \
+  } while (0)
+#define CLOVE_TRACE_POINT(i) \
+  do {                       \
+  } while (0)
+#define CLOVE_TRACE_MIN(i) \
+  do {                     \
+  } while (0)
+#define CLOVE_TRACE_MAX(i) \
+  do {                     \
+  } while (0)
+#define CLOVE_TRACE_SEQ() \
+  do {                    \
+  } while (0)
+#endif
 
 // Host side: read and clear this translation unit's device error word.
 #define CLOVE_DEFINE_ERROR_READER(fn_name)                                        \
