@@ -21,7 +21,10 @@ CLOVE_DEFINE_ERROR_READER(read_clear_error_tc)
 // Development builds only: copies the tile kernel's trace slots to the host.
 extern "C" int clove_trace_read_tc(unsigned long long* out, int n) {
   return static_cast<int>(
-      cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * (n < 64 ? n : 64)));
+      cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * (n < 256 ? n : 256)));
+}
+extern "C" int clove_trace_write_tc(const unsigned long long* in) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_clove_trace, in, sizeof(unsigned long long) * 256));
 }
 #endif
 
@@ -50,7 +53,7 @@ TcEntry make_entry(int op) {
   TcEntry e;
   e.op = op;
   e.bn = BN;
-  e.split = SPLIT ? 2 : 1;  // "split" entries serve every cluster size 2..8
+  e.split = SPLIT ? 2 : 1;  // "split" entries serve cluster sizes 2, 4 and 8
   e.out_bytes = OUT;
   e.fn = reinterpret_cast<const void*>(&kern::gemm_tc_kernel<Op, BN, SPLIT, OUT>);
   e.smem_bytes = S::SMEM_BYTES;
@@ -78,16 +81,19 @@ struct Table {
     add<OpF16, 256, false, 2>(kTcF16);
     add<OpF16, 32, true, 2>(kTcF16);
     add<OpF16, 64, true, 2>(kTcF16);
+    add<OpF16, 128, true, 2>(kTcF16);
     add<OpI8, 64, false, 2>(kTcI8);
     add<OpI8, 128, false, 2>(kTcI8);
     add<OpI8, 256, false, 2>(kTcI8);
     add<OpI8, 32, true, 2>(kTcI8);
     add<OpI8, 64, true, 2>(kTcI8);
+    add<OpI8, 128, true, 2>(kTcI8);
     add<OpI8, 64, false, 4>(kTcI8);
     add<OpI8, 128, false, 4>(kTcI8);
     add<OpI8, 256, false, 4>(kTcI8);
     add<OpI8, 32, true, 4>(kTcI8);
     add<OpI8, 64, true, 4>(kTcI8);
+    add<OpI8, 128, true, 4>(kTcI8);
   }
 };
 
@@ -109,7 +115,8 @@ int find_entry(int op, int bn, int split, int out_bytes) {
 }  // namespace
 
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes) {
-  if (split < 1 || split > 8) return false;
+  // A split tile's 128 rows are dealt out evenly over the cluster.
+  if (split != 1 && split != 2 && split != 4 && split != 8) return false;
   return find_entry(op, bn, split, out_bytes) >= 0;
 }
 
@@ -153,6 +160,7 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
 
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   EpiParams epv = ep;
+  epv.c_out = C;
   void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

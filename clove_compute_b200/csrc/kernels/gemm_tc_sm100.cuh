@@ -60,17 +60,22 @@ struct TcShape {
   static constexpr int CHUNK = BN < (128 / OUT_BYTES) ? BN : (128 / OUT_BYTES);  // cols / store
   static constexpr int STG_ROW = CHUNK * OUT_BYTES;                             // bytes / row
   static constexpr int STG_BUF = 32 * STG_ROW;
-  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x 4 KB (1 KB aligned)
+  // C staging: 4 warps x 2 buffers x 4 KB (1 KB aligned); split-K tiles store rows directly.
+  static constexpr int EPI_BYTES = SPLIT ? 0 : 4 * 2 * 4096;
+  // Split-K receive buffer: (S-1) * BM/S <= 112 partial rows (S <= 8), padded rows.
   static constexpr int PART_ROW = BN * 4 + 16;
-  static constexpr int PART_BYTES = SPLIT ? ((BM * PART_ROW + 1023) / 1024) * 1024 : 0;
+  static constexpr int PART_BYTES = SPLIT ? ((112 * PART_ROW + 1023) / 1024) * 1024 : 0;
+  // Split-K: the tile's column factors (col_scale or col_sum), staged before the
+  // accumulators are ready.
+  static constexpr int COLV_BYTES = SPLIT ? BN * 4 : 0;
   static constexpr int ACC_BUFS = SPLIT ? 1 : 2;
   static constexpr int TMEM_COLS = (ACC_BUFS * BN) < 32 ? 32 : (ACC_BUFS * BN);
   static constexpr int BAR_BYTES = 256;
   static constexpr int STAGES_FIT =
-      (kSmemLimit - 1024 - EPI_BYTES - PART_BYTES - BAR_BYTES) / STAGE_BYTES;
+      (kSmemLimit - 1024 - EPI_BYTES - PART_BYTES - COLV_BYTES - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + EPI_BYTES + PART_BYTES + BAR_BYTES;
+      1024 + STAGES * STAGE_BYTES + EPI_BYTES + PART_BYTES + COLV_BYTES + BAR_BYTES;
   static constexpr int THREADS = 192;
 
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N constraint for M=128");
@@ -81,7 +86,7 @@ struct TcShape {
   static_assert(STAGES >= 2, "pipeline depth");
   static_assert(SMEM_BYTES <= kSmemLimit, "smem budget");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS <= 512, "TMEM alloc size");
-  static_assert(!SPLIT || BN <= 64, "split mode keeps the whole tile in registers");
+  static_assert(!SPLIT || BN <= 128, "split-K receive buffers hold at most 128 columns");
 };
 
 // Grouped rasterisation: bands of kGroupM M-tiles, N-tiles walked inside a band
@@ -105,18 +110,16 @@ __device__ __forceinline__ uint32_t swz_chunk(uint32_t row, uint32_t chunk, uint
   return chunk ^ (((row * row_bytes) >> 7) & mask);
 }
 
-// Epilogue of one CHUNK-column slice of a 32-row warp slab: fp16 (or raw int32)
-// math on this thread's row, swizzled staging, TMA store of the warp's slab.
-template <class Op, int OUT_BYTES, int CHUNK>
-__device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const EpiParams& ep,
-                                            int row, int ncol0, int M, int N, int K,
-                                            float row_scale, int32_t row_corr, uint32_t lane,
-                                            uint8_t* stg_base, uint32_t& stg_count,
-                                            const CUtensorMap* tmC, int store_row0) {
-  // Epilogue math -> 16-byte packets.
-  constexpr int STG_ROW = CHUNK * OUT_BYTES;
-  constexpr int PKTS = STG_ROW / 16;
-  uint32_t pk[PKTS][4];
+// Epilogue math of one CHUNK-column slice of this thread's row: fp16 (or raw
+// int32) values packed into 16-byte packets. Column factors (col_scale / col_sum)
+// come from global memory, or with COLV from `colv` (shared, indexed by j).
+template <class Op, int OUT_BYTES, int CHUNK, bool COLV = false>
+__device__ __forceinline__ void epi_pack(const uint32_t (&v)[CHUNK], const EpiParams& ep, int row,
+                                         int ncol0, int M, int N, int K, float row_scale,
+                                         int32_t row_corr,
+                                         uint32_t (&pk)[CHUNK * OUT_BYTES / 16][4],
+                                         const uint32_t* colv = nullptr) {
+  constexpr int PKTS = CHUNK * OUT_BYTES / 16;
   if constexpr (OUT_BYTES == 2) {
     float f[CHUNK];
     if (ep.mode == kEpiF16AlphaBeta) {
@@ -143,8 +146,9 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
       for (int j = 0; j < CHUNK; ++j) {
         uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
         if (ep.za != 0) {
-          const int n = min(ncol0 + j, N - 1);
-          a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+          const uint32_t cs =
+              COLV ? colv[j] : static_cast<uint32_t>(ep.col_sum[min(ncol0 + j, N - 1)]);
+          a += 0u - static_cast<uint32_t>(ep.za) * cs;
           a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
                static_cast<uint32_t>(ep.zb);
         }
@@ -153,8 +157,8 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
     } else {  // kEpiI8RowCol
 #pragma unroll
       for (int j = 0; j < CHUNK; ++j) {
-        const int n = min(ncol0 + j, N - 1);
-        f[j] = (static_cast<float>(static_cast<int32_t>(v[j])) * row_scale) * ep.col_scale[n];
+        const float cs = COLV ? __uint_as_float(colv[j]) : ep.col_scale[min(ncol0 + j, N - 1)];
+        f[j] = (static_cast<float>(static_cast<int32_t>(v[j])) * row_scale) * cs;
       }
     }
 #pragma unroll
@@ -166,14 +170,29 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
     for (int j = 0; j < CHUNK; ++j) {
       uint32_t a = v[j] + static_cast<uint32_t>(row_corr);
       if (ep.za != 0) {
-        const int n = min(ncol0 + j, N - 1);
-        a += 0u - static_cast<uint32_t>(ep.za) * static_cast<uint32_t>(ep.col_sum[n]);
+        const uint32_t cs =
+            COLV ? colv[j] : static_cast<uint32_t>(ep.col_sum[min(ncol0 + j, N - 1)]);
+        a += 0u - static_cast<uint32_t>(ep.za) * cs;
         a += static_cast<uint32_t>(K) * static_cast<uint32_t>(ep.za) *
              static_cast<uint32_t>(ep.zb);
       }
       pk[j / 4][j % 4] = a;
     }
   }
+}
+
+// Epilogue of one CHUNK-column slice of a 32-row warp slab: epi_pack on this
+// thread's row, swizzled staging, TMA store of the warp's slab.
+template <class Op, int OUT_BYTES, int CHUNK>
+__device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const EpiParams& ep,
+                                            int row, int ncol0, int M, int N, int K,
+                                            float row_scale, int32_t row_corr, uint32_t lane,
+                                            uint8_t* stg_base, uint32_t& stg_count,
+                                            const CUtensorMap* tmC, int store_row0) {
+  constexpr int STG_ROW = CHUNK * OUT_BYTES;
+  constexpr int PKTS = STG_ROW / 16;
+  uint32_t pk[PKTS][4];
+  epi_pack<Op, OUT_BYTES, CHUNK>(v, ep, row, ncol0, M, N, K, row_scale, row_corr, pk);
 
   // Stage through swizzled smem and TMA-store this warp's 32-row slab.
   uint8_t* stg = stg_base + (stg_count & 1u) * 4096;
@@ -194,6 +213,27 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
   ++stg_count;
 }
 
+// Epilogue of one CHUNK-column slice of this thread's row, stored straight to C
+// with 16-byte stores (split-K tiles, whose rows are finished by different CTAs).
+template <class Op, int OUT_BYTES, int CHUNK>
+__device__ __forceinline__ void store_row_direct(const uint32_t (&v)[CHUNK], const EpiParams& ep,
+                                                 int row, int ncol0, int M, int N, int K,
+                                                 float row_scale, int32_t row_corr,
+                                                 const uint32_t* colv) {
+  constexpr int PKTS = CHUNK * OUT_BYTES / 16;
+  constexpr int COLS_PER_PKT = 16 / OUT_BYTES;
+  uint32_t pk[PKTS][4];
+  epi_pack<Op, OUT_BYTES, CHUNK, true>(v, ep, row, ncol0, M, N, K, row_scale, row_corr, pk, colv);
+  if (row >= M) return;
+  uint8_t* crow = static_cast<uint8_t*>(ep.c_out) +
+                  (static_cast<size_t>(row) * N + ncol0) * OUT_BYTES;
+#pragma unroll
+  for (int p = 0; p < PKTS; ++p) {
+    if (ncol0 + p * COLS_PER_PKT < N)  // N is a multiple of 8 on this path
+      *reinterpret_cast<uint4*>(crow + p * 16) = make_uint4(pk[p][0], pk[p][1], pk[p][2], pk[p][3]);
+  }
+}
+
 template <class Op, int BN, bool SPLIT, int OUT_BYTES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -205,17 +245,23 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* stage_base = smem;
   uint8_t* epi_base = smem + S::STAGES * S::STAGE_BYTES;
   uint8_t* part_base = epi_base + S::EPI_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(part_base + S::PART_BYTES);
+  uint32_t* colv = reinterpret_cast<uint32_t*>(part_base + S::PART_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(part_base + S::PART_BYTES + S::COLV_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + S::STAGES;
   uint64_t* tfull = bars + 2 * S::STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // split-K: peers' partial rows have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = dev::warp_idx();
   const uint32_t lane = dev::lane_idx();
-  if (threadIdx.x == 0) CLOVE_TRACE_POINT(0);
+  if (threadIdx.x == 0) {
+    CLOVE_TRACE_POINT(0);
+    CLOVE_TRACE_MIN(16);
+    CLOVE_TRACE_MAX(17);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -227,6 +273,13 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_init(&tempty[b], 4);
     }
     *abort_flag = 0;
+    if constexpr (SPLIT) {
+      // This CTA finishes rows [rank*BM/S, (rank+1)*BM/S) of the tile and receives
+      // those rows' partials from the other S-1 CTAs of the cluster.
+      const uint32_t parts = gridDim.x;
+      dev::mbar_init(rbar, 1);
+      dev::mbar_arrive_expect_tx(rbar, (parts - 1) * (S::BM / parts) * BN * 4);
+    }
     dev::fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -242,6 +295,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   dev::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  if constexpr (SPLIT) dev::cluster_arrive();  // receive barriers initialised
   if (threadIdx.x == 0) CLOVE_TRACE_POINT(1);
 
   const int tiles_m = (M + S::BM - 1) / S::BM;
@@ -354,6 +408,8 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
         dev::mma_commit(&tfull[buf]);
         CLOVE_TRACE_POINT(4);
+        CLOVE_TRACE_MAX(18);
+        CLOVE_TRACE_MIN(22);
       }
     }
     __syncwarp();
@@ -364,6 +420,7 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* stg_base = epi_base + (warp - 2) * (2 * 4096);
     uint32_t stg_count = 0;
     int it = 0;
+    if constexpr (SPLIT) dev::cluster_wait();  // every peer's rbar is initialised
     for (int tile = tile_first; tile < num_tiles; tile += tile_stride, ++it) {
       int m_blk, n_blk;
       if constexpr (SPLIT) {
@@ -374,6 +431,19 @@ __global__ void __launch_bounds__(192, 1)
       }
       const uint32_t buf = static_cast<uint32_t>(it) & (S::ACC_BUFS - 1);
       const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
+      if constexpr (SPLIT) {
+        // Stage the tile's column factors while the MMAs run (one tile per CTA in
+        // split mode, and these warps never leave the tile early, so the named
+        // barrier is always reached by all four).
+        const bool rowcol = ep.mode == kEpiI8RowCol;
+        if (rowcol || ((ep.mode == kEpiI8Tensor || ep.mode == kEpiI32Raw) && ep.za != 0)) {
+          for (int j = static_cast<int>(threadIdx.x) - 64; j < BN; j += 128) {
+            const int n = min(n_blk * BN + j, N - 1);
+            colv[j] = rowcol ? __float_as_uint(ep.col_scale[n]) : static_cast<uint32_t>(ep.col_sum[n]);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+      }
       bool have_acc = kb_end > kb_begin;
       if (have_acc) {
         const bool got = __all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag));
@@ -390,55 +460,6 @@ __global__ void __launch_bounds__(192, 1)
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + buf * BN;
 
-      // Split mode: gather the whole BN-wide row, reduce over the cluster.
-      uint32_t full_row[SPLIT ? BN : 1];
-      if constexpr (SPLIT) {
-#pragma unroll
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t v[16];
-          if (have_acc) {
-            dev::tmem_ld_x16(t_row + c, v);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0u;
-          }
-          dev::tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) full_row[c + j] = v[j];
-        }
-        const uint32_t rank = dev::cluster_ctarank();
-        uint8_t* my_part = part_base + row_in_tile * S::PART_ROW;
-        if (rank != 0) {
-#pragma unroll
-          for (int c = 0; c < BN; c += 4)
-            dev::st_shared_v4(dev::smem_u32(my_part + c * 4), full_row[c], full_row[c + 1],
-                              full_row[c + 2], full_row[c + 3]);
-        }
-        dev::cluster_sync_all();  // partials visible cluster-wide
-        if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(6);
-        if (rank == 0) {
-          for (uint32_t p = 1; p < gridDim.x; ++p) {
-            const uint32_t peer = dev::map_shared_to_rank(dev::smem_u32(my_part), p);
-#pragma unroll
-            for (int c = 0; c < BN; c += 4) {
-              const uint4 v = dev::ld_dsmem_v4(peer + c * 4);
-              if constexpr (Op::kInt) {
-                full_row[c + 0] += v.x;
-                full_row[c + 1] += v.y;
-                full_row[c + 2] += v.z;
-                full_row[c + 3] += v.w;
-              } else {
-                full_row[c + 0] = __float_as_uint(__uint_as_float(full_row[c + 0]) + __uint_as_float(v.x));
-                full_row[c + 1] = __float_as_uint(__uint_as_float(full_row[c + 1]) + __uint_as_float(v.y));
-                full_row[c + 2] = __float_as_uint(__uint_as_float(full_row[c + 2]) + __uint_as_float(v.z));
-                full_row[c + 3] = __float_as_uint(__uint_as_float(full_row[c + 3]) + __uint_as_float(v.w));
-              }
-            }
-          }
-        }
-      }
-      const bool do_store = !SPLIT || dev::cluster_ctarank() == 0;
-
       // Per-row epilogue constants.
       float row_scale = 0.f;
       int32_t row_corr = 0;
@@ -447,13 +468,98 @@ __global__ void __launch_bounds__(192, 1)
         row_corr = static_cast<int32_t>(0u - static_cast<uint32_t>(ep.zb) *
                                                  static_cast<uint32_t>(ep.row_sum[row]));
 
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += S::CHUNK) {
-        uint32_t v[S::CHUNK];
-        if constexpr (SPLIT) {
+      if constexpr (SPLIT) {
+        // Reduce-scatter over the cluster: the rows of the tile are dealt out in S
+        // equal slices (with S = 8 a warp's rows span two slices). Every CTA first
+        // pushes its partials of the other slices into their owners' shared memory
+        // (st.async, counted on the owner's rbar), then finishes its own slice:
+        // own partial first, then the S-1 received ones by rank. TMEM loads are
+        // warp-collective, so they sit in warp-uniform loops; only the pushes, the
+        // wait on rbar and the stores depend on the lane's slice. No CTA waits
+        // before it has pushed, so the exchange cannot deadlock.
+        const int parts = static_cast<int>(gridDim.x);
+        const int rank = static_cast<int>(dev::cluster_ctarank());
+        const int rs = S::BM / parts;
+        const int owner = row_in_tile / rs;
+        const int srow = row_in_tile - owner * rs;
+        const bool mine = owner == rank;
+        const int slot = mine ? 0 : (rank < owner ? rank : rank - 1);
+        const uint32_t dst = dev::map_shared_to_rank(
+            dev::smem_u32(part_base + (slot * rs + srow) * S::PART_ROW), static_cast<uint32_t>(owner));
+        const uint32_t rb = dev::map_shared_to_rank(dev::smem_u32(rbar), static_cast<uint32_t>(owner));
 #pragma unroll
-          for (int j = 0; j < S::CHUNK; ++j) v[j] = full_row[(c0 + j) % BN];
-        } else {
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          __syncwarp();  // reconverge after the previous pushes
+          if (have_acc) {
+            dev::tmem_ld_x16(t_row + c, v);
+            dev::tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0u;
+          }
+          if (!mine) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              dev::st_async_v4(dst + (c + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3], rb);
+          }
+        }
+        bool got = true;
+        if (mine) {
+          got = dev::mbar_wait<true>(rbar, 0u, abort_flag);
+          if (!got) {
+            // Error path: give late pushes a second bounded window to land before
+            // this CTA (and its shared memory) can exit.
+            volatile int no_abort = 0;
+            dev::mbar_wait<true>(rbar, 0u, &no_abort);
+          }
+        }
+        if (mine && srow == 0) CLOVE_TRACE_MAX(19);
+        __syncwarp();
+        if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(6);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += S::CHUNK) {
+          uint32_t v[S::CHUNK];
+          __syncwarp();  // reconverge after the previous slice's stores
+#pragma unroll
+          for (int j = 0; j < S::CHUNK; j += 16) {
+            uint32_t t[16];
+            if (have_acc) {
+              dev::tmem_ld_x16(t_row + c0 + j, t);
+              dev::tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int u = 0; u < 16; ++u) t[u] = 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+          }
+          if (!mine) continue;
+          for (int p = 0; p < parts - 1 && got; ++p) {
+            const uint8_t* src = part_base + (p * rs + srow) * S::PART_ROW + c0 * 4;
+#pragma unroll
+            for (int j = 0; j < S::CHUNK; j += 4) {
+              const uint4 r = *reinterpret_cast<const uint4*>(src + j * 4);
+              if constexpr (Op::kInt) {
+                v[j + 0] += r.x;
+                v[j + 1] += r.y;
+                v[j + 2] += r.z;
+                v[j + 3] += r.w;
+              } else {
+                v[j + 0] = __float_as_uint(__uint_as_float(v[j + 0]) + __uint_as_float(r.x));
+                v[j + 1] = __float_as_uint(__uint_as_float(v[j + 1]) + __uint_as_float(r.y));
+                v[j + 2] = __float_as_uint(__uint_as_float(v[j + 2]) + __uint_as_float(r.z));
+                v[j + 3] = __float_as_uint(__uint_as_float(v[j + 3]) + __uint_as_float(r.w));
+              }
+            }
+          }
+          store_row_direct<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale,
+                                                    row_corr, colv + c0);
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += S::CHUNK) {
+          uint32_t v[S::CHUNK];
 #pragma unroll
           for (int j = 0; j < S::CHUNK; j += 16) {
             uint32_t t[16];
@@ -468,28 +574,26 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&tempty[buf]);
           }
+          store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr,
+                                               lane, stg_base, stg_count, &tmC,
+                                               m0 + static_cast<int>(q) * 32);
         }
-        if (!do_store) continue;
-
-        store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
-                                             stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32);
       }
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);
-      if constexpr (SPLIT) dev::cluster_sync_all();  // peers may now exit
       if (*abort_flag) break;
     }
     if (lane == 0) dev::bulk_wait_group<0>();
     if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(8);
+    if (lane == 0) CLOVE_TRACE_MAX(20);
     __syncwarp();
   }
 
   if constexpr (SPLIT) {
-    // Warps 0/1 (and epilogue warps that broke out early) must match the epilogue's
-    // two cluster barriers per tile; in split mode every CTA owns exactly one tile.
-    if (warp < 2) {
-      dev::cluster_sync_all();
-      dev::cluster_sync_all();
-    }
+    // Warps 0/1 complete the start-up phase here (the epilogue warps did before
+    // pushing). No final cluster barrier: a CTA only exits after every push into
+    // its shared memory has landed (its rbar completed), and nothing reads another
+    // CTA's shared memory.
+    if (warp < 2) dev::cluster_wait();
   }
 
   dev::tc_fence_before_sync();
@@ -498,6 +602,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::tc_fence_after_sync();
     dev::tmem_dealloc(tmem_base, S::TMEM_COLS);
     if (lane == 0) CLOVE_TRACE_POINT(9);
+    if (lane == 0) CLOVE_TRACE_MAX(21);
   }
 }
 

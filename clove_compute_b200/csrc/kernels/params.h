@@ -25,6 +25,7 @@ struct EpiParams {
   int za, zb;               // int8 zero points
   const int32_t* row_sum;   // sum_k A[m,k]   (required when zb != 0)
   const int32_t* col_sum;   // sum_k B[k,n]   (required when za != 0)
+  void* c_out;              // C itself (split-K tiles store rows directly)
 };
 
 // Epilogue of the int8 GEMV (modes as EpiMode 1..3).

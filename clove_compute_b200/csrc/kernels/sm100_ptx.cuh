@@ -378,20 +378,32 @@ __device__ __forceinline__ void cluster_sync_all() {
           : "memory");
 }
 
+// Split cluster barrier: arrive (release) early, wait (acquire) when needed. Every
+// thread of every CTA in the cluster takes part in each phase.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16-byte store into another CTA's shared memory (address from mapa); its bytes
+// complete a transaction on that CTA's mbarrier `remote_bar` (also mapa'd).
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t a, uint32_t b,
+                                            uint32_t c, uint32_t d, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          remote_addr),
+      "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t map_shared_to_rank(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
 
-__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 
 // ----------------------------------------------------------------------------
 // Programmatic dependent launch. A kernel launched with the programmatic

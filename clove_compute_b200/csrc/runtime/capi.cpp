@@ -130,7 +130,9 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
       long long s = num_sms / std::max<long long>(tiles, 1);
       s = std::min<long long>(s, 8);
       s = std::min<long long>(s, kb_total / 2);
-      best.split = static_cast<int>(std::max<long long>(s, 1));
+      long long p2 = 1;  // cluster sizes 2, 4, 8 (a tile's rows split evenly)
+      while (p2 * 2 <= s) p2 *= 2;
+      best.split = static_cast<int>(p2);
     } else {
       best.split = 1;
     }
