@@ -261,6 +261,19 @@ def _secondary(cc, torch, peaks):
     t_pf = timeit(lambda i: cc.gemm_int4(Aq[i], As[i], Az[i], Bq, Bs, Bz, C), copies, 400)
     cc.set_weight_prefetch(False)
     nbytes = M * K // 2 + 2 * 2 * M * K // 128 + N * K // 2 + 2 * 2 * N * K // 128 + 2 * M * N
+    del Aq, As, Az
+
+    def read_floor(nb, n_copies):
+        """Seconds per launch of a bare read of nb bytes (nothing computed), same
+        rotation: what one kernel of this size can pull from HBM on this GPU."""
+        bufs = [torch.empty(nb // 16 * 16, dtype=torch.uint8, device="cuda").fill_(1)
+                for _ in range(n_copies)]
+        sink = torch.zeros(4, dtype=torch.int32, device="cuda")
+        tf = timeit(lambda i: cc.debug_stream_read(bufs[i], sink), n_copies, 400)
+        del bufs
+        return tf
+
+    t_floor = read_floor(nbytes, copies)
     out["int4_decode_4096x1x4096"] = {
         "kernel": cc.describe_dispatch("int4", M, N, K), "us_per_call": round(t * 1e6, 3),
         "GBps": round(nbytes / t / 1e9, 1), "bytes_per_call": nbytes,
@@ -272,8 +285,12 @@ def _secondary(cc, torch, peaks):
             "us_per_call": round(t_pf * 1e6, 3), "GBps": round(nbytes / t_pf / 1e9, 1),
             "frac": round(nbytes / t_pf / 1e9 / peaks["hbm_gbs"], 4),
             "note": "clove_set_weight_prefetch(1): each call streams its (distinct) weight "
-                    "matrix while the previous call drains"}}
-    del Aq, As, Az
+                    "matrix while the previous call drains"},
+        "read_floor": {
+            "us_per_call": round(t_floor * 1e6, 3), "GBps": round(nbytes / t_floor / 1e9, 1),
+            "decode_over_floor": round(t / t_floor, 3),
+            "note": "clove_debug_stream_read of the same byte count, one launch per call: the "
+                    "bandwidth a single kernel of this size reaches, without any math"}}
 
     # config 3: int8 batch-32 with per-row / per-column scales
     M, N, K = 4096, 32, 4096
@@ -284,13 +301,17 @@ def _secondary(cc, torch, peaks):
     C = torch.empty((M, N), dtype=torch.float16, device="cuda")
     t = timeit(lambda i: cc.gemm_int8_rowcol(Ad[i], Bd, sAd, sBd, C), copies, 200)
     nbytes = M * K + K * N + 4 * M + 4 * N + 2 * M * N
+    del Ad
+    t_floor = read_floor(nbytes, copies)
     out["int8_batch32_4096x32x4096"] = {
         "kernel": cc.describe_dispatch("int8", M, N, K), "us_per_call": round(t * 1e6, 3),
         "GBps": round(nbytes / t / 1e9, 1), "TOPS": round(2 * M * N * K / t / 1e12, 2),
         "roofline": {"bound": "hbm", "achieved": round(nbytes / t / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 4)}}
-    del Ad
+                     "frac": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 4)},
+        "read_floor": {"us_per_call": round(t_floor * 1e6, 3),
+                       "GBps": round(nbytes / t_floor / 1e9, 1),
+                       "gemm_over_floor": round(t / t_floor, 3)}}
 
     # config 1 and the square sweep (fp16), int8 square sweep
     for n in (1024, 2048, 4096, 8192):

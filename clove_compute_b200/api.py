@@ -176,6 +176,16 @@ def debug_int4_group_acc(A_q, A_scale, A_zero, B_q, B_scale, B_zero, stream=None
     return C, G
 
 
+def debug_stream_read(src, out, stream=None) -> None:
+    """Bare read of every byte of the contiguous CUDA tensor `src` (a multiple of 16
+    bytes), nothing computed: the HBM floor of one launch of that size. `out` is an
+    int32 CUDA tensor of at least one element (written only for one specific value)."""
+    if not src.is_contiguous() or src.numel() * src.element_size() % 16:
+        raise ValueError("src must be contiguous and a multiple of 16 bytes")
+    check(lib().clove_debug_stream_read(_ptr(src), src.numel() * src.element_size(), _ptr(out),
+                                        _stream(stream)))
+
+
 def set_dispatch_override(path: int = 0, bn: int = 0, split: int = 0) -> None:
     """Force a kernel family (tests): path 0 auto, 1 tensor core, 2 GEMV, 3 SIMT."""
     check(lib().clove_set_dispatch_override(int(path), int(bn), int(split)))

@@ -162,6 +162,15 @@ int gemv_f16_nc(const void* A, const void* B, void* C, int rows, int K, float al
 
 }  // namespace
 
+int launch_stream_read(const void* src, size_t nbytes, uint32_t* out, const DeviceInfo& dev,
+                       cudaStream_t stream) {
+  const size_t n16 = nbytes / 16;
+  if (n16 == 0) return CLOVE_OK;
+  kern::stream_read_kernel<<<static_cast<unsigned>(dev.num_sms * 2), kern::kStreamThreads, 0, stream>>>(
+      static_cast<const uint4*>(src), n16, out);
+  return check_cuda(cudaGetLastError(), "stream_read launch");
+}
+
 size_t gemv_int4_smem(int nc, int K) { return kern::gemv_int4_smem_bytes(nc, K); }
 size_t gemv_int8_smem(int nc, int K) { return kern::gemv_int8_smem_bytes(nc, K); }
 size_t gemv_f16_smem(int nc, int K) { return kern::gemv_f16_smem_bytes(nc, K); }

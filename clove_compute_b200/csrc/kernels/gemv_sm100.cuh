@@ -541,6 +541,29 @@ __global__ void __launch_bounds__(kWs2Threads, 2)
 #endif
 }
 
+// Bare streaming read of n16 16-byte words (test hook, no GEMM): every thread
+// keeps four 128-bit loads in flight and XOR-folds them. It measures what one
+// kernel launch of this size can pull from HBM -- the floor under the decode
+// GEMVs, which read the same number of bytes and also compute.
+constexpr int kStreamThreads = 512;
+__global__ void __launch_bounds__(kStreamThreads)
+    stream_read_kernel(const uint4* __restrict__ src, size_t n16, uint32_t* __restrict__ out) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  uint32_t x = 0;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const size_t j = i + u * stride;
+      v[u] = j < n16 ? dev::ld_nc_v4(reinterpret_cast<const uint8_t*>(src + j)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
+  }
+  // Keeps the loads live; the word is written only for one specific value.
+  if (x == 0x9E3779B9u) out[0] = x;
+}
+
 __host__ __device__ constexpr size_t gemv_int8_smem_bytes(int nc, int K) {
   return static_cast<size_t>(nc) * K + 4 * 8;
 }

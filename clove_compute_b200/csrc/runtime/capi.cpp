@@ -417,6 +417,16 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
                         as_stream(stream), nullptr);
 }
 
+int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream) {
+  if (src == nullptr || out == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "null pointer");
+  if (nbytes % 16 != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "stream_read needs 16-byte aligned, 16-byte multiple");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  return launch_stream_read(src, nbytes, out, dev, as_stream(stream));
+}
+
 // ---------------------------------------------------------------------------
 // Introspection
 // ---------------------------------------------------------------------------

@@ -80,6 +80,10 @@ int launch_gemv_f16(const void* A, const void* B, void* C, int rows, int nc, int
                     float beta, const DeviceInfo& dev, cudaStream_t stream);
 size_t gemv_f16_smem(int nc, int K);
 int read_clear_error_gemv();
+// Bare read of nbytes (multiple of 16, 16-byte aligned) into nothing: the HBM floor
+// of one launch of that size.
+int launch_stream_read(const void* src, size_t nbytes, uint32_t* out, const DeviceInfo& dev,
+                       cudaStream_t stream);
 
 // ---- SIMT fallback + helpers (kernels/fallback_simt.cu)
 int launch_simt_f16(const void* A, const void* B, void* C, int batch, int M, int N, int K,

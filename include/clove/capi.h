@@ -117,6 +117,12 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
                                const uint8_t* B_q, const void* B_scale, const void* B_zero,
                                void* C, int32_t* G, int M, int N, int K, void* stream);
 
+/* Bare streaming read of nbytes at src (16-byte aligned, a multiple of 16 bytes),
+ * nothing computed; *out is written only for one specific XOR of the data. It times
+ * what one launch of that size can pull from HBM: the floor under the decode GEMVs.
+ * (Measurement hook; no counterpart in the reference.) */
+int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream);
+
 /* Forces a kernel family for subsequent calls from any thread (tests only).
  * path: 0 = automatic, 1 = tensor-core tiles on one SM, 2 = GEMV, 3 = SIMT
  * fallback, 4 = tensor-core 256 x 256 tiles on CTA pairs.

@@ -133,3 +133,16 @@ def test_register_gemv_path(clove_lib, oracle_mod, cuda):
     """The register-resident GEMV (used when the bulk-copy kernel does not apply)."""
     clove_lib.set_dispatch_override(2, 1, 0)
     _check(clove_lib, oracle_mod, 4096, 1, 4096, path=2, seed=3, check_g=False)
+
+
+@pytest.mark.gpu
+def test_stream_read_hook(clove_lib, cuda):
+    """The bare-read measurement hook runs on any 16-byte multiple and rejects others."""
+    import torch
+    buf = torch.ones(1 << 20, dtype=torch.uint8, device="cuda")
+    sink = torch.zeros(4, dtype=torch.int32, device="cuda")
+    clove_lib.debug_stream_read(buf, sink)
+    torch.cuda.synchronize()
+    assert int(sink[0]) == 0  # XOR of an even number of equal words is 0, not the sentinel
+    with pytest.raises(ValueError):
+        clove_lib.debug_stream_read(buf[:17], sink)
