@@ -10,6 +10,19 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_int4)
 
+}  // namespace rt
+}  // namespace clove
+
+#ifdef CLOVE_TRACE
+// Development builds only: trace slots of the INT4 kernel.
+extern "C" int clove_trace_read_int4(unsigned long long* out) {
+  return static_cast<int>(cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * 256));
+}
+#endif
+
+namespace clove {
+namespace rt {
+
 namespace {
 std::atomic<uint64_t> g_attr_set[2];
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -52,7 +65,16 @@ int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const
   const dim3 grid((N + S::BN - 1) / S::BN, (M + S::BM - 1) / S::BM, 1);
   kernel<<<grid, S::THREADS, S::SMEM_BYTES, stream>>>(tAq, tBq, tAs, tAz, tBs, tBz, tC, M, N, K,
                                                       Gdbg);
-  return check_cuda(cudaGetLastError(), "gemm_int4_tc launch");
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, kernel);
+    return fail(CLOVE_ERR_CUDA,
+                "gemm_int4_tc launch: %s (regs %d, max threads %d, dyn smem %d of %d)",
+                cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, S::SMEM_BYTES,
+                fa.maxDynamicSharedSizeBytes);
+  }
+  return CLOVE_OK;
 }
 
 }  // namespace rt

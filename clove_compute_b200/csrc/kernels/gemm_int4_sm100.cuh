@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
   __syncthreads();
   dev::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) CLOVE_TRACE_POINT(0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -181,6 +182,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         dev::mbar_arrive_expect_tx(&pk_full[s], S::PK_BYTES);
         dev::tma_load_2d(pk, &tmAq, &pk_full[s], g * S::GB, m0);
         dev::tma_load_2d(pk + S::PK_A, &tmBq, &pk_full[s], g * S::GB, n0);
+        if (g < 32) CLOVE_TRACE_POINT(160 + g);
         armed |= 1u << s;
         armed_par = (armed_par & ~(1u << s)) | ((use & 1u) << s);
       }
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
                             abort_flag))
           break;
         dev::tc_fence_after_sync();
+        if (g < 32) CLOVE_TRACE_POINT(96 + g);
         const uint32_t a_addr = dev::smem_u32(smem + S::OFF_UN + u * S::UN_BYTES);
         const uint32_t b_addr = a_addr + S::UN_A;
         const uint32_t d = tmem_base + static_cast<uint32_t>(b) * S::BN;
@@ -282,6 +285,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
       __syncwarp();
       if (lane == 0) {
+        if (warp == 2 && g < 32) CLOVE_TRACE_POINT(64 + g);
         dev::mbar_arrive(&un_full[u]);
         dev::mbar_arrive(&sb_full[sbs]);
         dev::mbar_arrive(&pk_empty[s]);
@@ -357,6 +361,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) {
+        if (warp == 6 && g < 32) CLOVE_TRACE_POINT(128 + g);
         dev::mbar_arrive(&sb_empty[sbs]);
         if ((g & 7) == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
       }
