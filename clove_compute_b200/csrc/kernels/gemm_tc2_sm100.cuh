@@ -102,6 +102,10 @@ __global__ void __launch_bounds__(192, 1)
   dev::cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA use
   dev::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the set-up above overlaps the tail of the
+  // previous kernel on the stream; no global memory is touched before it completes.
+  dev::allow_dependent_launch();
+  dev::grid_dependency_wait();
 
   const int tiles_m = (M + 2 * S::BM - 1) / (2 * S::BM);
   const int tiles_n = (N + S::BN - 1) / S::BN;

@@ -163,23 +163,24 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
   epv.c_out = C;
   void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(e->smem_bytes);
   cfg.stream = stream;
+  cfg.attrs = attr;
   if (split > 1) {
     cfg.gridDim = dim3(static_cast<unsigned>(split), static_cast<unsigned>(tiles), 1);
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(split);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(split);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
   } else {
     const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.attrs = nullptr;
-    cfg.numAttrs = 0;
+    cfg.numAttrs = 1;
   }
   return check_cuda(cudaLaunchKernelExC(&cfg, e->fn, args), "gemm_tc launch");
 }
@@ -230,17 +231,19 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
   kern::EpiParams epv = ep;
   void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = 2;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = stream;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "gemm_tc2 launch");
 }
 

@@ -296,6 +296,10 @@ __global__ void __launch_bounds__(192, 1)
   dev::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   if constexpr (SPLIT) dev::cluster_arrive();  // receive barriers initialised
+  // Programmatic dependent launch: the set-up above overlaps the tail of the
+  // previous kernel on the stream; no global memory is touched before it completes.
+  dev::allow_dependent_launch();
+  dev::grid_dependency_wait();
   if (threadIdx.x == 0) CLOVE_TRACE_POINT(1);
 
   const int tiles_m = (M + S::BM - 1) / S::BM;

@@ -137,7 +137,7 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
       best.split = 1;
     }
   }
-  if (best.split > 1 && best.bn > 64) best.bn = 64;
+  if (best.split > 1 && best.bn > 128) best.bn = 128;
   // CTA pairs (256 x 256 tiles) when the one-SM plan is 128 x 256 tiles and the
   // pair tiles fill at least one wave of SM pairs.
   const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 255) / 256);
