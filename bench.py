@@ -313,6 +313,21 @@ def _secondary(cc, torch, peaks):
                        "GBps": round(nbytes / t_floor / 1e9, 1),
                        "gemm_over_floor": round(t / t_floor, 3)}}
 
+    # gemm_fp16_batched: 64 problems of 256^3 in one persistent launch (3D tensor
+    # maps, a batch plane per problem) against 64 single-problem launches; the
+    # 25 MB working set stays in L2: this measures launch and fill efficiency.
+    batch, n = 64, 256
+    Ab = torch.randn((batch, n, n), device="cuda").half() / 16
+    Bb = torch.randn((batch, n, n), device="cuda").half() / 16
+    Cb = torch.empty((batch, n, n), dtype=torch.float16, device="cuda")
+    t_b = timeit(lambda i: cc.gemm_fp16_batched(Ab, Bb, Cb), 1, 200)
+    t_l = timeit(lambda i: [cc.gemm_fp16(Ab[j], Bb[j], Cb[j]) for j in range(batch)], 1, 20)
+    out["fp16_batched_64x256x256x256"] = {
+        "us_per_call": round(t_b * 1e6, 3), "TFLOPS": round(2 * batch * n ** 3 / t_b / 1e12, 2),
+        "per_problem_launches_us": round(t_l * 1e6, 3),
+        "note": "one batched launch vs 64 clove_gemm_fp16 launches (CUDA graph), L2-resident"}
+    del Ab, Bb, Cb
+
     # config 1 and the square sweep (fp16), int8 square sweep
     for n in (1024, 2048, 4096, 8192):
         A, B = wl.fp16_operands(n, n, n, seed=0)

@@ -38,7 +38,7 @@ using kern::OpF16;
 using kern::OpI8;
 using kern::TcShape;
 
-typedef void (*TcKernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, EpiParams);
+typedef void (*TcKernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, int, EpiParams);
 
 struct TcEntry {
   int op, bn, split, out_bytes;
@@ -122,7 +122,9 @@ bool gemm_tc_supported(int op, int bn, int split, int out_bytes) {
 
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
-                   const DeviceInfo& dev, cudaStream_t stream) {
+                   const DeviceInfo& dev, cudaStream_t stream, int batch) {
+  if (batch < 1 || (batch > 1 && split > 1))
+    return fail(CLOVE_ERR_UNSUPPORTED, "batched tiles need split 1 (batch %d split %d)", batch, split);
   const int ei = find_entry(op, bn, split, out_bytes);
   if (ei < 0)
     return fail(CLOVE_ERR_UNSUPPORTED, "no tensor-core kernel for op=%d bn=%d split=%d out=%d", op,
@@ -137,16 +139,19 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
 
   CUtensorMap tmA, tmB, tmC;
   int rc;
+  // All three as [batch, rows, cols] (batch 1 for a plain GEMM), densely packed.
+  const uint64_t ub = static_cast<uint64_t>(batch);
   // A [M,K]: box 128 B of K x 128 rows, 128B swizzle.
-  rc = encode_tmap_2d(&tmA, in_dt, elem, A, K, M, static_cast<uint64_t>(K) * elem, e->bk, 128, 128);
+  rc = encode_tmap_3d(&tmA, in_dt, elem, A, K, M, ub, static_cast<uint64_t>(K) * elem,
+                      static_cast<uint64_t>(M) * K * elem, e->bk, 128, 128);
   if (rc) return rc;
   // B [K,N]: box (swizzle width of N) x BK rows.
-  rc = encode_tmap_2d(&tmB, in_dt, elem, B, N, K, static_cast<uint64_t>(N) * elem, e->b_atom_elems,
-                      e->bk, e->b_sw);
+  rc = encode_tmap_3d(&tmB, in_dt, elem, B, N, K, ub, static_cast<uint64_t>(N) * elem,
+                      static_cast<uint64_t>(K) * N * elem, e->b_atom_elems, e->bk, e->b_sw);
   if (rc) return rc;
   // C [M,N]: box CHUNK cols x 32 rows, swizzle = staging row bytes.
-  rc = encode_tmap_2d(&tmC, out_dt, out_bytes, C, N, M, static_cast<uint64_t>(N) * out_bytes,
-                      e->chunk, 32, e->stg_row);
+  rc = encode_tmap_3d(&tmC, out_dt, out_bytes, C, N, M, ub, static_cast<uint64_t>(N) * out_bytes,
+                      static_cast<uint64_t>(M) * N * out_bytes, e->chunk, 32, e->stg_row);
   if (rc) return rc;
 
   const uint64_t bit = 1ull << (dev.device & 63);
@@ -161,7 +166,7 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   EpiParams epv = ep;
   epv.c_out = C;
-  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
+  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &batch, &epv};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -178,7 +183,8 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   } else {
-    const int grid = tiles < dev.num_sms ? tiles : dev.num_sms;
+    const long long all = static_cast<long long>(tiles) * batch;
+    const int grid = all < dev.num_sms ? static_cast<int>(all) : dev.num_sms;
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.numAttrs = 1;
   }

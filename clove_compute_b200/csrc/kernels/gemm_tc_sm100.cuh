@@ -188,7 +188,8 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
                                             int row, int ncol0, int M, int N, int K,
                                             float row_scale, int32_t row_corr, uint32_t lane,
                                             uint8_t* stg_base, uint32_t& stg_count,
-                                            const CUtensorMap* tmC, int store_row0) {
+                                            const CUtensorMap* tmC, int store_row0,
+                                            int plane = -1) {
   constexpr int STG_ROW = CHUNK * OUT_BYTES;
   constexpr int PKTS = STG_ROW / 16;
   uint32_t pk[PKTS][4];
@@ -207,7 +208,10 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
   dev::fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    dev::tma_store_2d(tmC, stg, ncol0, store_row0);
+    if (plane < 0)  // 2D map (CTA-pair kernel)
+      dev::tma_store_2d(tmC, stg, ncol0, store_row0);
+    else            // 3D [batch, M, N] map
+      dev::tma_store_3d(tmC, stg, ncol0, store_row0, plane);
     dev::bulk_commit_group();
   }
   ++stg_count;
@@ -234,10 +238,19 @@ __device__ __forceinline__ void store_row_direct(const uint32_t (&v)[CHUNK], con
   }
 }
 
+// Epilogue parameters of batch plane `plane`: the beta source moves with C (the
+// batched entry is fp16 only; the int8 per-row / per-column vectors are unbatched).
+__device__ __forceinline__ EpiParams ep_plane(const EpiParams& ep, int plane, int M, int N) {
+  EpiParams e = ep;
+  if (e.c_in != nullptr) e.c_in += static_cast<size_t>(plane) * M * N;
+  return e;
+}
+
 template <class Op, int BN, bool SPLIT, int OUT_BYTES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep) {
+                   const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int batch,
+                   EpiParams ep) {
   using S = TcShape<Op, BN, SPLIT, OUT_BYTES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -302,9 +315,11 @@ __global__ void __launch_bounds__(192, 1)
   dev::grid_dependency_wait();
   if (threadIdx.x == 0) CLOVE_TRACE_POINT(1);
 
+  // Tensor maps are 3D [batch, rows, cols]; tile t covers plane t / (tiles_m * tiles_n).
   const int tiles_m = (M + S::BM - 1) / S::BM;
   const int tiles_n = (N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
+  const int tiles_mn = tiles_m * tiles_n;
+  const int num_tiles = tiles_mn * batch;
   const int kb_total = (K + S::BK - 1) / S::BK;
   int tile_first, tile_stride, kb_begin, kb_end;
   if constexpr (SPLIT) {
@@ -329,11 +344,12 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t armed_parity = 0;
       for (int tile = tile_first; tile < num_tiles; tile += tile_stride) {
         int m_blk, n_blk;
+        const int plane = tile / tiles_mn;
         if constexpr (SPLIT) {
           m_blk = tile / tiles_n;
           n_blk = tile % tiles_n;
         } else {
-          tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+          tile_coords(tile - plane * tiles_mn, tiles_m, tiles_n, m_blk, n_blk);
         }
         bool ok = true;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
@@ -345,11 +361,11 @@ __global__ void __launch_bounds__(192, 1)
           if (kb == kb_begin) CLOVE_TRACE_POINT(2);
           uint8_t* a_dst = stage_base + stage * S::STAGE_BYTES;
           uint8_t* b_dst = a_dst + S::A_BYTES;
-          dev::tma_load_2d(a_dst, &tmA, &full[stage], kb * S::BK, m_blk * S::BM);
+          dev::tma_load_3d(a_dst, &tmA, &full[stage], kb * S::BK, m_blk * S::BM, plane);
 #pragma unroll
           for (int a = 0; a < S::B_ATOMS; ++a) {
-            dev::tma_load_2d(b_dst + a * (S::BK * S::B_SW), &tmB, &full[stage],
-                             n_blk * BN + a * S::B_ATOM_ELEMS, kb * S::BK);
+            dev::tma_load_3d(b_dst + a * (S::BK * S::B_SW), &tmB, &full[stage],
+                             n_blk * BN + a * S::B_ATOM_ELEMS, kb * S::BK, plane);
           }
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -427,11 +443,12 @@ __global__ void __launch_bounds__(192, 1)
     if constexpr (SPLIT) dev::cluster_wait();  // every peer's rbar is initialised
     for (int tile = tile_first; tile < num_tiles; tile += tile_stride, ++it) {
       int m_blk, n_blk;
+      const int plane = tile / tiles_mn;
       if constexpr (SPLIT) {
         m_blk = tile / tiles_n;
         n_blk = tile % tiles_n;
       } else {
-        tile_coords(tile, tiles_m, tiles_n, m_blk, n_blk);
+        tile_coords(tile - plane * tiles_mn, tiles_m, tiles_n, m_blk, n_blk);
       }
       const uint32_t buf = static_cast<uint32_t>(it) & (S::ACC_BUFS - 1);
       const uint32_t use = static_cast<uint32_t>(it) / S::ACC_BUFS;
@@ -578,9 +595,10 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&tempty[buf]);
           }
-          store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr,
-                                               lane, stg_base, stg_count, &tmC,
-                                               m0 + static_cast<int>(q) * 32);
+          store_chunk<Op, OUT_BYTES, S::CHUNK>(v, plane == 0 ? ep : ep_plane(ep, plane, M, N), row,
+                                               n0 + c0, M, N, K, row_scale, row_corr, lane,
+                                               stg_base, stg_count, &tmC,
+                                               m0 + static_cast<int>(q) * 32, plane);
         }
       }
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);

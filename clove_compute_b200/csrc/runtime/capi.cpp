@@ -241,12 +241,56 @@ int clove_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, 
   return gemm_fp16_impl(A, B, C, M, N, K, alpha, beta, as_stream(stream), nullptr);
 }
 
+// Tile width for `batch` problems of M x N sharing one persistent launch: the
+// plan_tc cost (waves x width x narrow-tile penalty) over all problems' tiles.
+static int plan_bn_batched(int M, int N, int batch, int num_sms) {
+  const Override ov = get_override();
+  if (ov.bn == 64 || ov.bn == 128 || ov.bn == 256) return ov.bn;
+  const long long tm = (M + 127) / 128;
+  const int cand[3] = {256, 128, 64};
+  const double penalty[3] = {1.0, 1.15, 1.45};
+  int best = 256;
+  double best_cost = 1e30;
+  for (int i = 0; i < 3; ++i) {
+    const long long tiles = tm * ((N + cand[i] - 1) / cand[i]) * batch;
+    const long long waves = (tiles + num_sms - 1) / num_sms;
+    const double cost = static_cast<double>(waves) * cand[i] * penalty[i];
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = cand[i];
+    }
+  }
+  return best;
+}
+
 int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K,
                             float alpha, float beta, void* stream) {
   if (batch < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative batch");
   if (batch == 0 || M == 0 || N == 0) return CLOVE_OK;
+  if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
   const size_t sa = static_cast<size_t>(M) * K * 2, sb = static_cast<size_t>(K) * N * 2,
                sc = static_cast<size_t>(M) * N * 2;
+  if (batch > 1 && K > 0 && A != nullptr && B != nullptr && C != nullptr) {
+    // Problems too small to fill the GPU on their own share one persistent launch
+    // of the tile kernel (3D tensor maps, a batch plane per problem); larger ones
+    // run back to back through the single-problem dispatch (CTA pairs etc.).
+    DeviceInfo dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const Override ov = get_override();
+    const bool tc_ok = K % 8 == 0 && N % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
+                       (ov.path == 0 || ov.path == 1) && (ov.split == 0 || ov.split == 1);
+    const long long tiles1 = static_cast<long long>((M + 127) / 128) * ((N + 63) / 64);
+    if (tc_ok && tiles1 < dev.num_sms) {
+      kern::EpiParams ep{};
+      ep.mode = kern::kEpiF16AlphaBeta;
+      ep.alpha = alpha;
+      ep.beta = beta;
+      ep.c_in = static_cast<const __half*>(C);
+      return launch_gemm_tc(kTcF16, plan_bn_batched(M, N, batch, dev.num_sms), 1, 2, A, B, C, M,
+                            N, K, ep, dev, as_stream(stream), batch);
+    }
+  }
   for (int b = 0; b < batch; ++b) {
     const int rc = gemm_fp16_impl(static_cast<const char*>(A) + b * sa,
                                   static_cast<const char*>(B) + b * sb,

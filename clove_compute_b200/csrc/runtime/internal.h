@@ -57,9 +57,11 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms);
 enum TcOp { kTcF16 = 0, kTcI8 = 1 };
 // bn in {32,64,128,256}; split in [1,8] (split > 1 requires bn <= 64);
 // out_bytes 2 (fp16 C) or 4 (int32 C, raw accumulators).
+// batch > 1: `batch` densely packed problems ([batch,M,K] . [batch,K,N]) in one
+// persistent launch (split must be 1).
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
-                   const DeviceInfo& dev, cudaStream_t stream);
+                   const DeviceInfo& dev, cudaStream_t stream, int batch = 1);
 // CTA-pair kernel: 256 x 256 tiles on two SMs (fp16 C).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream);

@@ -25,15 +25,19 @@ void resolve_encode() {
 }
 }  // namespace
 
-int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
-                   uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                   uint32_t box_outer, int swizzle_bytes) {
+namespace {
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                int rank, const uint64_t* dims_in, const uint64_t* strides_in, uint32_t box_inner,
+                uint32_t box_outer, int swizzle_bytes) {
   std::call_once(g_encode_once, resolve_encode);
   if (g_encode == nullptr)
     return fail(CLOVE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
                 cudaGetErrorString(g_encode_err));
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_bytes & 15u) != 0)
-    return fail(CLOVE_ERR_UNSUPPORTED, "TMA needs 16-byte aligned base and row stride");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(CLOVE_ERR_UNSUPPORTED, "TMA needs a 16-byte aligned base");
+  for (int i = 0; i + 1 < rank; ++i)
+    if ((strides_in[i] & 15u) != 0)
+      return fail(CLOVE_ERR_UNSUPPORTED, "TMA needs 16-byte multiple strides");
   if (static_cast<uint64_t>(box_inner) * elem_bytes % 16 != 0)
     return fail(CLOVE_ERR_UNSUPPORTED, "TMA box inner extent must be a multiple of 16 bytes");
   CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
@@ -44,22 +48,44 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
     case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
     default: return fail(CLOVE_ERR_INVALID_ARG, "bad swizzle width %d", swizzle_bytes);
   }
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+  cuuint64_t dims[3];
+  cuuint64_t strides[2];
+  const cuuint32_t box[3] = {box_inner, box_outer, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) dims[i] = static_cast<cuuint64_t>(dims_in[i]);
+  for (int i = 0; i + 1 < rank; ++i) strides[i] = static_cast<cuuint64_t>(strides_in[i]);
+  const CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(CLOVE_ERR_UNSUPPORTED,
-                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu box %u x %u sw %d",
-                static_cast<int>(r), static_cast<unsigned long long>(inner),
-                static_cast<unsigned long long>(outer),
-                static_cast<unsigned long long>(row_stride_bytes), box_inner, box_outer,
+                "cuTensorMapEncodeTiled failed (%d): rank %d dims %llu x %llu x %llu box %u x %u sw %d",
+                static_cast<int>(r), rank, static_cast<unsigned long long>(dims_in[0]),
+                static_cast<unsigned long long>(dims_in[1]),
+                static_cast<unsigned long long>(rank > 2 ? dims_in[2] : 1), box_inner, box_outer,
                 swizzle_bytes);
   return CLOVE_OK;
+}
+}  // namespace
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                   uint32_t box_outer, int swizzle_bytes) {
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_stride_bytes};
+  return encode_tmap(map, dtype, elem_bytes, base, 2, dims, strides, box_inner, box_outer,
+                     swizzle_bytes);
+}
+
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t depth, uint64_t row_stride_bytes,
+                   uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                   int swizzle_bytes) {
+  const uint64_t dims[3] = {inner, outer, depth};
+  const uint64_t strides[2] = {row_stride_bytes, plane_stride_bytes};
+  return encode_tmap(map, dtype, elem_bytes, base, 3, dims, strides, box_inner, box_outer,
+                     swizzle_bytes);
 }
 
 }  // namespace rt

@@ -16,5 +16,13 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                    uint32_t box_outer, int swizzle_bytes);
 
+// As encode_tmap_2d for a stack of `depth` such matrices, plane_stride_bytes apart
+// (a batch): a 3D tensor [depth, outer, inner] with a box one plane deep, so that
+// out-of-bounds rows of one matrix never read or write its neighbour.
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t depth, uint64_t row_stride_bytes,
+                   uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                   int swizzle_bytes);
+
 }  // namespace rt
 }  // namespace clove

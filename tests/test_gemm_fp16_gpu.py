@@ -108,14 +108,36 @@ def test_k_zero_scales_c(clove_lib, cuda):
     np.testing.assert_array_equal(host(Cd), (C0.astype(np.float32) * 0.5).astype(np.float16))
 
 
-def test_batched(clove_lib, oracle_mod, cuda):
-    batch, M, N, K = 3, 128, 64, 96
-    rng = np.random.default_rng(4)
+@pytest.mark.parametrize("batch,M,N,K", [
+    (3, 128, 64, 96),      # one tile per problem: one batched launch
+    (5, 200, 136, 128),    # ragged M and N: rows past M must not touch the next problem
+    (64, 128, 128, 256),   # many problems share the persistent grid
+    (2, 2048, 2048, 256),  # each problem fills the GPU: per-problem dispatch
+])
+def test_batched(clove_lib, oracle_mod, cuda, batch, M, N, K):
+    rng = np.random.default_rng(4 + batch)
     A = (rng.standard_normal((batch, M, K)) / np.sqrt(K)).astype(np.float16)
     B = (rng.standard_normal((batch, K, N)) / np.sqrt(K)).astype(np.float16)
     C = host(clove_lib.gemm_fp16_batched(dev(A), dev(B)))
     for b in range(batch):
-        assert rel_fro(C[b], oracle_mod.gemm_fp16(A[b], B[b])) < TOL_TIGHT
+        assert rel_fro(C[b], oracle_mod.gemm_fp16(A[b], B[b])) < TOL_TIGHT, b
+
+
+def test_batched_alpha_beta(clove_lib, oracle_mod, cuda):
+    """beta reads each problem's own C plane in the single-launch batched path."""
+    import torch
+    batch, M, N, K = 4, 192, 72, 64
+    rng = np.random.default_rng(11)
+    A = (rng.standard_normal((batch, M, K)) / np.sqrt(K)).astype(np.float16)
+    B = (rng.standard_normal((batch, K, N)) / np.sqrt(K)).astype(np.float16)
+    C0 = rng.uniform(-1, 1, (batch, M, N)).astype(np.float16)
+    Ad, Bd, Cd = dev(A), dev(B), dev(C0.copy())
+    clove_lib.gemm_fp16_batched(Ad, Bd, Cd, alpha=0.5, beta=-2.0)
+    torch.cuda.synchronize()
+    C = host(Cd)
+    for b in range(batch):
+        ref = oracle_mod.gemm_fp16(A[b], B[b], C=C0[b].copy(), alpha=0.5, beta=-2.0)
+        assert rel_fro(C[b], ref) < TOL_TIGHT, b
 
 
 def test_no_writes_outside_c(clove_lib, oracle_mod, cuda):
