@@ -176,6 +176,22 @@ def debug_int4_group_acc(A_q, A_scale, A_zero, B_q, B_scale, B_zero, stream=None
     return C, G
 
 
+def quantize_int4(W: torch.Tensor, stream=None):
+    """Pack fp16 weights W [rows, K] (K % 128 == 0) into the INT4 layout gemm_int4
+    reads: (codes [rows, K/2] uint8, scales [rows, K/128] fp16, zeros [rows, K/128] fp16).
+    Asymmetric min/max per 128-group; see include/clove/capi.h for the rounding rules."""
+    _need(W, "W", torch.float16, 2)
+    rows, K = W.shape
+    if K % INT4_GROUP_SIZE:
+        raise ValueError("K must be a multiple of 128")
+    codes = torch.empty((rows, K // 2), dtype=torch.uint8, device=W.device)
+    scales = torch.empty((rows, K // INT4_GROUP_SIZE), dtype=torch.float16, device=W.device)
+    zeros = torch.empty((rows, K // INT4_GROUP_SIZE), dtype=torch.float16, device=W.device)
+    check(lib().clove_quantize_int4(_ptr(W), rows, K, _ptr(codes), _ptr(scales), _ptr(zeros),
+                                    _stream(stream)))
+    return codes, scales, zeros
+
+
 def debug_stream_read(src, out, stream=None) -> None:
     """Bare read of every byte of the contiguous CUDA tensor `src` (a multiple of 16
     bytes), nothing computed: the HBM floor of one launch of that size. `out` is an

@@ -461,6 +461,23 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
                         as_stream(stream), nullptr);
 }
 
+int clove_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,
+                        void* stream) {
+  if (rows < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
+  if (K % CLOVE_INT4_GROUP_SIZE != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "quantize_int4: K must be a multiple of 128");
+  if (rows == 0 || K == 0) return CLOVE_OK;
+  if (W == nullptr || codes == nullptr || scales == nullptr || zeros == nullptr)
+    return fail(CLOVE_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(W) & 7u) != 0 || (reinterpret_cast<uintptr_t>(codes) & 1u) != 0 ||
+      !aligned2(scales) || !aligned2(zeros))
+    return fail(CLOVE_ERR_INVALID_ARG, "quantize_int4: W 8-byte, codes/scales/zeros 2-byte aligned");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  return launch_quantize_int4(W, rows, K, codes, scales, zeros, as_stream(stream));
+}
+
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream) {
   if (src == nullptr || out == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "null pointer");
   if (nbytes % 16 != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) != 0)

@@ -87,6 +87,10 @@ int read_clear_error_gemv();
 int launch_stream_read(const void* src, size_t nbytes, uint32_t* out, const DeviceInfo& dev,
                        cudaStream_t stream);
 
+// ---- INT4 packing tool (kernels/quant_int4.cu)
+int launch_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,
+                         cudaStream_t stream);
+
 // ---- SIMT fallback + helpers (kernels/fallback_simt.cu)
 int launch_simt_f16(const void* A, const void* B, void* C, int batch, int M, int N, int K,
                     float alpha, float beta, cudaStream_t stream);

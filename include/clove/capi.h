@@ -106,6 +106,14 @@ int clove_gemm_int4(const uint8_t* A_q, const void* A_scale, const void* A_zero,
                     const uint8_t* B_q, const void* B_scale, const void* B_zero, void* C, int M,
                     int N, int K, void* stream);
 
+/* INT4 packing tool (no counterpart in the reference, whose weight loader is a
+ * stub): W [rows,K] binary16 -> codes [rows,K/2], scales / zeros [rows,K/128] in
+ * exactly the layout clove_gemm_int4 reads. Asymmetric min/max per 128-group over
+ * a range that contains 0: scale = half((max-min)/15), zero = clamp(rint(-min/scale),0,15),
+ * code = clamp(rint(w/scale)+zero,0,15). K % 128 == 0; W 8-byte aligned. */
+int clove_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,
+                        void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Test hooks: exact int32 accumulators through the same kernels.              */
 /* ------------------------------------------------------------------------- */

@@ -48,6 +48,7 @@ _SIGS = {
     "clove_oracle_int4_group_acc": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
     "clove_oracle_gemm_int4": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
     "clove_oracle_gemm_int4_refcompat": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
+    "clove_oracle_quantize_int4": ([_P, _I, _I, _P, _P, _P], None),
 }
 
 
@@ -210,3 +211,17 @@ def rel_frobenius(x, ref) -> float:
     den = np.linalg.norm(ref)
     num = np.linalg.norm(x - ref)
     return float(num / den) if den > 0 else float(num)
+
+
+def quantize_int4(W):
+    """(codes [rows,K/2] uint8, scales [rows,K/128] fp16, zeros [rows,K/128] fp16):
+    this build's INT4 packing specification (min/max per 128-group) on the CPU."""
+    W = np.ascontiguousarray(W, np.float16)
+    rows, K = W.shape
+    assert K % 128 == 0
+    codes = np.zeros((rows, K // 2), np.uint8)
+    scales = np.zeros((rows, K // 128), np.uint16)
+    zeros = np.zeros((rows, K // 128), np.uint16)
+    lib().clove_oracle_quantize_int4(_ptr(W.view(np.uint16)), rows, K, _ptr(codes), _ptr(scales),
+                                     _ptr(zeros))
+    return codes, scales.view(np.float16), zeros.view(np.float16)

@@ -378,3 +378,52 @@ void clove_oracle_gemm_int4_refcompat(const uint8_t* Aq, const uint16_t* As,
         }
     }
 }
+
+/* ------------------------------------------------------------------------- */
+/* INT4 packing of fp16 weights into the layout clove_gemm_int4 consumes.     */
+/* The reference has no quantizer (its safetensors loader is a stub,          */
+/* src/runtime/model_loader.cpp:57-85); this is the specification of this     */
+/* build's tool, restated on the CPU: asymmetric min/max per 128-group over  */
+/* a range that contains 0 (min <= 0 <= max, so an all-positive or constant   */
+/* group keeps its values), scale = half((max-min)/15) (0 -> smallest         */
+/* subnormal, clamped to 65504),                                              */
+/* zero = clamp(rint(-min/scale), 0, 15), code = clamp(rint(w/scale) + zero, */
+/* 0, 15), fp32 arithmetic with IEEE division and ties-to-even rounding.      */
+/* ------------------------------------------------------------------------- */
+void clove_oracle_quantize_int4(const uint16_t* W, int rows, int K, uint8_t* codes,
+                                uint16_t* scales, uint16_t* zeros) {
+    if (rows <= 0 || K <= 0 || K % INT4_GROUP != 0) return;
+    const int ng = K / INT4_GROUP;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++) {
+        for (int g = 0; g < ng; g++) {
+            const uint16_t* w = W + (int64_t)r * K + (int64_t)g * INT4_GROUP;
+            float mn = 0.0f, mx = 0.0f; /* the range always contains 0 */
+            for (int i = 0; i < INT4_GROUP; i++) {
+                float v = clove_oracle_h2f(w[i]);
+                mn = v < mn ? v : mn;
+                mx = v > mx ? v : mx;
+            }
+            float s = (mx - mn) / 15.0f;
+            uint16_t sh = clove_oracle_f2h(s);
+            if ((sh & 0x7fff) == 0) sh = 0x0001;       /* smallest positive subnormal */
+            if ((sh & 0x7fff) > 0x7bff) sh = 0x7bff;   /* 65504 */
+            const float sf = clove_oracle_h2f(sh);
+            float zf = rintf(-mn / sf);
+            zf = zf < 0.0f ? 0.0f : (zf > 15.0f ? 15.0f : zf);
+            const int z = (int)zf;
+            scales[(int64_t)r * ng + g] = sh;
+            zeros[(int64_t)r * ng + g] = clove_oracle_f2h((float)z);
+            uint8_t* out = codes + (int64_t)r * (K / 2) + (int64_t)g * (INT4_GROUP / 2);
+            for (int j = 0; j < INT4_GROUP / 2; j++) {
+                int q[2];
+                for (int e = 0; e < 2; e++) {
+                    float t = rintf(clove_oracle_h2f(w[2 * j + e]) / sf) + (float)z;
+                    t = t < 0.0f ? 0.0f : (t > 15.0f ? 15.0f : t);
+                    q[e] = (int)t;
+                }
+                out[j] = (uint8_t)((q[0] << 4) | q[1]);
+            }
+        }
+    }
+}

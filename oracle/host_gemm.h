@@ -100,6 +100,15 @@ void clove_oracle_gemm_int4_refcompat(const uint8_t* Aq, const uint16_t* As,
                                       uint16_t* C, int M, int N, int K,
                                       int row_begin, int row_end, int nthreads);
 
+/* INT4 packing tool (this build's specification; the reference has none):
+ * W [rows,K] binary16, K % 128 == 0 -> codes [rows,K/2] (element 2j in the high
+ * nibble of byte j), scales / zeros [rows,K/128] binary16. Asymmetric min/max per
+ * 128-group over a range that contains 0 (min <= 0 <= max):
+ * scale = half((max-min)/15) (0 -> smallest subnormal, capped at 65504),
+ * zero = clamp(rint(-min/scale),0,15), code = clamp(rint(w/scale)+zero,0,15). */
+void clove_oracle_quantize_int4(const uint16_t* W, int rows, int K, uint8_t* codes,
+                                uint16_t* scales, uint16_t* zeros);
+
 #ifdef __cplusplus
 }
 #endif

@@ -251,3 +251,69 @@ def test_oracle_refcompat_vs_reference_int4_golden(oracle_mod, fname):
     M, N, K = int(d["M"]), int(d["N"]), int(d["K"])
     C = oracle_mod.gemm_int4_refcompat(d["A_q"], d["A_scale"], d["B_q"], d["B_scale"], M, N, K)
     assert np.array_equal(C.view(np.uint16), d["C_ref"].view(np.uint16))
+
+
+# ---------------------------------------------------------------------------
+# INT4 packing tool: the C restatement against an independent numpy statement of
+# the same specification, and known answers.
+# ---------------------------------------------------------------------------
+def _np_quantize_int4(W):
+    rows, K = W.shape
+    w = W.astype(np.float32).reshape(rows, K // 128, 128)
+    mn = np.minimum(w.min(-1), np.float32(0))
+    mx = np.maximum(w.max(-1), np.float32(0))
+    s = ((mx - mn) / np.float32(15)).astype(np.float32)
+    bits = s.astype(np.float16).view(np.uint16).copy()
+    bits[(bits & 0x7FFF) == 0] = 1
+    bits[(bits & 0x7FFF) > 0x7BFF] = 0x7BFF
+    sh = bits.view(np.float16)
+    sf = sh.astype(np.float32)
+    z = np.clip(np.rint(-mn / sf), 0, 15).astype(np.float32) + np.float32(0)  # -0 -> +0
+    q = np.clip(np.rint(w / sf[..., None]) + z[..., None], 0, 15).astype(np.uint8)
+    codes = ((q[..., 0::2] << 4) | q[..., 1::2]).reshape(rows, K // 2)
+    return codes, sh, z.astype(np.float16)
+
+
+def test_quantize_int4_matches_numpy_statement(oracle_mod):
+    rng = np.random.default_rng(21)
+    W = (rng.standard_normal((37, 512)) * rng.uniform(0.01, 3.0, (37, 1))).astype(np.float16)
+    W[3, :128] = 0.25          # constant positive group
+    W[4, 128:256] = 0.0        # all-zero group
+    W[5, 256:384] = np.abs(W[5, 256:384])  # positive-only group
+    W[6, :128] = -7.0          # constant negative group
+    W[7, 384:] *= 2000         # large magnitudes
+    got = oracle_mod.quantize_int4(W)
+    want = _np_quantize_int4(W)
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(np.ascontiguousarray(g).view(np.uint8),
+                                      np.ascontiguousarray(w).view(np.uint8))
+
+
+def test_quantize_int4_known_answers(oracle_mod):
+    W = np.full((1, 128), 0.5, np.float16)
+    codes, s, z = oracle_mod.quantize_int4(W)
+    assert codes.tolist() == [[0xFF] * 64] and float(z[0, 0]) == 0.0
+    assert float(s[0, 0]) == float(np.float16(0.5 / 15))
+    codes, s, z = oracle_mod.quantize_int4(np.zeros((1, 128), np.float16))
+    assert not codes.any() and not z.astype(np.float32).any()
+    # ramp -1 .. 1 over one group: scale 2/15, zero rint(7.5) = 8 (ties to even)
+    W = np.linspace(-1, 1, 128, dtype=np.float32).astype(np.float16)[None]
+    codes, s, z = oracle_mod.quantize_int4(W)
+    assert float(z[0, 0]) == 8.0
+    assert codes[0, 0] >> 4 == 0 and codes[0, -1] & 15 == 15
+
+
+def test_quantize_int4_round_trip_error(oracle_mod):
+    rng = np.random.default_rng(22)
+    W = rng.standard_normal((16, 1024)).astype(np.float16)
+    codes, s, z = oracle_mod.quantize_int4(W)
+    q = np.empty((16, 1024), np.float32)
+    q[:, 0::2] = codes >> 4
+    q[:, 1::2] = codes & 15
+    sf = np.repeat(s.astype(np.float32), 128, axis=1)
+    zf = np.repeat(z.astype(np.float32), 128, axis=1)
+    err = np.abs((q - zf) * sf - W.astype(np.float32))
+    # Half a step, except where the fp16-rounded scale pulls an extreme value one
+    # code past 15 (clamped): at most one step.
+    assert np.all(err <= sf * (1 + 1e-3))
+    assert np.mean(err <= 0.5 * sf * (1 + 1e-3) + 1e-6) > 0.99
