@@ -328,6 +328,25 @@ def _secondary(cc, torch, peaks):
         "note": "one batched launch vs 64 clove_gemm_fp16 launches (CUDA graph), L2-resident"}
     del Ab, Bb, Cb
 
+    # swiglu_fused at the Llama-7B FFN shape in the runtime's orientation (tokens x
+    # hidden . hidden x intermediate): one CTA-pair kernel for both projections and
+    # the activation, against two GEMMs + the elementwise pass.
+    T, H, I = 2048, 4096, 11008
+    Xs = torch.randn((T, H), device="cuda").half()
+    Wg = (torch.randn((H, I), device="cuda") / 64).half()
+    Wu = (torch.randn((H, I), device="cuda") / 64).half()
+    Os = torch.empty((T, I), dtype=torch.float16, device="cuda")
+    t_f = timeit(lambda i: cc.swiglu_fused(Xs, Wg, Wu, Os), 1, 20)
+    cc.set_dispatch_override(1, 0, 0)  # tile kernels only: the unfused route
+    t_u = timeit(lambda i: cc.swiglu_fused(Xs, Wg, Wu, Os), 1, 20)
+    cc.set_dispatch_override(0, 0, 0)
+    flop = 4.0 * T * H * I
+    out["swiglu_fused_2048x4096x11008"] = {
+        "kernel": cc.describe_dispatch("swiglu", T, I, H), "us_per_call": round(t_f * 1e6, 2),
+        "TFLOPS": round(flop / t_f / 1e12, 1), "unfused_us": round(t_u * 1e6, 2),
+        "note": "silu(X.W_gate) * (X.W_up), fp16; unfused = two tile-kernel GEMMs + elementwise"}
+    del Xs, Wg, Wu, Os
+
     # config 1 and the square sweep (fp16), int8 square sweep
     for n in (1024, 2048, 4096, 8192):
         A, B = wl.fp16_operands(n, n, n, seed=0)

@@ -37,6 +37,7 @@ SIGNATURES = {
     "clove_debug_int8_acc": ([_P, _P, _P, _I, _I, _I, _I8, _I8, _P], _I),
     "clove_debug_int4_group_acc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
     "clove_quantize_int4": ([_P, _I, _I, _P, _P, _P, _P], _I),
+    "clove_swiglu_fused": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
     "clove_debug_stream_read": ([_P, _SZ, _P, _P], _I),
     "clove_set_dispatch_override": ([_I, _I, _I], _I),
     "clove_set_weight_prefetch": ([_I], _I),

@@ -176,6 +176,25 @@ def debug_int4_group_acc(A_q, A_scale, A_zero, B_q, B_scale, B_zero, stream=None
     return C, G
 
 
+def swiglu_fused(X: torch.Tensor, W_gate: torch.Tensor, W_up: torch.Tensor,
+                 out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out = silu(X @ W_gate) * (X @ W_up): X [T, H], W_gate / W_up [H, I] fp16
+    (activations.cuh:37-46 of the reference, declared there but never defined)."""
+    _need(X, "X", torch.float16, 2)
+    _need(W_gate, "W_gate", torch.float16, 2)
+    _need(W_up, "W_up", torch.float16, 2)
+    T, H = X.shape
+    if W_gate.shape[0] != H or W_up.shape != W_gate.shape:
+        raise ValueError("X [T,H], W_gate and W_up [H,I] disagree")
+    inter = W_gate.shape[1]
+    if out is None:
+        out = torch.empty((T, inter), dtype=torch.float16, device=X.device)
+    _need(out, "out", torch.float16, 2)
+    check(lib().clove_swiglu_fused(_ptr(X), _ptr(W_gate), _ptr(W_up), _ptr(out), T, H, inter,
+                                   _stream(stream)))
+    return out
+
+
 def quantize_int4(W: torch.Tensor, stream=None):
     """Pack fp16 weights W [rows, K] (K % 128 == 0) into the INT4 layout gemm_int4
     reads: (codes [rows, K/2] uint8, scales [rows, K/128] fp16, zeros [rows, K/128] fp16).
@@ -214,7 +233,7 @@ def set_weight_prefetch(enable: bool) -> None:
 
 
 def describe_dispatch(dtype: str, M: int, N: int, K: int) -> str:
-    code = {"fp16": 0, "int8": 1, "int4": 2}[dtype]
+    code = {"fp16": 0, "int8": 1, "int4": 2, "swiglu": 3}[dtype]
     buf = ctypes.create_string_buffer(128)
     check(lib().clove_describe_dispatch(code, M, N, K, buf, len(buf)))
     return buf.value.decode()

@@ -52,6 +52,26 @@ int launch_int8_col_sums(const int8_t* B, int32_t* out, int K, int N, cudaStream
   return check_cuda(cudaGetLastError(), "int8 col sums launch");
 }
 
+// out = silu(g) * u elementwise (the unfused SwiGLU: the reference's swiglu,
+// src/kernels/activations.cu:76-121, with silu(x) = x / (1 + exp(-x)), :9-11).
+__global__ void swiglu_f16_kernel(const __half* __restrict__ g, const __half* __restrict__ u,
+                                  __half* __restrict__ out, long long n) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float x = __half2float(g[i]);
+    out[i] = __float2half_rn(x / (1.0f + expf(-x)) * __half2float(u[i]));
+  }
+}
+
+int launch_swiglu_f16(const void* g, const void* u, void* out, long long n, cudaStream_t stream) {
+  if (n <= 0) return CLOVE_OK;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 65535LL * 8) blocks = 65535LL * 8;
+  swiglu_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const __half*>(g), static_cast<const __half*>(u), static_cast<__half*>(out), n);
+  return check_cuda(cudaGetLastError(), "swiglu launch");
+}
+
 int launch_scale_f16(void* C, long long n, float beta, cudaStream_t stream) {
   const unsigned grid = static_cast<unsigned>((n + 255) / 256);
   kern::scale_f16_kernel<<<grid, 256, 0, stream>>>(static_cast<__half*>(C), n, beta);

@@ -54,11 +54,19 @@ struct Tc2Shape {
   static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
-template <class Op>
+// GLU (fp16 only): C = silu(A . B) * (A . B2) with B = W_gate, B2 = W_up [K,N].
+// The pair's 256 accumulator columns become 128 gate columns (B half loaded by the
+// leader CTA) followed by the same 128 columns of up (loaded by the peer CTA), so
+// one MMA stream computes both projections of a 256 x 128 output tile and the
+// epilogue applies silu(gate) * up before the only store.
+template <class Op, bool GLU = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, EpiParams ep) {
+                    const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC,
+                    int M, int N, int K, EpiParams ep) {
   using S = Tc2Shape<Op>;
+  static_assert(!GLU || !Op::kInt, "GLU epilogue is fp16");
+  constexpr int TILE_N = GLU ? S::BNH : S::BN;  // output columns per pair tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -108,7 +116,7 @@ __global__ void __launch_bounds__(192, 1)
   dev::grid_dependency_wait();
 
   const int tiles_m = (M + 2 * S::BM - 1) / (2 * S::BM);
-  const int tiles_n = (N + S::BN - 1) / S::BN;
+  const int tiles_n = (N + TILE_N - 1) / TILE_N;
   const int num_tiles = tiles_m * tiles_n;
   const int kb_total = (K + S::BK - 1) / S::BK;
   const int pair = static_cast<int>(blockIdx.x >> 1);
@@ -122,7 +130,8 @@ __global__ void __launch_bounds__(192, 1)
         int m_blk, n_blk;
         tile_coords<kPairGroupM>(tile, tiles_m, tiles_n, m_blk, n_blk);
         const int my_m = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
-        const int my_n = n_blk * S::BN + static_cast<int>(rank) * S::BNH;
+        const int my_n = GLU ? n_blk * S::BNH : n_blk * S::BN + static_cast<int>(rank) * S::BNH;
+        const CUtensorMap* my_b = (GLU && rank == 1) ? &tmB2 : &tmB;
         bool ok = true;
         for (int kb = 0; kb < kb_total; ++kb) {
           if (!dev::mbar_wait<true>(&empty[stage], phase ^ 1u, abort_flag)) {
@@ -135,7 +144,7 @@ __global__ void __launch_bounds__(192, 1)
           dev::tma_load_2d_pair(a_dst, &tmA, &full[stage], kb * S::BK, my_m);
 #pragma unroll
           for (int a = 0; a < S::B_ATOMS; ++a)
-            dev::tma_load_2d_pair(b_dst + a * (S::BK * S::B_SW), &tmB, &full[stage],
+            dev::tma_load_2d_pair(b_dst + a * (S::BK * S::B_SW), my_b, &full[stage],
                                   my_n + a * S::B_ATOM_ELEMS, kb * S::BK);
           if (++stage == S::STAGES) {
             stage = 0;
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag))) break;
       dev::tc_fence_after_sync();
       const int m0 = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
-      const int n0 = n_blk * S::BN;
+      const int n0 = n_blk * TILE_N;
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + buf * S::BN;
 
@@ -217,17 +226,28 @@ __global__ void __launch_bounds__(192, 1)
         row_corr = static_cast<int32_t>(0u - static_cast<uint32_t>(ep.zb) *
                                                  static_cast<uint32_t>(ep.row_sum[row]));
 #pragma unroll 1
-      for (int c0 = 0; c0 < S::BN; c0 += S::CHUNK) {
+      for (int c0 = 0; c0 < TILE_N; c0 += S::CHUNK) {
         uint32_t v[S::CHUNK];
 #pragma unroll
         for (int j = 0; j < S::CHUNK; j += 16) {
           uint32_t t[16];
           dev::tmem_ld_x16(t_row + c0 + j, t);
-          dev::tmem_ld_wait();
+          if constexpr (GLU) {
+            uint32_t tu[16];
+            dev::tmem_ld_x16(t_row + S::BNH + c0 + j, tu);  // the same columns of up
+            dev::tmem_ld_wait();
 #pragma unroll
-          for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+            for (int u = 0; u < 16; ++u) {
+              const float g = __uint_as_float(t[u]);
+              v[j + u] = __float_as_uint(g / (1.0f + expf(-g)) * __uint_as_float(tu[u]));
+            }
+          } else {
+            dev::tmem_ld_wait();
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+          }
         }
-        if (c0 + S::CHUNK >= S::BN) {
+        if (c0 + S::CHUNK >= TILE_N) {
           // Accumulator drained: release it to the leader's MMA thread.
           dev::tc_fence_before_sync();
           __syncwarp();

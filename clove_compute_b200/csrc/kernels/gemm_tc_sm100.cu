@@ -198,44 +198,57 @@ namespace clove {
 namespace rt {
 
 namespace {
-std::atomic<uint64_t> g_tc2_attr[2];
+std::atomic<uint64_t> g_tc2_attr[3];
 }
 
 // CTA-pair 256 x 256 tile kernel (fp16 C only).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
-                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream) {
+                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
+                    const void* B2) {
   using SF = kern::Tc2Shape<kern::OpF16>;
   using SI = kern::Tc2Shape<kern::OpI8>;
   const bool f16 = op == kTcF16;
-  const void* fn = f16 ? reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpF16>)
-                       : reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpI8>);
+  const bool glu = B2 != nullptr;
+  if (glu && !f16) return fail(CLOVE_ERR_UNSUPPORTED, "GLU epilogue is fp16 only");
+  const void* fn =
+      glu ? reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpF16, true>)
+          : f16 ? reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpF16>)
+                : reinterpret_cast<const void*>(&kern::gemm_tc2_kernel<kern::OpI8>);
   const int smem = f16 ? SF::SMEM_BYTES : SI::SMEM_BYTES;
   const int bk = f16 ? SF::BK : SI::BK;
   const int b_atom = f16 ? SF::B_ATOM_ELEMS : SI::B_ATOM_ELEMS;
   const int elem = f16 ? 2 : 1;
   const CUtensorMapDataType in_dt =
       f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUtensorMap tmA, tmB, tmC;
+  CUtensorMap tmA, tmB, tmB2, tmC;
   int rc = encode_tmap_2d(&tmA, in_dt, elem, A, K, M, static_cast<uint64_t>(K) * elem, bk, 128, 128);
   if (rc) return rc;
   rc = encode_tmap_2d(&tmB, in_dt, elem, B, N, K, static_cast<uint64_t>(N) * elem, b_atom, bk, 128);
   if (rc) return rc;
+  if (glu) {
+    rc = encode_tmap_2d(&tmB2, in_dt, elem, B2, N, K, static_cast<uint64_t>(N) * elem, b_atom, bk,
+                        128);
+    if (rc) return rc;
+  } else {
+    tmB2 = tmB;
+  }
   rc = encode_tmap_2d(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, N, M,
                       static_cast<uint64_t>(N) * 2, 64, 32, 128);
   if (rc) return rc;
   const uint64_t bit = 1ull << (dev.device & 63);
-  std::atomic<uint64_t>& attr = g_tc2_attr[f16 ? 0 : 1];
+  std::atomic<uint64_t>& attr = g_tc2_attr[glu ? 2 : f16 ? 0 : 1];
   if ((attr.load(std::memory_order_acquire) & bit) == 0) {
     rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                     "cudaFuncSetAttribute(tc2 smem)");
     if (rc) return rc;
     attr.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int tile_n = glu ? 128 : 256;
+  const int tiles = ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
   int pairs = dev.num_sms / 2;
   if (pairs > tiles) pairs = tiles;
   kern::EpiParams epv = ep;
-  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &epv};
+  void* args[] = {&tmA, &tmB, &tmB2, &tmC, &M, &N, &K, &epv};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;

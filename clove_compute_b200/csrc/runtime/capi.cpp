@@ -302,6 +302,49 @@ int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, in
 }
 
 // ---------------------------------------------------------------------------
+// SwiGLU-fused projection (activations.cuh:37-46, declared but not defined in the
+// reference): output = silu(input . W_gate) * (input . W_up).
+// ---------------------------------------------------------------------------
+static bool swiglu_fused_ok(const void* X, const void* Wg, const void* Wu, const void* out, int M,
+                            int N, int K) {
+  const Override ov = get_override();
+  return (ov.path == 0 || ov.path == 4) && M >= 128 && K > 0 && K % 8 == 0 && N % 8 == 0 &&
+         aligned16(X) && aligned16(Wg) && aligned16(Wu) && aligned16(out);
+}
+
+int clove_swiglu_fused(const void* input, const void* W_gate, const void* W_up, void* output,
+                       int batch_seq, int hidden_dim, int intermediate_dim, void* stream) {
+  const int M = batch_seq, K = hidden_dim, N = intermediate_dim;
+  if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
+  if (M == 0 || N == 0) return CLOVE_OK;
+  if (output == nullptr || (K > 0 && (input == nullptr || W_gate == nullptr || W_up == nullptr)))
+    return fail(CLOVE_ERR_INVALID_ARG, "null matrix pointer");
+  DeviceInfo dev;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  cudaStream_t s = as_stream(stream);
+  if (swiglu_fused_ok(input, W_gate, W_up, output, M, N, K)) {
+    kern::EpiParams ep{};
+    ep.mode = kern::kEpiF16AlphaBeta;
+    ep.alpha = 1.f;
+    ep.beta = 0.f;
+    return launch_gemm_tc2(kTcF16, input, W_gate, output, M, N, K, ep, dev, s, W_up);
+  }
+  // Unfused: both projections into stream-ordered scratch, then the elementwise op.
+  const size_t n = static_cast<size_t>(M) * N;
+  void* scratch = nullptr;
+  rc = check_cuda(cudaMallocAsync(&scratch, 2 * n * sizeof(__half), s), "cudaMallocAsync(swiglu)");
+  if (rc) return rc;
+  __half* g = static_cast<__half*>(scratch);
+  __half* u = g + n;
+  rc = gemm_fp16_impl(input, W_gate, g, M, N, K, 1.f, 0.f, s, nullptr);
+  if (!rc) rc = gemm_fp16_impl(input, W_up, u, M, N, K, 1.f, 0.f, s, nullptr);
+  if (!rc) rc = launch_swiglu_f16(g, u, output, static_cast<long long>(n), s);
+  const int rc2 = check_cuda(cudaFreeAsync(scratch, s), "cudaFreeAsync(swiglu)");
+  return rc ? rc : rc2;
+}
+
+// ---------------------------------------------------------------------------
 // INT8
 // ---------------------------------------------------------------------------
 // mode: 1 per-tensor, 2 row/col, 3 raw int32 accumulators.
@@ -501,6 +544,13 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
   int bn = 0, split = 0;
   if (M <= 0 || N <= 0) {
     name = "noop";
+  } else if (dtype == 3) {
+    // Projection shapes only (alignment is the caller's): fused unless M < 128 or
+    // K, N are not multiples of 8.
+    const Override ovs = get_override();
+    const bool fused = (ovs.path == 0 || ovs.path == 4) && M >= 128 && K > 0 && K % 8 == 0 &&
+                       N % 8 == 0;
+    name = fused ? "tc2_swiglu" : "unfused_swiglu";
   } else if (dtype == 0) {
     const bool gemv = N <= 8 && K % 8 == 0 && gemv_f16_smem(N, K) <= 200 * 1024;
     const bool tc = K % 8 == 0 && N % 8 == 0 && K > 0;

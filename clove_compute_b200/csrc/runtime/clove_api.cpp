@@ -49,4 +49,11 @@ void gemm_fp16_batched(const half* A, const half* B, half* C, int batch, int M, 
                "gemm_fp16_batched");
 }
 
+void swiglu_fused(const half* input, const half* W_gate, const half* W_up, half* output,
+                  int batch_seq, int hidden_dim, int intermediate_dim, cudaStream_t stream) {
+  die_on_error(clove_swiglu_fused(input, W_gate, W_up, output, batch_seq, hidden_dim,
+                                  intermediate_dim, stream),
+               "swiglu_fused");
+}
+
 }  // namespace clove

@@ -63,8 +63,10 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
                    const DeviceInfo& dev, cudaStream_t stream, int batch = 1);
 // CTA-pair kernel: 256 x 256 tiles on two SMs (fp16 C).
+// B2 != nullptr: fp16 GLU, C = silu(A . B) * (A . B2) (256 x 128 output tiles).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
-                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream);
+                    const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
+                    const void* B2 = nullptr);
 // True when (op, bn, split, out_bytes) is an instantiated kernel.
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();
@@ -86,6 +88,9 @@ int read_clear_error_gemv();
 // of one launch of that size.
 int launch_stream_read(const void* src, size_t nbytes, uint32_t* out, const DeviceInfo& dev,
                        cudaStream_t stream);
+
+// out = silu(g) * u over n fp16 elements (kernels/fallback_simt.cu).
+int launch_swiglu_f16(const void* g, const void* u, void* out, long long n, cudaStream_t stream);
 
 // ---- INT4 packing tool (kernels/quant_int4.cu)
 int launch_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,

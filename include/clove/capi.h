@@ -64,6 +64,16 @@ int clove_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, 
 int clove_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N,
                             int K, float alpha, float beta, void* stream);
 
+/* SwiGLU-fused projection, the reference's declared-only clove::swiglu_fused
+ * (include/clove/kernels/activations.cuh:37-46): input [batch_seq, hidden],
+ * W_gate / W_up [hidden, intermediate], output [batch_seq, intermediate] =
+ * silu(input . W_gate) * (input . W_up), silu(x) = x / (1 + exp(-x)) in fp32 on
+ * the fp32 accumulators. One CTA-pair kernel computes both projections of each
+ * 256 x 128 output tile (batch_seq >= 128, hidden and intermediate multiples of 8,
+ * 16-byte aligned pointers); other shapes run two GEMMs and an elementwise pass. */
+int clove_swiglu_fused(const void* input, const void* W_gate, const void* W_up, void* output,
+                       int batch_seq, int hidden_dim, int intermediate_dim, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* INT8 (reference signature): C = half( sum_k (A-A_zero)(B-B_zero) * A_scale*B_scale ) */
 /* A_q [M,K] int8, B_q [K,N] int8, C [M,N] binary16; int32 accumulation.        */
@@ -147,7 +157,7 @@ int clove_set_dispatch_override(int path, int bn, int split);
 int clove_set_weight_prefetch(int enable);
 
 /* Describes the kernel the automatic dispatch picks for a shape:
- * dtype 0 = fp16, 1 = int8, 2 = int4. Writes a short name into buf. */
+ * dtype 0 = fp16, 1 = int8, 2 = int4, 3 = swiglu_fused. Writes a short name into buf. */
 int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t buflen);
 
 /* ------------------------------------------------------------------------- */

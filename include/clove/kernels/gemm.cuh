@@ -46,4 +46,11 @@ void gemm_int4(const uint8_t* A_q, const half* A_scale, const half* A_zero, cons
 void gemm_fp16_batched(const half* A, const half* B, half* C, int batch, int M, int N, int K,
                        float alpha = 1.0f, float beta = 0.0f, cudaStream_t stream = 0);
 
+// The reference declares swiglu_fused in include/clove/kernels/activations.cuh:37-46
+// (with `stream = 0`) and never defines it; this library defines it (one CTA-pair
+// GEMM computing both projections, silu(gate) * up in the epilogue). Declared here
+// without a default argument so that both headers can be included together.
+void swiglu_fused(const half* input, const half* W_gate, const half* W_up, half* output,
+                  int batch_seq, int hidden_dim, int intermediate_dim, cudaStream_t stream);
+
 }  // namespace clove

@@ -49,6 +49,7 @@ _SIGS = {
     "clove_oracle_gemm_int4": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
     "clove_oracle_gemm_int4_refcompat": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
     "clove_oracle_quantize_int4": ([_P, _I, _I, _P, _P, _P], None),
+    "clove_oracle_swiglu": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
 }
 
 
@@ -225,3 +226,19 @@ def quantize_int4(W):
     lib().clove_oracle_quantize_int4(_ptr(W.view(np.uint16)), rows, K, _ptr(codes), _ptr(scales),
                                      _ptr(zeros))
     return codes, scales.view(np.float16), zeros.view(np.float16)
+
+
+def swiglu(X, Wg, Wu, rows=None, nthreads=0):
+    """half(silu(X@Wg) * (X@Wu)) with fp32 accumulation (reference silu_f)."""
+    X = np.ascontiguousarray(X, np.float16)
+    Wg = np.ascontiguousarray(Wg, np.float16)
+    Wu = np.ascontiguousarray(Wu, np.float16)
+    M, K = X.shape
+    assert Wg.shape == Wu.shape and Wg.shape[0] == K
+    N = Wg.shape[1]
+    out = np.zeros((M, N), np.float16)
+    r0, r1 = _rows(M, rows)
+    lib().clove_oracle_swiglu(_ptr(X.view(np.uint16)), _ptr(Wg.view(np.uint16)),
+                              _ptr(Wu.view(np.uint16)), _ptr(out.view(np.uint16)), M, N, K, r0, r1,
+                              nthreads)
+    return out

@@ -427,3 +427,49 @@ void clove_oracle_quantize_int4(const uint16_t* W, int rows, int K, uint8_t* cod
         }
     }
 }
+
+/* ------------------------------------------------------------------------- */
+/* SwiGLU projection: out = half(silu(g) * u), g = X.Wg, u = X.Wu in fp32       */
+/* (k ascending), silu(x) = x / (1 + expf(-x)) as the reference's silu_f       */
+/* (src/kernels/activations.cu:9-11) applied by its swiglu kernel (:76-121) -- */
+/* here on the fp32 accumulators, which is what clove_swiglu_fused fuses       */
+/* (the reference declares swiglu_fused, activations.cuh:37-46, and never      */
+/* defines it).                                                               */
+/* ------------------------------------------------------------------------- */
+void clove_oracle_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* Wu, uint16_t* out,
+                         int M, int N, int K, int row_begin, int row_end, int nthreads) {
+    if (row_end > M) row_end = M;
+    if (row_begin < 0) row_begin = 0;
+    if (row_end <= row_begin || N <= 0) return;
+    int nt = resolve_threads(nthreads);
+    float* Wgf = (float*)malloc(sizeof(float) * (size_t)K * N + 1);
+    float* Wuf = (float*)malloc(sizeof(float) * (size_t)K * N + 1);
+    for (int64_t i = 0; i < (int64_t)K * N; i++) {
+        Wgf[i] = clove_oracle_h2f(Wg[i]);
+        Wuf[i] = clove_oracle_h2f(Wu[i]);
+    }
+#pragma omp parallel num_threads(nt)
+    {
+        float* g = (float*)malloc(sizeof(float) * (size_t)N);
+        float* u = (float*)malloc(sizeof(float) * (size_t)N);
+#pragma omp for schedule(dynamic, 1)
+        for (int m = row_begin; m < row_end; m++) {
+            for (int n = 0; n < N; n++) g[n] = u[n] = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const float a = clove_oracle_h2f(X[(int64_t)m * K + k]);
+                const float* bg = Wgf + (int64_t)k * N;
+                const float* bu = Wuf + (int64_t)k * N;
+                for (int n = 0; n < N; n++) {
+                    g[n] += a * bg[n];
+                    u[n] += a * bu[n];
+                }
+            }
+            for (int n = 0; n < N; n++)
+                out[(int64_t)m * N + n] = clove_oracle_f2h(g[n] / (1.0f + expf(-g[n])) * u[n]);
+        }
+        free(g);
+        free(u);
+    }
+    free(Wgf);
+    free(Wuf);
+}

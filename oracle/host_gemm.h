@@ -100,6 +100,12 @@ void clove_oracle_gemm_int4_refcompat(const uint8_t* Aq, const uint16_t* As,
                                       uint16_t* C, int M, int N, int K,
                                       int row_begin, int row_end, int nthreads);
 
+/* SwiGLU projection: out[m,n] = half(silu(g)*u), g = X.Wg, u = X.Wu (fp32, k
+ * ascending), silu(x) = x/(1+expf(-x)) (reference activations.cu:9-11,76-121).
+ * X [M,K], Wg/Wu [K,N], out [M,N] binary16; rows [row_begin,row_end) only. */
+void clove_oracle_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* Wu, uint16_t* out,
+                         int M, int N, int K, int row_begin, int row_end, int nthreads);
+
 /* INT4 packing tool (this build's specification; the reference has none):
  * W [rows,K] binary16, K % 128 == 0 -> codes [rows,K/2] (element 2j in the high
  * nibble of byte j), scales / zeros [rows,K/128] binary16. Asymmetric min/max per

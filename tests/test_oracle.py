@@ -317,3 +317,18 @@ def test_quantize_int4_round_trip_error(oracle_mod):
     # code past 15 (clamped): at most one step.
     assert np.all(err <= sf * (1 + 1e-3))
     assert np.mean(err <= 0.5 * sf * (1 + 1e-3) + 1e-6) > 0.99
+
+
+def test_swiglu_matches_float64(oracle_mod):
+    rng = np.random.default_rng(31)
+    X = rng.standard_normal((9, 256)).astype(np.float16)
+    Wg = (rng.standard_normal((256, 40)) / 16).astype(np.float16)
+    Wu = (rng.standard_normal((256, 40)) / 16).astype(np.float16)
+    out = oracle_mod.swiglu(X, Wg, Wu).astype(np.float64)
+    g = X.astype(np.float64) @ Wg.astype(np.float64)
+    u = X.astype(np.float64) @ Wu.astype(np.float64)
+    ref = g / (1 + np.exp(-g)) * u
+    assert np.linalg.norm(out - ref) / np.linalg.norm(ref) < 1e-3
+    part = oracle_mod.swiglu(X, Wg, Wu, rows=(2, 5))
+    np.testing.assert_array_equal(part[2:5], oracle_mod.swiglu(X, Wg, Wu)[2:5])
+    assert not part[:2].any() and not part[5:].any()
