@@ -55,3 +55,31 @@ def test_dispatch_description_without_gpu(clove_lib):
     assert clove_lib.describe_dispatch("int4", 4096, 1, 4096).startswith("gemv_int4")
     assert clove_lib.describe_dispatch("int8", 4096, 32, 4096).startswith("tc_int8")
     assert "split" in clove_lib.describe_dispatch("int8", 4096, 32, 4096)
+
+
+def test_swiglu_dispatch_without_gpu(clove_lib):
+    assert clove_lib.describe_dispatch("swiglu", 2048, 11008, 4096).startswith("tc2_swiglu")
+    assert clove_lib.describe_dispatch("swiglu", 64, 11008, 4096).startswith("unfused")
+    assert clove_lib.describe_dispatch("swiglu", 2048, 11008, 4100).startswith("unfused")
+
+
+def test_split_k_clusters_are_powers_of_two(clove_lib):
+    # A split tile's 128 rows are dealt out evenly over the cluster: 2, 4 or 8 CTAs.
+    for M, N, K in [(4096, 32, 4096), (256, 96, 4096), (128, 64, 8192), (384, 64, 4096)]:
+        d = clove_lib.describe_dispatch("int8", M, N, K)
+        split = int(d.split("split=")[1].split()[0])
+        assert split in (1, 2, 4, 8), d
+
+
+def test_host_argument_checks_need_no_gpu(clove_lib):
+    """Argument errors are reported before any device work."""
+    lib = clove_lib.lib()
+    # K not a multiple of the 128-element group
+    assert lib.clove_quantize_int4(None, 4, 200, None, None, None, None) == clove_lib.CLOVE_ERR_INVALID_ARG
+    assert lib.clove_quantize_int4(None, -1, 128, None, None, None, None) == clove_lib.CLOVE_ERR_INVALID_ARG
+    assert lib.clove_swiglu_fused(None, None, None, None, -1, 8, 8, None) == clove_lib.CLOVE_ERR_INVALID_ARG
+    assert lib.clove_gemm_fp16_batched(None, None, None, -2, 8, 8, 8, 1.0, 0.0, None) == \
+        clove_lib.CLOVE_ERR_INVALID_ARG
+    # empty problems are no-ops
+    assert lib.clove_swiglu_fused(None, None, None, None, 0, 8, 8, None) == clove_lib.CLOVE_OK
+    assert lib.clove_quantize_int4(None, 0, 128, None, None, None, None) == clove_lib.CLOVE_OK
