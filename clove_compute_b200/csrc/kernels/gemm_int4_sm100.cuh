@@ -7,29 +7,30 @@
 //   G[m,n,g] = sum_{k in g} (a - zA)(b - zB)   exact in int32.
 //
 // One CTA computes a 128 x 128 tile of C; K advances one group (128 codes,
-// 64 packed bytes) at a time. 14 warps:
+// 64 packed bytes) at a time. 18 warps:
 //   warp 0      TMA producer: packed A / B boxes [128 rows x 64 B] (64B swizzle)
 //               into a 4-deep ring; every 8 groups, boxes [128 rows x 8 groups] of
 //               A/B scales and zero points into a 2-slot ring.
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
-//               group into one of two int32 TMEM buffers (a fresh accumulator per
+//               group into one of four int32 TMEM buffers (a fresh accumulator per
 //               group), so every G leaves the tensor core exact.
-//   warps 2-5   transform: thread t unpacks row t of the A and of the B tile into
-//               a 128B-swizzled u8 stage (the MMA operand) holding the biased codes
-//               a'' = a - zA + 16 and b'' = b - zB + 16, both in [1, 31], formed with
-//               plain adds (no per-byte carries). Within a group both operands use
-//               the same K order (the high nibbles of a 4-byte word, then its low
-//               nibbles), which leaves the dot product unchanged. Per row they also
-//               sum the codes: with R = sum(a - zA), Cc = sum(b - zB),
+//   warps 2-9   transform: warps 2-5 unpack row t of the A tile, warps 6-9 row t of
+//               the B tile, into a 128B-swizzled u8 stage (the MMA operand) holding
+//               the biased codes a'' = a - zA + 16 and b'' = b - zB + 16, both in
+//               [1, 31], formed with plain adds (no per-byte carries). Within a
+//               group both operands use the same K order (the high nibbles of a
+//               4-byte word, then its low nibbles), which leaves the dot product
+//               unchanged. Per row they also sum the codes: with R = sum(a - zA),
+//               Cc = sum(b - zB),
 //                 G = D - 16 R - 16 Cc - 32768,   D = sum a'' b''  (u8 x u8 MMA).
 //               They publish, per group, the B scales (fp32), 16 Cc per column and
 //               0x4B400000 - 16 R - 32768 per row.
-//   warps 6-13  epilogue: two warps per TMEM lane quarter, 64 columns each. One
-//               3-input integer add turns D into the fp32 bit pattern of
-//               12582912 + G (exact: |G| < 2^22), one subtraction gives float(G);
-//               acc += float(G) * (sA * sB) with packed fp32x2 math, in registers,
-//               while the tensor core computes the next group; finally fp16 through
-//               swizzled smem and a TMA store.
+//   warps 10-17 epilogue: two warps per TMEM lane quarter, 64 columns each, read
+//               16 columns at a time. One 3-input integer add turns D into the fp32
+//               bit pattern of 12582912 + G (exact: |G| < 2^22), one subtraction
+//               gives float(G); acc += float(G) * (sA * sB) with packed fp32x2
+//               math, in registers, while the tensor core computes the next group;
+//               finally fp16 through swizzled smem and a TMA store.
 // Zero points must be integer codes in [0, 15].
 #pragma once
 
@@ -55,7 +56,7 @@ struct I4Shape {
   static constexpr int META_SLOTS = 2;
   static constexpr int SBF_BYTES = SB_SLOTS * 3 * BN * 4;  // per slot: B scales, col/row terms
   static constexpr int EPI_BYTES = 8 * 4096;          // 8 warps x 32 rows x 128 B
-  static constexpr int THREADS = 14 * 32;
+  static constexpr int THREADS = 18 * 32;
   static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int OFF_UN = 0;                                      // 1024-aligned
   static constexpr int OFF_PK = OFF_UN + UN_STAGES * UN_BYTES;
@@ -116,10 +117,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S::PK_STAGES; ++i) {
       dev::mbar_init(&pk_full[i], 1);
-      dev::mbar_init(&pk_empty[i], 4);
+      dev::mbar_init(&pk_empty[i], 8);
     }
     for (int i = 0; i < S::UN_STAGES; ++i) {
-      dev::mbar_init(&un_full[i], 4);
+      dev::mbar_init(&un_full[i], 8);
       dev::mbar_init(&un_empty[i], 1);
     }
     for (int i = 0; i < S::ACC_BUFS; ++i) {
@@ -127,12 +128,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       dev::mbar_init(&acc_empty[i], 8);
     }
     for (int i = 0; i < S::SB_SLOTS; ++i) {
-      dev::mbar_init(&sb_full[i], 4);
+      dev::mbar_init(&sb_full[i], 8);
       dev::mbar_init(&sb_empty[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
       dev::mbar_init(&meta_full[i], 1);
-      dev::mbar_init(&meta_empty[i], 12);
+      dev::mbar_init(&meta_empty[i], 16);
     }
     *abort_flag = 0;
     dev::fence_mbarrier_init();
@@ -222,9 +223,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ transform
-    const int t = static_cast<int>((warp - 2) * 32 + lane);  // row of the A and B tiles
+    const int t = static_cast<int>(((warp - 2) & 3) * 32 + lane);  // row of the A or B tile
+    const int opw = static_cast<int>(warp - 2) >> 2;                 // 0: A rows, 1: B rows
     for (int g = 0; g < NG; ++g) {
       const int c = g >> 3;
       const int mslot = c & 1;
@@ -243,15 +245,16 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const __half* meta_bs = reinterpret_cast<const __half*>(mt + 2 * S::META_BOX);
       const __half* meta_bz = reinterpret_cast<const __half*>(mt + 3 * S::META_BOX);
       const int gi = g & 7;
-      const int za = __half2int_rn(meta_az[t * 8 + gi]);
-      const int zb = __half2int_rn(meta_bz[t * 8 + gi]);
+      const int za = opw == 0 ? __half2int_rn(meta_az[t * 8 + gi]) : 0;
+      const int zb = opw == 1 ? __half2int_rn(meta_bz[t * 8 + gi]) : 0;
       float* slot = sbf + sbs * 3 * S::BN;  // [B scale][16 Cc][row term]
-      slot[t] = __half2float(meta_bs[t * 8 + gi]);
+      if (opw == 1) slot[t] = __half2float(meta_bs[t * 8 + gi]);
 
       const uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
       uint8_t* un = smem + S::OFF_UN + u * S::UN_BYTES;
 #pragma unroll
       for (int op = 0; op < 2; ++op) {
+        if (op != opw) continue;  // warp-uniform: this warp transforms one operand
         const uint8_t* src = pk + op * S::PK_A + t * 64;                 // 64B-swizzled packed row
         const uint32_t dst = dev::smem_u32(un + op * S::UN_A + t * 128);  // 128B-swizzled row
         const int z = op == 0 ? za : zb;
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t q = warp & 3u;
-    const int h = static_cast<int>(warp - 6) >> 2;  // column half of the tile
+    const int h = static_cast<int>(warp - 10) >> 2;  // column half of the tile
     const int row = static_cast<int>(q * 32 + lane);
     float2 acc[32];
 #pragma unroll
@@ -322,35 +325,34 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + static_cast<uint32_t>(b) * S::BN + h * 64;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t v0[16], v1[16];
-        dev::tmem_ld_x16(taddr + half * 32, v0);
-        dev::tmem_ld_x16(taddr + half * 32 + 16, v1);
+      for (int qc = 0; qc < 4; ++qc) {  // 16 columns at a time (register budget)
+        uint32_t vv[16];
+        dev::tmem_ld_x16(taddr + qc * 16, vv);
         dev::tmem_ld_wait();
-        if (half == 1) {
+        if (qc == 3) {
           dev::tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) dev::mbar_arrive(&acc_empty[b]);
         }
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 s4 = *reinterpret_cast<const float4*>(sb + half * 32 + j);
-          const int4 c4 = *reinterpret_cast<const int4*>(colt + half * 32 + j);
-          const uint32_t* vv = j < 16 ? &v0[j] : &v1[j - 16];
+        for (int j = 0; j < 16; j += 4) {
+          const int col = qc * 16 + j;  // column within this warp's 64
+          const float4 s4 = *reinterpret_cast<const float4*>(sb + col);
+          const int4 c4 = *reinterpret_cast<const int4*>(colt + col);
           // fp32 bit patterns of 12582912 + G: one 3-input add each.
-          const int f0 = static_cast<int>(vv[0]) + rowt - c4.x;
-          const int f1 = static_cast<int>(vv[1]) + rowt - c4.y;
-          const int f2 = static_cast<int>(vv[2]) + rowt - c4.z;
-          const int f3 = static_cast<int>(vv[3]) + rowt - c4.w;
+          const int f0 = static_cast<int>(vv[j + 0]) + rowt - c4.x;
+          const int f1 = static_cast<int>(vv[j + 1]) + rowt - c4.y;
+          const int f2 = static_cast<int>(vv[j + 2]) + rowt - c4.z;
+          const int f3 = static_cast<int>(vv[j + 3]) + rowt - c4.w;
           const float2 g01 = __fadd2_rn(make_float2(__int_as_float(f0), __int_as_float(f1)), neg_magic);
           const float2 g23 = __fadd2_rn(make_float2(__int_as_float(f2), __int_as_float(f3)), neg_magic);
           const float2 s01 = __fmul2_rn(sa2, make_float2(s4.x, s4.y));
           const float2 s23 = __fmul2_rn(sa2, make_float2(s4.z, s4.w));
-          const int a = (half * 32 + j) >> 1;
+          const int a = col >> 1;
           acc[a] = __ffma2_rn(g01, s01, acc[a]);
           acc[a + 1] = __ffma2_rn(g23, s23, acc[a + 1]);
           if (DBG && m0 + row < M) {  // test hook: exact group accumulators
-            const int nb = n0 + h * 64 + half * 32 + j;
+            const int nb = n0 + h * 64 + col;
             const int fs[4] = {f0, f1, f2, f3};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -361,14 +363,14 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) {
-        if (warp == 6 && g < 32) CLOVE_TRACE_POINT(128 + g);
+        if (warp == 10 && g < 32) CLOVE_TRACE_POINT(128 + g);
         dev::mbar_arrive(&sb_empty[sbs]);
         if ((g & 7) == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
       }
     }
     if (ok) {
       // fp16 into a 128B-swizzled staging tile, one TMA store per warp.
-      uint8_t* stg = smem + S::OFF_EPI + (warp - 6) * 4096;
+      uint8_t* stg = smem + S::OFF_EPI + (warp - 10) * 4096;
       const uint32_t sa_ = dev::smem_u32(stg);
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
