@@ -239,6 +239,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       ok = ok && dev::mbar_wait(&un_empty[u], (static_cast<uint32_t>(g / S::UN_STAGES) & 1u) ^ 1u, abort_flag);
       ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g / S::SB_SLOTS) & 1u) ^ 1u, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
+      if (warp == 2 && lane == 0 && g < 32) CLOVE_TRACE_POINT(192 + g);
 
       const uint8_t* mt = smem + S::OFF_META + mslot * S::META_BYTES;
       const __half* meta_az = reinterpret_cast<const __half*>(mt + 1 * S::META_BOX);
@@ -314,6 +315,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g / S::SB_SLOTS) & 1u, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
+      if (warp == 10 && lane == 0 && g < 32) CLOVE_TRACE_POINT(224 + g);
       dev::tc_fence_after_sync();
       const __half* meta_as = reinterpret_cast<const __half*>(smem + S::OFF_META + mslot * S::META_BYTES);
       const float sa = __half2float(meta_as[row * 8 + (g & 7)]);
