@@ -91,8 +91,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
                         int32_t* __restrict__ Gdbg) {
   using S = I4Shape;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = dev::align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   uint64_t* pk_full = bars;                        // [4]
   uint64_t* pk_empty = bars + 4;                   // [4]
@@ -326,11 +325,21 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const float2 sa2 = make_float2(sa, sa);
       const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
       const uint32_t taddr = tmem_base + ((q * 32u) << 16) + static_cast<uint32_t>(b) * S::BN + h * 64;
+#ifdef CLOVE_TRACE
+      long long t_e0 = clock64();
+#endif
 #pragma unroll
       for (int qc = 0; qc < 4; ++qc) {  // 16 columns at a time (register budget)
         uint32_t vv[16];
+#ifdef CLOVE_TRACE
+        long long t_ld0 = clock64();
+#endif
         dev::tmem_ld_x16(taddr + qc * 16, vv);
         dev::tmem_ld_wait();
+#ifdef CLOVE_TRACE
+        if (warp == 10 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
+          g_clove_trace[40 + qc] = static_cast<unsigned long long>(clock64() - t_ld0 + (vv[0] & 0));
+#endif
         if (qc == 3) {
           dev::tc_fence_before_sync();
           __syncwarp();
@@ -363,6 +372,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
           }
         }
       }
+#ifdef CLOVE_TRACE
+      if (warp == 10 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
+        g_clove_trace[44] = static_cast<unsigned long long>(clock64() - t_e0 + (acc[0].x == 1.5f));
+#endif
       __syncwarp();
       if (lane == 0) {
         if (warp == 10 && g < 32) CLOVE_TRACE_POINT(128 + g);

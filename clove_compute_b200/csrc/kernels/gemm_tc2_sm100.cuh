@@ -68,8 +68,7 @@ __global__ void __launch_bounds__(192, 1)
   static_assert(!GLU || !Op::kInt, "GLU epilogue is fp16");
   constexpr int TILE_N = GLU ? S::BNH : S::BN;  // output columns per pair tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = dev::align_smem_1024(smem_raw);
   uint8_t* stage_base = smem;
   uint8_t* epi_base = smem + S::STAGES * S::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_base + S::EPI_BYTES);

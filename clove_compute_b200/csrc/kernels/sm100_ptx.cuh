@@ -40,6 +40,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// First 1024-byte aligned byte of the dynamic shared memory array. Indexing the
+// array (rather than rounding its address as an integer) keeps the pointer in the
+// shared state space, so plain C++ loads through it compile to shared-memory loads
+// instead of generic ones.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem_raw) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  return smem_raw + ((1024u - (a & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint32_t warp_idx() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_idx() { return threadIdx.x & 31; }
 
