@@ -225,9 +225,10 @@ def _secondary(cc, torch, peaks):
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
     stream = torch.cuda.current_stream()
 
-    def timeit(fn, n_copies, reps, warm=3):
-        """Seconds per call: the n_copies rotating calls are captured once in a CUDA
-        graph and replayed, so host launch overhead does not pace the GPU."""
+    def timeit(fn, n_copies, reps, warm=3, repeats=5):
+        """Seconds per call, the median of `repeats` timed batches: the n_copies
+        rotating calls are captured once in a CUDA graph and replayed, so host launch
+        overhead does not pace the GPU."""
         for i in range(max(warm, n_copies)):
             fn(i % n_copies)
         torch.cuda.synchronize()
@@ -237,15 +238,18 @@ def _secondary(cc, torch, peaks):
                 fn(i)
         g.replay()
         torch.cuda.synchronize()
-        n_rep = max(2, reps // n_copies)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n_rep):
-            g.replay()
-        e1.record(stream)
-        e1.synchronize()
+        n_rep = max(2, reps // (n_copies * repeats))
+        times = []
+        for _ in range(repeats):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n_rep):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) / (n_rep * n_copies) * 1e-3)
         del g
-        return e0.elapsed_time(e1) / (n_rep * n_copies) * 1e-3  # seconds per call
+        return statistics.median(times)  # seconds per call
 
     # config 2: int4 decode GEMV, 4096x4096 weights, N = 1
     M, N, K = 4096, 1, 4096
