@@ -103,6 +103,31 @@ int gemv_int4_ws2(const uint8_t* Aq, const void* As, const void* Az, const uint8
       "gemv_int4_ws2 launch");
 }
 
+template <int NC, int PW>
+int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                  const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
+                  long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
+  int grid = dev.num_sms;
+  if (rows < grid * 8) grid = (rows + 7) / 8;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kern::kLdgThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int early = weight_prefetch_enabled() ? 1 : 0;
+  return check_cuda(
+      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, 8>, Aq,
+                         static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
+                         static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
+                         static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),
+      "gemv_int4_ldg launch");
+}
+
 template <int NC, int P>
 int gemv_int4_reg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                   const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int K,
@@ -195,17 +220,26 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
   // Register-resident B when this lane's share of the vectors fits (nc * P <= 8,
   // P = 1024-element windows per row) and the 16-byte B loads are aligned.
   const int P = (K + 1023) / 1024;
-  // Warp-specialised bulk-copy kernel: whole 1024-element windows, 16-byte aligned
-  // rows of codes, scales and zero points (K % 1024 == 0), no debug output.
+  // Whole 1024-element windows, 16-byte aligned rows of codes, scales and zero
+  // points (K % 1024 == 0), no debug output.
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (Gdbg == nullptr && K % 1024 == 0 && K <= 24576 && nc * P <= 8 && a16(Aq) && a16(As) &&
       a16(Az) && a16(Bq) && !ws_disabled()) {
     const int PW = (P + kern::kWs2WindowGroups - 1) / kern::kWs2WindowGroups;
+    // Direct 128-bit loads (gemv_int4_ldg_kernel); the bulk-copy ring variant
+    // (gemv_int4_ws2_kernel) stays reachable through the test override.
+    if (ws2_selected()) {
 #define WS2(n, pw)                                                                            \
   if (nc == n && PW == pw)                                                                     \
     return gemv_int4_ws2<n, pw>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
-    WS2(1, 1) WS2(1, 2) WS2(2, 1)
+      WS2(1, 1) WS2(1, 2) WS2(2, 1)
 #undef WS2
+    }
+#define LDG(n, pw)                                                                            \
+  if (nc == n && PW == pw)                                                                     \
+    return gemv_int4_ldg<n, pw>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
+    LDG(1, 1) LDG(1, 2) LDG(2, 1)
+#undef LDG
   }
   if (nc * P <= 8 && (reinterpret_cast<uintptr_t>(Bq) & 15u) == 0) {
 #define REG(n, p)                                                                          \

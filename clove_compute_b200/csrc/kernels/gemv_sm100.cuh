@@ -541,6 +541,161 @@ __global__ void __launch_bounds__(kWs2Threads, 2)
 #endif
 }
 
+// INT4 decode with direct 128-bit loads (no shared-memory ring): the consumer
+// decomposition of gemv_int4_ws2_kernel -- warp w = 4 * rg + wg takes rows
+// rg, rg + 4, ... of the CTA's block and the 1024-element windows wg, wg + 4, ...
+// of each -- but every lane loads its own 16-byte chunks of up to RMAX rows with
+// ld.global.nc straight into registers, all issued before any math, like a bare
+// streaming read. With weights_early those loads are issued before
+// griddepcontrol.wait. The RMAX row partials of a warp are reduced by one
+// transposed butterfly (lane 4i ends with row i), the four window partials of a
+// row are added in fixed order through shared memory.
+constexpr int kLdgRowGroups = 4;
+constexpr int kLdgWindowGroups = 4;
+constexpr int kLdgThreads = kLdgRowGroups * kLdgWindowGroups * 32;
+
+template <int NC, int PW, int RMAX>
+__global__ void __launch_bounds__(kLdgThreads, 1)
+    gemv_int4_ldg_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
+                         const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
+                         const __half* __restrict__ Bs, const __half* __restrict__ Bz,
+                         __half* __restrict__ C, int rows, int K, long long ldc_row,
+                         long long ldc_col, int weights_early) {
+  static_assert(RMAX == 8, "the transposed butterfly reduces 8 row partials");
+  constexpr int ROWS = kLdgRowGroups * RMAX;  // rows of the block per round
+  __shared__ float part[ROWS][kLdgWindowGroups][NC];
+  const int NG = K >> 7;
+  const int P = K >> 10;
+  const int KB = K >> 1;
+  const int warp = static_cast<int>(dev::warp_idx());
+  const int lane = static_cast<int>(dev::lane_idx());
+  const int rg = warp >> 2;
+  const int wg = warp & 3;
+  const int per_cta = (rows + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * per_cta;
+  const int nrows = max(0, min(rows, r0 + per_cta) - r0);
+
+  dev::allow_dependent_launch();
+  if (!weights_early) dev::grid_dependency_wait();
+
+  uint4 a[RMAX][PW];
+  __half2 zs[RMAX][PW];
+  auto load_round = [&](int base) {
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+      const int rl = base + rg + kLdgRowGroups * i;
+#pragma unroll
+      for (int pw = 0; pw < PW; ++pw) {
+        const int p = wg + kLdgWindowGroups * pw;
+        if (rl < nrows && p < P) {
+          const size_t m = static_cast<size_t>(r0 + rl);
+          const int ch = p * 32 + lane;
+          a[i][pw] = dev::ld_nc_v4(Aq + m * KB + static_cast<size_t>(ch) * 16);
+          const size_t gi = m * NG + (ch >> 2);
+          zs[i][pw] = __halves2half2(Az[gi], As[gi]);
+        } else {
+          a[i][pw] = make_uint4(0u, 0u, 0u, 0u);
+          zs[i][pw] = __halves2half2(__float2half(0.f), __float2half(0.f));
+        }
+      }
+    }
+  };
+  load_round(0);
+  if (weights_early) dev::grid_dependency_wait();  // B and C may belong to the previous kernel
+
+  uint32_t bw[NC][PW][8];
+  int bsum[NC][PW];
+  float bsc[NC][PW];
+#pragma unroll
+  for (int n = 0; n < NC; ++n)
+#pragma unroll
+    for (int pw = 0; pw < PW; ++pw) {
+      const int p = wg + kLdgWindowGroups * pw;
+      const int ch = p * 32 + lane;
+      uint4 q = make_uint4(0u, 0u, 0u, 0u);
+      int zb = 0;
+      bsc[n][pw] = 0.f;
+      if (p < P) {
+        q = *reinterpret_cast<const uint4*>(Bq + static_cast<size_t>(n) * KB + static_cast<size_t>(ch) * 16);
+        zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (ch >> 2)]);
+        bsc[n][pw] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
+      }
+      const uint32_t zq = static_cast<uint32_t>(zb & 0xff) * 0x01010101u;
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      int sum = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        bw[n][pw][2 * u] = __vsub4((w[u] >> 4) & 0x0f0f0f0fu, zq);
+        bw[n][pw][2 * u + 1] = __vsub4(w[u] & 0x0f0f0f0fu, zq);
+        sum = __dp4a(static_cast<int>(bw[n][pw][2 * u]), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(bw[n][pw][2 * u + 1]), 0x01010101, sum);
+      }
+      bsum[n][pw] = p < P ? sum : 0;
+    }
+
+  const bool b4 = (lane & 16) != 0;
+  const bool b3 = (lane & 8) != 0;
+  const bool b2 = (lane & 4) != 0;
+  for (int base = 0; base < nrows; base += ROWS) {
+    float v[RMAX][NC];
+#pragma unroll
+    for (int i = 0; i < RMAX; ++i) {
+#pragma unroll
+      for (int n = 0; n < NC; ++n) v[i][n] = 0.f;
+#pragma unroll
+      for (int pw = 0; pw < PW; ++pw) {
+        const uint32_t w[4] = {a[i][pw].x, a[i][pw].y, a[i][pw].z, a[i][pw].w};
+        const int za = __half2int_rn(__low2half(zs[i][pw]));
+        const float sa = __high2float(zs[i][pw]);
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+          // High nibbles used in place (16 x code, unsigned bytes), shifted back exactly.
+          int dh = 0, dl = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            dh = dev::dp4a_u8s8(w[u] & 0xf0f0f0f0u, bw[n][pw][2 * u], dh);
+            dl = __dp4a(static_cast<int>(w[u] & 0x0f0f0f0fu), static_cast<int>(bw[n][pw][2 * u + 1]), dl);
+          }
+          const int d = dl + (dh >> 4) - za * bsum[n][pw];
+          v[i][n] = fmaf(static_cast<float>(d), sa * bsc[n][pw], v[i][n]);
+        }
+      }
+    }
+    // The registers of this round are consumed: the next round's rows in flight.
+    if (base + ROWS < nrows) load_round(base + ROWS);
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+      float x[4], y[2];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float keep = b4 ? v[4 + q][n] : v[q][n];
+        const float send = b4 ? v[q][n] : v[4 + q][n];
+        x[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float keep = b3 ? x[2 + q] : x[q];
+        const float send = b3 ? x[q] : x[2 + q];
+        y[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      float z = (b2 ? y[1] : y[0]) + __shfl_xor_sync(0xffffffffu, b2 ? y[0] : y[1], 4);
+      z += __shfl_xor_sync(0xffffffffu, z, 2);
+      z += __shfl_xor_sync(0xffffffffu, z, 1);
+      if ((lane & 3) == 0) part[rg + kLdgRowGroups * (lane >> 2)][wg][n] = z;  // row slot lane/4
+    }
+    __syncthreads();
+    for (int t = static_cast<int>(threadIdx.x); t < ROWS * NC; t += kLdgThreads) {
+      const int r = t / NC;
+      const int n = t - r * NC;
+      if (base + r < nrows) {
+        const float sum = ((part[r][0][n] + part[r][1][n]) + part[r][2][n]) + part[r][3][n];
+        C[static_cast<long long>(r0 + base + r) * ldc_row + n * ldc_col] = __float2half_rn(sum);
+      }
+    }
+    __syncthreads();  // part is reused by the next round
+  }
+}
+
 // Bare streaming read of n16 16-byte words (test hook, no GEMM): every thread
 // keeps four 128-bit loads in flight and XOR-folds them. It measures what one
 // kernel launch of this size can pull from HBM -- the floor under the decode

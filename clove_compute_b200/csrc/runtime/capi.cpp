@@ -88,6 +88,7 @@ Override get_override() {
 
 bool weight_prefetch_enabled() { return g_weight_prefetch.load() != 0; }
 bool ws_disabled() { return g_ov_path.load() == 2 && g_ov_bn.load() == 1; }
+bool ws2_selected() { return g_ov_path.load() == 2 && g_ov_bn.load() == 2; }
 
 // ---------------------------------------------------------------------------
 // Tile-shape policy for the tensor-core kernels

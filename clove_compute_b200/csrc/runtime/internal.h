@@ -44,6 +44,9 @@ bool weight_prefetch_enabled();
 // Test hook: path 2 with bn == 1 forces the register GEMV instead of the
 // warp-specialised one.
 bool ws_disabled();
+// Test hook: override (path 2, bn 2) picks the bulk-copy-ring INT4 decode kernel
+// instead of the default direct-load one.
+bool ws2_selected();
 
 // Tile shape chosen for a tensor-core call (capi.cpp).
 struct TcPlan {

@@ -129,6 +129,13 @@ def test_decode_back_to_back_ordering(clove_lib, oracle_mod, cuda, prefetch):
     assert clove_lib.device_error() == 0
 
 
+@pytest.mark.parametrize("N,K", [(1, 4096), (2, 4096), (1, 8192), (1, 1024)])
+def test_bulk_copy_decode_path(clove_lib, oracle_mod, cuda, N, K):
+    """The shared-memory ring variant of the decode GEMV (override path 2, bn 2)."""
+    clove_lib.set_dispatch_override(2, 2, 0)
+    _check(clove_lib, oracle_mod, 1000, N, K, path=2, seed=N + K, check_g=False)
+
+
 def test_register_gemv_path(clove_lib, oracle_mod, cuda):
     """The register-resident GEMV (used when the bulk-copy kernel does not apply)."""
     clove_lib.set_dispatch_override(2, 1, 0)
