@@ -44,6 +44,12 @@ def test_config2_decode_gemv(clove_lib, oracle_mod, cuda):
     _check(clove_lib, oracle_mod, 4096, 1, 4096)
 
 
+@pytest.mark.parametrize("M", [5, 9000, 16384])
+def test_decode_row_counts(clove_lib, oracle_mod, cuda, M):
+    """Decode blocks of a few rows per CTA up to several 32-row rounds per CTA."""
+    _check(clove_lib, oracle_mod, M, 1, 2048, seed=M, check_g=False)
+
+
 @pytest.mark.parametrize("N", [2, 3, 4, 8])
 def test_gemv_small_n(clove_lib, oracle_mod, cuda, N):
     _check(clove_lib, oracle_mod, 1000, N, 2048, seed=N)
