@@ -38,7 +38,8 @@ using kern::OpF16;
 using kern::OpI8;
 using kern::TcShape;
 
-typedef void (*TcKernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, int, EpiParams);
+typedef void (*TcKernelFn)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, int, int,
+                           EpiParams);
 
 struct TcEntry {
   int op, bn, split, out_bytes;
@@ -142,8 +143,12 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
   // All three as [batch, rows, cols] (batch 1 for a plain GEMM), densely packed.
   const uint64_t ub = static_cast<uint64_t>(batch);
   // A [M,K]: box 128 B of K x 128 rows, 128B swizzle.
+  // A box: 128 rows, or M rounded up to 8 (a whole swizzle atom) when M < 128, so
+  // that a decode-sized A does not stream 128 rows of zero fill per stage.
+  int a_rows = M < 128 ? ((M + 7) / 8) * 8 : 128;
   rc = encode_tmap_3d(&tmA, in_dt, elem, A, K, M, ub, static_cast<uint64_t>(K) * elem,
-                      static_cast<uint64_t>(M) * K * elem, e->bk, 128, 128);
+                      static_cast<uint64_t>(M) * K * elem, e->bk, static_cast<uint32_t>(a_rows),
+                      128);
   if (rc) return rc;
   // B [K,N]: box (swizzle width of N) x BK rows.
   rc = encode_tmap_3d(&tmB, in_dt, elem, B, N, K, ub, static_cast<uint64_t>(N) * elem,
@@ -166,7 +171,7 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   EpiParams epv = ep;
   epv.c_out = C;
-  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &batch, &epv};
+  void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &batch, &a_rows, &epv};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

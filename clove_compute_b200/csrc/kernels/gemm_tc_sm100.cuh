@@ -250,7 +250,7 @@ template <class Op, int BN, bool SPLIT, int OUT_BYTES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int batch,
-                   EpiParams ep) {
+                   int a_rows, EpiParams ep) {
   using S = TcShape<Op, BN, SPLIT, OUT_BYTES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = dev::align_smem_1024(smem_raw);
@@ -356,7 +356,9 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          dev::mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          // A's box is a_rows tall (M rounded up to 8 when M < 128): rows past it in
+          // the stage are stale and only feed accumulator rows that are never stored.
+          dev::mbar_arrive_expect_tx(&full[stage], a_rows * 128 + S::B_BYTES);
           if (kb == kb_begin) CLOVE_TRACE_POINT(2);
           uint8_t* a_dst = stage_base + stage * S::STAGE_BYTES;
           uint8_t* b_dst = a_dst + S::A_BYTES;
