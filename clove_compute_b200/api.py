@@ -221,6 +221,15 @@ def debug_stream_read(src, out, stream=None) -> None:
                                         _stream(stream)))
 
 
+def debug_stream_k_plan(tiles: int, pairs: int, kb_total: int, force: int = 0) -> dict:
+    """The CTA-pair kernel's stream-K schedule for `tiles` output tiles of kb_total
+    K blocks on `pairs` CTA pairs (host only; force 0 auto, 1 never, 2 always)."""
+    out = (ctypes.c_int * 4)()
+    check(lib().clove_debug_stream_k_plan(int(tiles), int(pairs), int(kb_total), int(force),
+                                          ctypes.cast(out, ctypes.c_void_p)))
+    return {"dp_tiles": out[0], "sk_tiles": out[1], "max_contrib": out[2], "pairs": out[3]}
+
+
 def set_dispatch_override(path: int = 0, bn: int = 0, split: int = 0) -> None:
     """Force a kernel family (tests): path 0 auto, 1 tensor core, 2 GEMV, 3 SIMT."""
     check(lib().clove_set_dispatch_override(int(path), int(bn), int(split)))

@@ -54,6 +54,57 @@ struct Tc2Shape {
   static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
+// One piece of a pair's work: K blocks [kb0, kb1) of `tile`.
+struct Tc2Work {
+  int tile, kb0, kb1;
+  int sk_idx;  // stream-K tile index (-1: a whole-K tile)
+  int j, nc;   // this pair's contributor index within the tile, the tile's contributor count
+};
+
+// Work order of one pair (SkParams): its contiguous range of stream-K units (unit =
+// one K block of one stream-K tile) first, then its round-robin whole-K tiles, so
+// that the last contributor's sum over the partial slots (L2 round trips) overlaps
+// the whole-K tiles' main loops instead of trailing the kernel. Producer, MMA
+// issuer and epilogue each walk the same sequence.
+struct Tc2Sched {
+  int pair, pairs, dp_tiles, kb_total, next_dp;
+  long long U, u, u_end;
+  __device__ Tc2Sched(int pair_, int pairs_, const SkParams& sk, int kb_total_)
+      : pair(pair_), pairs(pairs_), dp_tiles(sk.dp_tiles), kb_total(kb_total_), next_dp(pair_) {
+    U = static_cast<long long>(sk.sk_tiles) * kb_total_;
+    u = U * pair_ / pairs_;
+    u_end = U * (pair_ + 1) / pairs_;
+  }
+  // The pair whose range [U p / P, U (p+1) / P) holds unit v.
+  __device__ int owner(long long v) const {
+    return static_cast<int>(((v + 1) * pairs + U - 1) / U) - 1;
+  }
+  __device__ bool next(Tc2Work& w) {
+    if (u >= u_end) {
+      if (next_dp >= dp_tiles) return false;
+      w.tile = next_dp;
+      w.kb0 = 0;
+      w.kb1 = kb_total;
+      w.sk_idx = -1;
+      w.j = 0;
+      w.nc = 1;
+      next_dp += pairs;
+      return true;
+    }
+    const int t = static_cast<int>(u / kb_total);
+    const long long t0 = static_cast<long long>(t) * kb_total;
+    w.kb0 = static_cast<int>(u - t0);
+    w.kb1 = static_cast<int>(min(static_cast<long long>(kb_total), w.kb0 + (u_end - u)));
+    const int first = owner(t0);
+    w.tile = dp_tiles + t;
+    w.sk_idx = t;
+    w.j = pair - first;
+    w.nc = owner(t0 + kb_total - 1) - first + 1;
+    u += w.kb1 - w.kb0;
+    return true;
+  }
+};
+
 // GLU (fp16 only): C = silu(A . B) * (A . B2) with B = W_gate, B2 = W_up [K,N].
 // The pair's 256 accumulator columns become 128 gate columns (B half loaded by the
 // leader CTA) followed by the same 128 columns of up (loaded by the peer CTA), so
@@ -63,7 +114,7 @@ template <class Op, bool GLU = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC,
-                    int M, int N, int K, EpiParams ep) {
+                    int M, int N, int K, EpiParams ep, SkParams sk) {
   using S = Tc2Shape<Op>;
   static_assert(!GLU || !Op::kInt, "GLU epilogue is fp16");
   constexpr int TILE_N = GLU ? S::BNH : S::BN;  // output columns per pair tile
@@ -76,8 +127,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = bars + S::STAGES;       // both CTAs (commit multicast)
   uint64_t* tfull = bars + 2 * S::STAGES;   // both CTAs (commit multicast)
   uint64_t* tempty = tfull + 2;             // leader's used (4 local + 4 remote arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* skbar = tempty + 2;             // stream-K hand-offs among this CTA's epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(skbar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* sk_last = abort_flag + 1;   // this CTA holds a stream-K tile's last ticket
 
   const uint32_t warp = dev::warp_idx();
   const uint32_t lane = dev::lane_idx();
@@ -93,6 +146,8 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_init(&tfull[b], 1);
       dev::mbar_init(&tempty[b], 8);
     }
+    dev::mbar_init(&skbar[0], 4);
+    dev::mbar_init(&skbar[1], 1);
     *abort_flag = 0;
     dev::fence_mbarrier_init();
   }
@@ -116,7 +171,6 @@ __global__ void __launch_bounds__(192, 1)
 
   const int tiles_m = (M + 2 * S::BM - 1) / (2 * S::BM);
   const int tiles_n = (N + TILE_N - 1) / TILE_N;
-  const int num_tiles = tiles_m * tiles_n;
   const int kb_total = (K + S::BK - 1) / S::BK;
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int pairs = static_cast<int>(gridDim.x >> 1);
@@ -125,14 +179,16 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      for (int tile = pair; tile < num_tiles; tile += pairs) {
+      Tc2Sched sched(pair, pairs, sk, kb_total);
+      Tc2Work w;
+      while (sched.next(w)) {
         int m_blk, n_blk;
-        tile_coords<kPairGroupM>(tile, tiles_m, tiles_n, m_blk, n_blk);
+        tile_coords<kPairGroupM>(w.tile, tiles_m, tiles_n, m_blk, n_blk);
         const int my_m = m_blk * 2 * S::BM + static_cast<int>(rank) * S::BM;
         const int my_n = GLU ? n_blk * S::BNH : n_blk * S::BN + static_cast<int>(rank) * S::BNH;
         const CUtensorMap* my_b = (GLU && rank == 1) ? &tmB2 : &tmB;
         bool ok = true;
-        for (int kb = 0; kb < kb_total; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!dev::mbar_wait<true>(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -162,13 +218,15 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t stage = 0, phase = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += pairs, ++it) {
+      Tc2Sched sched(pair, pairs, sk, kb_total);
+      Tc2Work w;
+      for (; ok && sched.next(w); ++it) {
         const uint32_t buf = static_cast<uint32_t>(it) & 1u;
         const uint32_t use = static_cast<uint32_t>(it) >> 1;
         if (!dev::mbar_wait<true>(&tempty[buf], (use & 1u) ^ 1u, abort_flag)) break;
         dev::tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + buf * S::BN;
-        for (int kb = 0; kb < kb_total; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!dev::mbar_wait<true>(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -182,7 +240,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t bdesc = dev::make_smem_desc(b_addr + k * S::UMMA_K * S::B_SW,
                                                        S::BK * S::B_SW, 8 * S::B_SW,
                                                        dev::kLayoutSw128);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > w.kb0 || k > 0) ? 1u : 0u;
             if constexpr (Op::kInt)
               dev::mma_i8_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
             else
@@ -205,10 +263,13 @@ __global__ void __launch_bounds__(192, 1)
     const int row_in_tile = static_cast<int>(q * 32 + lane);
     uint8_t* stg_base = epi_base + (warp - 2) * (2 * 4096);
     uint32_t stg_count = 0;
+    uint32_t sk_phase = 0;
     int it = 0;
-    for (int tile = pair; tile < num_tiles; tile += pairs, ++it) {
+    Tc2Sched sched(pair, pairs, sk, kb_total);
+    Tc2Work w;
+    for (; sched.next(w); ++it) {
       int m_blk, n_blk;
-      tile_coords<kPairGroupM>(tile, tiles_m, tiles_n, m_blk, n_blk);
+      tile_coords<kPairGroupM>(w.tile, tiles_m, tiles_n, m_blk, n_blk);
       const uint32_t buf = static_cast<uint32_t>(it) & 1u;
       const uint32_t use = static_cast<uint32_t>(it) >> 1;
       if (!__all_sync(0xffffffffu, dev::mbar_wait<true>(&tfull[buf], use & 1u, abort_flag))) break;
@@ -224,6 +285,91 @@ __global__ void __launch_bounds__(192, 1)
       if ((ep.mode == kEpiI8Tensor || ep.mode == kEpiI32Raw) && ep.zb != 0 && row < M)
         row_corr = static_cast<int32_t>(0u - static_cast<uint32_t>(ep.zb) *
                                                  static_cast<uint32_t>(ep.row_sum[row]));
+      if constexpr (!GLU) {
+        if (w.nc > 1) {
+          // Stream-K piece: park the 32-bit partial accumulators in this piece's
+          // slot, laid out [column quad][row] so that a warp's 16-byte stores
+          // cover 512 contiguous bytes, then take a ticket; the last of the
+          // tile's contributors sums every slot in contributor order and runs
+          // the epilogue.
+          constexpr size_t kSlot = static_cast<size_t>(S::BN) * S::BM;  // words per CTA and piece
+          uint32_t* part = sk.partials +
+                           ((static_cast<size_t>(w.sk_idx) * sk.max_contrib + w.j) * 2 + rank) * kSlot;
+#pragma unroll 1
+          for (int c0 = 0; c0 < S::BN; c0 += 32) {
+            uint32_t t0[16], t1[16];
+            dev::tmem_ld_x16(t_row + c0, t0);
+            dev::tmem_ld_x16(t_row + c0 + 16, t1);
+            dev::tmem_ld_wait();
+#pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              *reinterpret_cast<uint4*>(part + ((c0 / 4 + qd) * S::BM + row_in_tile) * 4) =
+                  make_uint4(t0[4 * qd], t0[4 * qd + 1], t0[4 * qd + 2], t0[4 * qd + 3]);
+              *reinterpret_cast<uint4*>(part + ((c0 / 4 + 4 + qd) * S::BM + row_in_tile) * 4) =
+                  make_uint4(t1[4 * qd], t1[4 * qd + 1], t1[4 * qd + 2], t1[4 * qd + 3]);
+            }
+          }
+          dev::tc_fence_before_sync();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader)
+              dev::mbar_arrive(&tempty[buf]);
+            else
+              dev::mbar_arrive_remote(&tempty[buf], 0);
+            dev::mbar_arrive(&skbar[0]);
+          }
+          bool ok = dev::mbar_wait(&skbar[0], sk_phase & 1u, abort_flag);
+          if (warp == 2 && lane == 0 && ok) {
+            __threadfence();
+            const int old = atomicAdd(&sk.tickets[w.sk_idx * 2 + static_cast<int>(rank)], 1);
+            *sk_last = old == w.nc - 1 ? 1 : 0;
+            dev::mbar_arrive(&skbar[1]);
+          }
+          ok = __all_sync(0xffffffffu, ok);
+          ok = ok && dev::mbar_wait(&skbar[1], sk_phase & 1u, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          ++sk_phase;
+          if (!ok) break;
+          if (*sk_last) {
+            __threadfence();
+            const uint32_t* slot0 =
+                sk.partials + (static_cast<size_t>(w.sk_idx) * sk.max_contrib * 2 + rank) * kSlot;
+#pragma unroll 1
+            for (int c0 = 0; c0 < S::BN; c0 += S::CHUNK) {
+              uint32_t v[S::CHUNK];
+#pragma unroll 1
+              for (int jj = 0; jj < w.nc; ++jj) {
+                const uint32_t* src =
+                    slot0 + static_cast<size_t>(jj) * 2 * kSlot + ((c0 / 4) * S::BM + row_in_tile) * 4;
+                uint4 x[S::CHUNK / 4];
+#pragma unroll
+                for (int qd = 0; qd < S::CHUNK / 4; ++qd)
+                  x[qd] = __ldcg(reinterpret_cast<const uint4*>(src + qd * S::BM * 4));
+#pragma unroll
+                for (int qd = 0; qd < S::CHUNK / 4; ++qd) {
+                  const uint32_t e[4] = {x[qd].x, x[qd].y, x[qd].z, x[qd].w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    uint32_t& d = v[4 * qd + i];
+                    if (jj == 0)
+                      d = e[i];
+                    else if constexpr (Op::kInt)
+                      d += e[i];
+                    else
+                      d = __float_as_uint(__uint_as_float(d) + __uint_as_float(e[i]));
+                  }
+                }
+              }
+              store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
+                                           stg_base, stg_count, &tmC,
+                                           m0 + static_cast<int>(q) * 32);
+            }
+          }
+          if (*abort_flag) break;
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < TILE_N; c0 += S::CHUNK) {
         uint32_t v[S::CHUNK];

@@ -2,7 +2,10 @@
 // TMA descriptor encoding, kernel instantiation table, persistent / cluster launch.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cstdint>
+#include <mutex>
 
 #include "gemm_tc2_sm100.cuh"
 #include "gemm_tc_sm100.cuh"
@@ -204,6 +207,76 @@ namespace rt {
 
 namespace {
 std::atomic<uint64_t> g_tc2_attr[3];
+std::atomic<int> g_tc2_clusters[64][3];  // co-resident pairs per device and variant (0: unknown)
+
+// Stream-ordered pool for the stream-K partials, one per device, that keeps its
+// memory between calls (the default pool may return it to the driver at every
+// synchronisation, and a 40 MB re-map per call would cost more than the schedule
+// saves).
+std::mutex g_sk_pool_mu;
+cudaMemPool_t g_sk_pool[64];
+
+int sk_pool(int device, cudaMemPool_t* out) {
+  std::lock_guard<std::mutex> lock(g_sk_pool_mu);
+  if (g_sk_pool[device & 63] == nullptr) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    cudaMemPool_t pool;
+    int rc = check_cuda(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate(stream-K)");
+    if (rc) return rc;
+    uint64_t keep = UINT64_MAX;
+    rc = check_cuda(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
+                    "cudaMemPoolSetAttribute(stream-K)");
+    if (rc) return rc;
+    g_sk_pool[device & 63] = pool;
+  }
+  *out = g_sk_pool[device & 63];
+  return CLOVE_OK;
+}
+
+}  // namespace
+
+// Stream-K plan of the CTA-pair kernel for `tiles` output tiles of kb_total K
+// blocks on `pairs` co-resident pairs (SkParams). A partial last wave leaves
+// (1 - tiles / (waves * pairs)) of the GPU idle for a whole tile; the last partial
+// wave's tiles (plus one full wave when the partial wave is under half full, so
+// that no tile is cut into more than three pieces) can instead be spread evenly
+// over all pairs by K block. That costs a fixed ~10 us per launch (partial slots,
+// the tickets' memset, which also ends the programmatic overlap with the previous
+// kernel), and under the power cap the idle SMs of a partial wave let the busy
+// ones clock higher, which recovers part of the loss anyway; measured on B200,
+// the schedule only pays for long K ranges (>= 128 K blocks) with >= 10 % idle:
+// FFN down 4096 x 2048 x 11008 146 -> 142 us, 3584 x 2048 x 11008 150 -> 133 us,
+// while FFN up 11008 x 2048 x 4096 loses (130 -> 138 us). force: 1 = never, 2 =
+// whenever the tile count is not a multiple of the pairs (and every pair gets a K
+// block).
+SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force) {
+  SkPlan p{tiles, 0, 0, std::min(pairs, std::max(tiles, 1))};
+  if (force == 1 || pairs <= 1 || tiles <= 0 || tiles % pairs == 0) return p;
+  const long long waves = (tiles + pairs - 1) / pairs;
+  const double idle = 1.0 - static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+  int sk = tiles % pairs;
+  if (tiles > pairs && 2 * sk < pairs) sk += pairs;
+  const long long units = static_cast<long long>(sk) * kb_total;
+  // Automatic only with at least one full wave (then no piece is under half a
+  // tile's K range); forced plans may cut a tile into many pieces (tests).
+  if (force != 2 && (tiles < pairs || idle < 0.10 || kb_total < 128)) return p;
+  if (units < pairs) return p;  // every pair needs at least one K block
+  auto owner = [&](long long v) {
+    return static_cast<int>(((v + 1) * pairs + units - 1) / units) - 1;
+  };
+  int mc = 1;
+  for (int t = 0; t < sk; ++t) {
+    const long long t0 = static_cast<long long>(t) * kb_total;
+    mc = std::max(mc, owner(t0 + kb_total - 1) - owner(t0) + 1);
+  }
+  p.dp_tiles = tiles - sk;
+  p.sk_tiles = sk;
+  p.max_contrib = mc;
+  p.pairs = pairs;
+  return p;
 }
 
 // CTA-pair 256 x 256 tile kernel (fp16 C only).
@@ -250,10 +323,9 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
   }
   const int tile_n = glu ? 128 : 256;
   const int tiles = ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
-  int pairs = dev.num_sms / 2;
-  if (pairs > tiles) pairs = tiles;
   kern::EpiParams epv = ep;
-  void* args[] = {&tmA, &tmB, &tmB2, &tmC, &M, &N, &K, &epv};
+  kern::SkParams skp = {};
+  void* args[] = {&tmA, &tmB, &tmB2, &tmC, &M, &N, &K, &epv, &skp};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -262,13 +334,67 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
   attrs[0].val.clusterDim.z = 1;
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = stream;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  return check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "gemm_tc2 launch");
+
+  // Pairs that can be resident at once (clusters must fit in one GPC).
+  std::atomic<int>& known = g_tc2_clusters[dev.device & 63][glu ? 2 : f16 ? 0 : 1];
+  int resident = known.load(std::memory_order_acquire);
+  if (resident == 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(dev.num_sms & ~1), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = dev.num_sms / 2;
+    }
+    resident = std::min(n, dev.num_sms / 2);
+    known.store(resident, std::memory_order_release);
+  }
+  const int kb_total = (K + bk - 1) / bk;
+  const Override ov = get_override();
+  const SkPlan plan = plan_stream_k(tiles, resident, kb_total,
+                                    glu ? 1 : ov.path == 4 ? ov.split : 0);
+  skp.dp_tiles = plan.dp_tiles;
+  skp.sk_tiles = plan.sk_tiles;
+  skp.max_contrib = plan.max_contrib;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * plan.pairs), 1, 1);
+
+  void* ws = nullptr;
+  if (plan.sk_tiles > 0) {
+    const size_t ticket_bytes = (static_cast<size_t>(plan.sk_tiles) * 2 * sizeof(int) + 255) & ~size_t(255);
+    const size_t part_bytes = static_cast<size_t>(plan.sk_tiles) * plan.max_contrib * 2 *
+                              (256 * 128) * sizeof(uint32_t);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    rc = check_cuda(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");
+    if (rc) return rc;
+    if (cap == cudaStreamCaptureStatusNone) {
+      cudaMemPool_t pool;
+      rc = sk_pool(dev.device, &pool);
+      if (rc) return rc;
+      rc = check_cuda(cudaMallocFromPoolAsync(&ws, ticket_bytes + part_bytes, pool, stream),
+                      "cudaMallocFromPoolAsync(stream-K)");
+    } else {  // graph capture: an allocation node of the graph's own pool
+      rc = check_cuda(cudaMallocAsync(&ws, ticket_bytes + part_bytes, stream),
+                      "cudaMallocAsync(stream-K)");
+    }
+    if (rc) return rc;
+    skp.tickets = static_cast<int*>(ws);
+    skp.partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ticket_bytes);
+    rc = check_cuda(cudaMemsetAsync(ws, 0, ticket_bytes, stream), "cudaMemsetAsync(stream-K)");
+    if (rc) {
+      cudaFreeAsync(ws, stream);
+      return rc;
+    }
+  }
+  rc = check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "gemm_tc2 launch");
+  if (ws != nullptr) {
+    const int rc2 = check_cuda(cudaFreeAsync(ws, stream), "cudaFreeAsync(stream-K)");
+    if (rc == CLOVE_OK) rc = rc2;
+  }
+  return rc;
 }
 
 }  // namespace rt

@@ -28,6 +28,20 @@ struct EpiParams {
   void* c_out;              // C itself (split-K tiles store rows directly)
 };
 
+// Stream-K schedule of the CTA-pair kernel. Tiles [0, dp_tiles) go round-robin to
+// the pairs with their whole K range. The K blocks of tiles [dp_tiles, dp_tiles +
+// sk_tiles), taken tile after tile, are cut into one contiguous range per pair of
+// equal length, so every pair ends at the same time; a tile cut between several
+// pairs is summed by whichever contributor finishes last (an atomic ticket), from
+// 32-bit partial accumulators in `partials`. sk_tiles == 0: plain persistent tiles.
+struct SkParams {
+  int dp_tiles;
+  int sk_tiles;
+  int max_contrib;          // partial slots per stream-K tile
+  uint32_t* partials;       // [sk_tiles][max_contrib][2 CTAs][64 column quads][128 rows][4]
+  int* tickets;             // [sk_tiles][2 CTAs], zero at launch
+};
+
 // Epilogue of the int8 GEMV (modes as EpiMode 1..3).
 struct GemvI8Epi {
   int mode;

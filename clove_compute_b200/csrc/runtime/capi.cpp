@@ -535,6 +535,18 @@ int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void*
 // ---------------------------------------------------------------------------
 // Introspection
 // ---------------------------------------------------------------------------
+int clove_debug_stream_k_plan(int tiles, int pairs, int kb_total, int force, int* out) {
+  if (out == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "null output");
+  if (tiles < 0 || pairs < 1 || kb_total < 1 || force < 0 || force > 2)
+    return fail(CLOVE_ERR_INVALID_ARG, "bad stream-K plan arguments");
+  const SkPlan p = plan_stream_k(tiles, pairs, kb_total, force);
+  out[0] = p.dp_tiles;
+  out[1] = p.sk_tiles;
+  out[2] = p.max_contrib;
+  out[3] = p.pairs;
+  return CLOVE_OK;
+}
+
 int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t buflen) {
   if (buf == nullptr || buflen == 0) return fail(CLOVE_ERR_INVALID_ARG, "null buffer");
   DeviceInfo dev{0, 148, 10, 0};

@@ -65,6 +65,12 @@ enum TcOp { kTcF16 = 0, kTcI8 = 1 };
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
                    const DeviceInfo& dev, cudaStream_t stream, int batch = 1);
+// Stream-K schedule of the CTA-pair kernel (kern::SkParams); pairs = CTA pairs to
+// launch. force: 0 auto, 1 never, 2 whenever the tiles leave a partial wave.
+struct SkPlan {
+  int dp_tiles, sk_tiles, max_contrib, pairs;
+};
+SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force);
 // CTA-pair kernel: 256 x 256 tiles on two SMs (fp16 C).
 // B2 != nullptr: fp16 GLU, C = silu(A . B) * (A . B2) (256 x 128 output tiles).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,

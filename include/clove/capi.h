@@ -141,11 +141,20 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
  * (Measurement hook; no counterpart in the reference.) */
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream);
 
+/* Stream-K schedule the CTA-pair kernel uses for `tiles` 256 x 256 output tiles of
+ * kb_total K blocks on `pairs` co-resident CTA pairs (force: 0 automatic, 1 never,
+ * 2 whenever the tiles leave a partial wave). Writes {whole-K tiles, stream-K
+ * tiles, partial slots per stream-K tile, pairs launched} to out[0..3]. Host only.
+ * (Introspection hook; no counterpart in the reference.) */
+int clove_debug_stream_k_plan(int tiles, int pairs, int kb_total, int force, int* out);
+
 /* Forces a kernel family for subsequent calls from any thread (tests only).
  * path: 0 = automatic, 1 = tensor-core tiles on one SM, 2 = GEMV, 3 = SIMT
  * fallback, 4 = tensor-core 256 x 256 tiles on CTA pairs.
  * bn: tensor-core N tile (0 = automatic; 32/64/128/256). split: cluster split-K
- * factor (0 = automatic, 1 = none, 2..8). Returns CLOVE_OK. */
+ * factor (0 = automatic, 1 = none, 2..8); with path 4 it selects the stream-K
+ * schedule instead (0 automatic, 1 never, 2 whenever the tiles leave a partial
+ * wave). Returns CLOVE_OK. */
 int clove_set_dispatch_override(int path, int bn, int split);
 
 /* Decode kernels (N <= 8 or M <= 8) start streaming their large operand -- the

@@ -83,3 +83,69 @@ def test_host_argument_checks_need_no_gpu(clove_lib):
     # empty problems are no-ops
     assert lib.clove_swiglu_fused(None, None, None, None, 0, 8, 8, None) == clove_lib.CLOVE_OK
     assert lib.clove_quantize_int4(None, 0, 128, None, None, None, None) == clove_lib.CLOVE_OK
+
+
+def _stream_k_pieces(plan, kb):
+    """Restates the CTA-pair kernel's per-pair work order (Tc2Sched in
+    csrc/kernels/gemm_tc2_sm100.cuh): each pair's contiguous range of stream-K
+    units, then its round-robin whole-K tiles. Yields (pair, tile, kb0, kb1, sk_idx,
+    j, nc)."""
+    P, dp, sk = plan["pairs"], plan["dp_tiles"], plan["sk_tiles"]
+    U = sk * kb
+    owner = lambda v: ((v + 1) * P + U - 1) // U - 1
+    for p in range(P):
+        u, ue = U * p // P, U * (p + 1) // P
+        while u < ue:
+            t = u // kb
+            kb0 = u - t * kb
+            kb1 = min(kb, kb0 + ue - u)
+            first = owner(t * kb)
+            yield p, dp + t, kb0, kb1, t, p - first, owner(t * kb + kb - 1) - first + 1
+            u += kb1 - kb0
+        for t in range(p, dp, P):
+            yield p, t, 0, kb, -1, 0, 1
+
+
+@pytest.mark.parametrize("tiles,pairs,kb,force", [
+    (344, 74, 64, 2),    # FFN up: 4.65 waves
+    (128, 74, 172, 0),   # FFN down: 1.73 waves
+    (256, 74, 64, 2),    # 4096^3: a partial wave under half full -> one full wave joins it
+    (80, 74, 64, 2), (1024, 74, 128, 0), (296, 74, 64, 2), (112, 74, 172, 0),
+    (5, 74, 64, 2), (7, 3, 5, 2), (10, 4, 3, 2), (1, 74, 200, 2), (3, 2, 1, 2)])
+def test_stream_k_schedule_covers_each_k_block_once(clove_lib, tiles, pairs, kb, force):
+    plan = clove_lib.debug_stream_k_plan(tiles, pairs, kb, force)
+    assert plan["dp_tiles"] + plan["sk_tiles"] == tiles
+    pieces = list(_stream_k_pieces(plan, kb))
+    by_tile = {}
+    for p, t, kb0, kb1, ski, j, nc in pieces:
+        assert 0 <= kb0 < kb1 <= kb
+        by_tile.setdefault(t, []).append((kb0, kb1, ski, j, nc, p))
+    assert sorted(by_tile) == list(range(tiles))
+    load = [0] * plan["pairs"]
+    for t, ps in by_tile.items():
+        ps.sort()
+        assert ps[0][0] == 0 and ps[-1][1] == kb
+        assert all(a[1] == b[0] for a, b in zip(ps, ps[1:]))  # contiguous, no overlap
+        nc = len(ps)
+        assert all(x[4] == nc for x in ps)
+        assert sorted(x[3] for x in ps) == list(range(nc))     # one partial slot each
+        assert [x[5] for x in ps] == sorted(x[5] for x in ps)  # consecutive pairs
+        if nc > 1:
+            assert nc <= plan["max_contrib"]
+        for kb0, kb1, ski, j, _, p in ps:
+            if ski >= 0:
+                load[p] += kb1 - kb0
+    if plan["sk_tiles"]:
+        assert max(load) - min(load) <= 1  # stream-K ranges differ by at most one K block
+
+
+def test_stream_k_plans_for_the_ffn_shapes(clove_lib):
+    up = clove_lib.debug_stream_k_plan(43 * 8, 74, 64)       # 11008 x 2048, K = 4096
+    down = clove_lib.debug_stream_k_plan(16 * 8, 74, 172)    # 4096 x 2048, K = 11008
+    assert up["sk_tiles"] == 0  # 7 % idle over 64 K blocks: not worth the fixed cost
+    assert down["sk_tiles"] == 128 % 74 and down["max_contrib"] <= 3
+    assert clove_lib.debug_stream_k_plan(43 * 8, 74, 64, 2)["sk_tiles"] == 344 % 74
+    # A last wave of 1024 / 74 = 13.8 waves idles 1 %: plain persistent tiles.
+    assert clove_lib.debug_stream_k_plan(1024, 74, 128)["sk_tiles"] == 0
+    assert clove_lib.debug_stream_k_plan(100, 74, 64, 1)["sk_tiles"] == 0
+    assert clove_lib.debug_stream_k_plan(5, 74, 64)["pairs"] == 5

@@ -156,3 +156,68 @@ def test_no_writes_outside_c(clove_lib, oracle_mod, cuda):
 def test_dispatch_choices(clove_lib, cuda):
     assert clove_lib.describe_dispatch("fp16", 1024, 1024, 1024).startswith("tc_f16")
     assert clove_lib.describe_dispatch("fp16", 4096, 1, 4096).startswith("gemv_f16")
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 4096), (768, 520, 1000), (640, 776, 2048),
+                                   (256, 256, 8192), (1280, 1024, 64)])
+def test_tc_cta_pair_stream_k_forced(clove_lib, oracle_mod, cuda, M, N, K):
+    """Stream-K schedule forced on shapes with few tiles: each tile's K range is cut
+    over many CTA pairs (up to ~19 partial slots), summed by the last contributor."""
+    _run(clove_lib, oracle_mod, M, N, K, path=4, split=2, seed=K)
+
+
+def test_tc_cta_pair_stream_k_alpha_beta(clove_lib, oracle_mod, cuda):
+    _run(clove_lib, oracle_mod, 768, 512, 2048, path=4, split=2, alpha=0.5, beta=1.0, seed=3)
+
+
+def _sampled_rows_check(cc, oracle, A, B, C, rows):
+    ref = oracle.gemm_fp16(np.ascontiguousarray(A[rows]), B)
+    assert rel_fro(C[rows], ref) < TOL_TIGHT
+
+
+def test_ffn_down_stream_k(clove_lib, oracle_mod, cuda):
+    """FFN down (4096 x 2048 x 11008): 128 pair tiles on 74 pairs, so the last 54
+    tiles run as stream-K pieces. Rows from whole-K and stream-K tiles are checked
+    against the oracle, and the result does not depend on which contributor
+    finishes last (slots are summed in a fixed order)."""
+    M, N, K = 4096, 2048, 11008
+    rng = np.random.default_rng(21)
+    A = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
+    B = rng.standard_normal((K, N)).astype(np.float16)
+    Ad, Bd = dev(A), dev(B)
+    C1 = clove_lib.gemm_fp16(Ad, Bd)
+    C2 = clove_lib.gemm_fp16(Ad, Bd)
+    torch.cuda.synchronize()
+    h1, h2 = host(C1), host(C2)
+    np.testing.assert_array_equal(h1, h2)
+    rows = np.r_[0:8, 1020:1030, 2300:2310, 3580:3600, 4080:4096]
+    _sampled_rows_check(clove_lib, oracle_mod, A, B, h1, rows)
+    clove_lib.set_dispatch_override(4, 0, 1)  # same kernel, whole-K tiles only
+    h3 = host(clove_lib.gemm_fp16(Ad, Bd))
+    assert rel_fro(h1, h3) < 1e-3
+    assert clove_lib.device_error() == 0
+
+
+def test_stream_k_in_cuda_graph(clove_lib, cuda):
+    """The stream-K workspace becomes an allocation node when captured; replays
+    reproduce the eager result bit for bit."""
+    M, N, K = 4096, 2048, 11008
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.5).half()
+    B = torch.randn(K, N, device="cuda", generator=g).half()
+    C = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    clove_lib.gemm_fp16(A, B, C)
+    torch.cuda.synchronize()
+    eager = C.clone()
+    C.zero_()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            clove_lib.gemm_fp16(A, B, C, stream=s)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(C, eager)
+    assert clove_lib.device_error() == 0

@@ -73,11 +73,14 @@ def test_per_tensor_reference_signature(clove_lib, oracle_mod, cuda):
     assert clove_lib.device_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 272, 512)])
-def test_tc_cta_pair_rowcol(clove_lib, oracle_mod, cuda, M, N, K):
-    """int8 on CTA pairs (kind::i8, cta_group::2): C bit-identical in practice."""
+@pytest.mark.parametrize("sk", [0, 2])
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 272, 512), (768, 512, 4096)])
+def test_tc_cta_pair_rowcol(clove_lib, oracle_mod, cuda, M, N, K, sk):
+    """int8 on CTA pairs (kind::i8, cta_group::2): C bit-identical in practice; with
+    the stream-K schedule forced (sk=2) the int32 partials of a tile's K pieces are
+    summed exactly, so C stays bit-identical too."""
     A, B, sA, sB = wl.int8_operands(M, N, K, seed=M)
-    clove_lib.set_dispatch_override(4, 0, 0)
+    clove_lib.set_dispatch_override(4, 0, sk)
     C = host(clove_lib.gemm_int8_rowcol(dev(A), dev(B), dev(sA), dev(sB)))
     ref = oracle_mod.gemm_int8_rowcol(A, B, sA, sB)
     assert rel_fro(C, ref) < 1e-3
