@@ -351,8 +351,44 @@ def _secondary(cc, torch, peaks):
         "note": "silu(X.W_gate) * (X.W_up), fp16; unfused = two tile-kernel GEMMs + elementwise"}
     del Xs, Wg, Wu, Os
 
-    # config 1 and the square sweep (fp16, 1024-16384), int8 square sweep
+    # The two FFN GEMMs against cuBLAS (torch.matmul) on the same operands, timed
+    # interleaved (graph of 10 calls each, alternated 6 times, medians) so that both
+    # see the same clocks; two weight copies (180 MB) rotate, so HBM is measured.
     gen = torch.Generator(device="cuda")
+    ffn_cmp = {}
+    for name, (M, N, K) in (("up", (11008, 2048, 4096)), ("down", (4096, 2048, 11008))):
+        gen.manual_seed(M + K)
+        W = [(torch.randn((M, K), device="cuda", generator=gen) / K ** 0.5).half()
+             for _ in range(2)]
+        X = torch.randn((K, N), device="cuda", generator=gen).half()
+        Cf = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        graphs = {}
+        for impl in ("clove", "cublas"):
+            fn = (lambda i: cc.gemm_fp16(W[i % 2], X, Cf)) if impl == "clove" else \
+                 (lambda i: torch.matmul(W[i % 2], X, out=Cf))
+            for i in range(3):
+                fn(i)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(10):
+                    fn(i)
+            graphs[impl] = g
+        ts = {k: [] for k in graphs}
+        for _ in range(6):
+            for k, g in graphs.items():
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                e1.synchronize()
+                ts[k].append(e0.elapsed_time(e1) * 1e3 / 10)
+        ffn_cmp[name] = {k: round(statistics.median(v), 2) for k, v in ts.items()}
+        ffn_cmp[name]["kernel"] = cc.describe_dispatch("fp16", M, N, K)
+        del graphs, W, X, Cf
+    out["ffn_vs_cublas_us"] = dict(ffn_cmp, note="per call, same box and operands, interleaved")
+
+    # config 1 and the square sweep (fp16, 1024-16384), int8 square sweep
     for n in (1024, 2048, 4096, 8192, 16384):
         # Timing-only operands: the config distribution N(0,1)/sqrt(K), drawn on the
         # GPU from a seeded generator (host generation of 16384^2 takes minutes).

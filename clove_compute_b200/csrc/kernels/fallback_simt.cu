@@ -84,6 +84,18 @@ int launch_scale_f16(void* C, long long n, float beta, cudaStream_t stream) {
 namespace clove {
 namespace rt {
 
+int launch_peer_signal_wait(int nranks, int rank, unsigned long long* epoch,
+                            unsigned long long* const* flags, cudaStream_t stream) {
+  if (nranks > kern::kMaxPeers) return fail(CLOVE_ERR_UNSUPPORTED, "too many ranks");
+  kern::PeerSync ps = {};
+  ps.nranks = nranks;
+  ps.rank = rank;
+  ps.epoch = epoch;
+  for (int q = 0; q < nranks; ++q) ps.flags[q] = flags[q];
+  kern::peer_signal_wait_kernel<<<1, 32, 0, stream>>>(ps);
+  return check_cuda(cudaGetLastError(), "peer signal launch");
+}
+
 int launch_relayout_columns(const void* staging, void* C, int M, int N, int P, int Nmax,
                             int elem_bytes, cudaStream_t stream) {
   if (elem_bytes != 2) return fail(CLOVE_ERR_UNSUPPORTED, "relayout: 16-bit elements only");

@@ -164,5 +164,48 @@ __global__ void relayout_columns_kernel(const uint16_t* __restrict__ staging,
   C[idx] = staging[(static_cast<size_t>(p) * M + m) * Nmax + j];
 }
 
+// Cross-rank completion signal after a replicated-output GEMM (PeerOut). Rank r
+// bumps its device-side epoch e, then stores e into slot r of every rank's flag
+// array (system-scope release, after a system fence, so the GEMM's remote stores
+// that preceded this kernel on the stream are visible first) and waits until
+// every other rank's slot in its own array holds >= e (system-scope acquire).
+// All ranks make the same calls in the same order, so the epochs agree, also
+// when the kernel is replayed from a CUDA graph. The wait gives up after 2 s and
+// records a timeout instead of hanging.
+struct PeerSync {
+  int nranks, rank;
+  unsigned long long* epoch;                    // this rank's counter
+  unsigned long long* flags[kMaxPeers];         // flags[q]: rank q's array [nranks]
+};
+
+__global__ void peer_signal_wait_kernel(PeerSync ps) {
+  const int lane = static_cast<int>(threadIdx.x);
+  unsigned long long e = 0;
+  if (lane == 0) {
+    e = *ps.epoch + 1;
+    *ps.epoch = e;
+  }
+  e = __shfl_sync(0xffffffffu, e, 0);
+  __threadfence_system();
+  if (lane < ps.nranks)
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ps.flags[lane] + ps.rank), "l"(e)
+                 : "memory");
+  if (lane < ps.nranks && lane != ps.rank) {
+    const unsigned long long* f = ps.flags[ps.rank] + lane;
+    const uint64_t t0 = dev::globaltimer_ns();
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+      if (v >= e) break;
+      if (dev::globaltimer_ns() - t0 > dev::kWaitTimeoutNs) {
+        dev::record_error(dev::kDevErrWaitTimeout);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncwarp();
+}
+
 }  // namespace kern
 }  // namespace clove

@@ -114,7 +114,7 @@ template <class Op, bool GLU = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC,
-                    int M, int N, int K, EpiParams ep, SkParams sk) {
+                    int M, int N, int K, const __grid_constant__ EpiParams ep, SkParams sk) {
   using S = Tc2Shape<Op>;
   static_assert(!GLU || !Op::kInt, "GLU epilogue is fp16");
   constexpr int TILE_N = GLU ? S::BNH : S::BN;  // output columns per pair tile
@@ -408,7 +408,12 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (*abort_flag) break;
     }
-    if (lane == 0) dev::bulk_wait_group<0>();
+    if (lane == 0) {
+      dev::bulk_wait_group<0>();
+      // Replicated output: the completed remote stores are ordered before the
+      // cross-rank signal that follows the kernel on the stream.
+      if (ep.peer.count > 0) __threadfence_system();
+    }
     __syncwarp();
   }
 

@@ -17,6 +17,9 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_tc)
 
+int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int swizzle,
+                     kern::PeerOut* out);
+
 }  // namespace rt
 }  // namespace clove
 
@@ -126,7 +129,10 @@ bool gemm_tc_supported(int op, int bn, int split, int out_bytes) {
 
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
-                   const DeviceInfo& dev, cudaStream_t stream, int batch) {
+                   const DeviceInfo& dev, cudaStream_t stream, int batch,
+                   const PeerTargets* peer) {
+  if (peer != nullptr && (batch > 1 || split > 1 || out_bytes != 2))
+    return CLOVE_ERR_UNSUPPORTED;  // replicated output: plain fp16 tiles only
   if (batch < 1 || (batch > 1 && split > 1))
     return fail(CLOVE_ERR_UNSUPPORTED, "batched tiles need split 1 (batch %d split %d)", batch, split);
   const int ei = find_entry(op, bn, split, out_bytes);
@@ -174,6 +180,11 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   EpiParams epv = ep;
   epv.c_out = C;
+  epv.peer.count = 0;
+  if (peer != nullptr) {
+    rc = encode_peer_maps(*peer, M, N, static_cast<uint32_t>(e->chunk), e->stg_row, &epv.peer);
+    if (rc) return rc;
+  }
   void* args[] = {&tmA, &tmB, &tmC, &M, &N, &K, &batch, &a_rows, &epv};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -204,6 +215,23 @@ int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, cons
 
 namespace clove {
 namespace rt {
+
+// One TMA store map per rank for the replicated output: rank d's C from column 0
+// to this rank's last column (col0 + N), rows M, row pitch ldc; the box and swizzle
+// of the kernel's own C store.
+int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int swizzle,
+                     kern::PeerOut* out) {
+  if (pt.count > kern::kMaxPeers) return fail(CLOVE_ERR_UNSUPPORTED, "too many ranks");
+  out->count = pt.count;
+  out->col0 = pt.col0;
+  for (int d = 0; d < pt.count; ++d) {
+    const int rc = encode_tmap_2d(&out->maps[d], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pt.dst[d],
+                                  static_cast<uint64_t>(pt.col0) + N, M,
+                                  static_cast<uint64_t>(pt.ldc) * 2, box_cols, 32, swizzle);
+    if (rc) return rc;
+  }
+  return CLOVE_OK;
+}
 
 namespace {
 std::atomic<uint64_t> g_tc2_attr[3];
@@ -282,7 +310,8 @@ SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force) {
 // CTA-pair 256 x 256 tile kernel (fp16 C only).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
-                    const void* B2) {
+                    const void* B2, const PeerTargets* peer) {
+  if (peer != nullptr && (B2 != nullptr || op != kTcF16)) return CLOVE_ERR_UNSUPPORTED;
   using SF = kern::Tc2Shape<kern::OpF16>;
   using SI = kern::Tc2Shape<kern::OpI8>;
   const bool f16 = op == kTcF16;
@@ -324,6 +353,11 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
   const int tile_n = glu ? 128 : 256;
   const int tiles = ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
   kern::EpiParams epv = ep;
+  epv.peer.count = 0;
+  if (peer != nullptr) {
+    rc = encode_peer_maps(*peer, M, N, 64, 128, &epv.peer);
+    if (rc) return rc;
+  }
   kern::SkParams skp = {};
   void* args[] = {&tmA, &tmB, &tmB2, &tmC, &M, &N, &K, &epv, &skp};
   cudaLaunchConfig_t cfg = {};

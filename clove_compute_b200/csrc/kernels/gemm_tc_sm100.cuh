@@ -118,7 +118,7 @@ __device__ __forceinline__ void epi_pack(const uint32_t (&v)[CHUNK], const EpiPa
                                          int ncol0, int M, int N, int K, float row_scale,
                                          int32_t row_corr,
                                          uint32_t (&pk)[CHUNK * OUT_BYTES / 16][4],
-                                         const uint32_t* colv = nullptr) {
+                                         const uint32_t* colv = nullptr, size_t c_off = 0) {
   constexpr int PKTS = CHUNK * OUT_BYTES / 16;
   if constexpr (OUT_BYTES == 2) {
     float f[CHUNK];
@@ -126,7 +126,7 @@ __device__ __forceinline__ void epi_pack(const uint32_t (&v)[CHUNK], const EpiPa
 #pragma unroll
       for (int j = 0; j < CHUNK; ++j) f[j] = ep.alpha * __uint_as_float(v[j]);
       if (ep.beta != 0.f && row < M) {
-        const __half* crow = ep.c_in + static_cast<size_t>(row) * N;
+        const __half* crow = ep.c_in + c_off + static_cast<size_t>(row) * N;
 #pragma unroll
         for (int j = 0; j < CHUNK; j += 8) {
           if (ncol0 + j < N) {  // N % 8 == 0 on this path
@@ -193,7 +193,10 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
   constexpr int STG_ROW = CHUNK * OUT_BYTES;
   constexpr int PKTS = STG_ROW / 16;
   uint32_t pk[PKTS][4];
-  epi_pack<Op, OUT_BYTES, CHUNK>(v, ep, row, ncol0, M, N, K, row_scale, row_corr, pk);
+  // Batch plane p reads its beta source from plane p of C.
+  const size_t c_off = plane > 0 ? static_cast<size_t>(plane) * M * N : 0;
+  epi_pack<Op, OUT_BYTES, CHUNK>(v, ep, row, ncol0, M, N, K, row_scale, row_corr, pk, nullptr,
+                                 c_off);
 
   // Stage through swizzled smem and TMA-store this warp's 32-row slab.
   uint8_t* stg = stg_base + (stg_count & 1u) * 4096;
@@ -212,6 +215,14 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
       dev::tma_store_2d(tmC, stg, ncol0, store_row0);
     else            // 3D [batch, M, N] map
       dev::tma_store_3d(tmC, stg, ncol0, store_row0, plane);
+    if constexpr (OUT_BYTES == 2) {
+      // Replicated output (never with batch planes): the same staged tile to every
+      // rank's C. `ep` is the kernel's __grid_constant__ parameter here, so the
+      // maps are addressed in parameter space.
+#pragma unroll 1
+      for (int d = 0; d < ep.peer.count; ++d)
+        dev::tma_store_2d(&ep.peer.maps[d], stg, ep.peer.col0 + ncol0, store_row0);
+    }
     dev::bulk_commit_group();
   }
   ++stg_count;
@@ -238,19 +249,11 @@ __device__ __forceinline__ void store_row_direct(const uint32_t (&v)[CHUNK], con
   }
 }
 
-// Epilogue parameters of batch plane `plane`: the beta source moves with C (the
-// batched entry is fp16 only; the int8 per-row / per-column vectors are unbatched).
-__device__ __forceinline__ EpiParams ep_plane(const EpiParams& ep, int plane, int M, int N) {
-  EpiParams e = ep;
-  if (e.c_in != nullptr) e.c_in += static_cast<size_t>(plane) * M * N;
-  return e;
-}
-
 template <class Op, int BN, bool SPLIT, int OUT_BYTES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int batch,
-                   int a_rows, EpiParams ep) {
+                   int a_rows, const __grid_constant__ EpiParams ep) {
   using S = TcShape<Op, BN, SPLIT, OUT_BYTES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = dev::align_smem_1024(smem_raw);
@@ -596,16 +599,20 @@ __global__ void __launch_bounds__(192, 1)
             __syncwarp();
             if (lane == 0) dev::mbar_arrive(&tempty[buf]);
           }
-          store_chunk<Op, OUT_BYTES, S::CHUNK>(v, plane == 0 ? ep : ep_plane(ep, plane, M, N), row,
-                                               n0 + c0, M, N, K, row_scale, row_corr, lane,
-                                               stg_base, stg_count, &tmC,
+          store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr,
+                                               lane, stg_base, stg_count, &tmC,
                                                m0 + static_cast<int>(q) * 32, plane);
         }
       }
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);
       if (*abort_flag) break;
     }
-    if (lane == 0) dev::bulk_wait_group<0>();
+    if (lane == 0) {
+      dev::bulk_wait_group<0>();
+      // Replicated output: the completed remote stores are ordered before the
+      // cross-rank signal that follows the kernel on the stream.
+      if (ep.peer.count > 0) __threadfence_system();
+    }
     if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(8);
     if (lane == 0) CLOVE_TRACE_MAX(20);
     __syncwarp();

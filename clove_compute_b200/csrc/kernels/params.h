@@ -1,6 +1,7 @@
 // params.h -- plain parameter structs shared by the kernels and the host launchers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 
@@ -12,6 +13,19 @@ enum EpiMode : int {
   kEpiI8Tensor = 1,      // C = half(float(acc') * scale)
   kEpiI8RowCol = 2,      // C = half(float(acc) * row_scale[m] * col_scale[n])
   kEpiI32Raw = 3,        // C(int32) = acc'  (acc' = zero-point corrected acc)
+};
+
+// Replicated output of an N-split GEMM: every fp16 tile the kernel finishes is
+// also TMA-stored, from the same staged shared-memory tile as the local store,
+// into the row-major C of each rank (this rank's own and its peers', mapped
+// through CUDA IPC; NVLink carries the remote stores), at columns col0 + n. Map d
+// spans columns [0, col0 + N) of rank d's C, so the box clips at this rank's last
+// column. count == 0: no replicated output.
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+  int count;
+  int col0;
+  CUtensorMap maps[kMaxPeers];
 };
 
 // Epilogue of the tensor-core tile kernels.
@@ -26,6 +40,7 @@ struct EpiParams {
   const int32_t* row_sum;   // sum_k A[m,k]   (required when zb != 0)
   const int32_t* col_sum;   // sum_k B[k,n]   (required when za != 0)
   void* c_out;              // C itself (split-K tiles store rows directly)
+  PeerOut peer;             // replicated output (fp16 C only)
 };
 
 // Stream-K schedule of the CTA-pair kernel. Tiles [0, dp_tiles) go round-robin to
@@ -33,7 +48,8 @@ struct EpiParams {
 // sk_tiles), taken tile after tile, are cut into one contiguous range per pair of
 // equal length, so every pair ends at the same time; a tile cut between several
 // pairs is summed by whichever contributor finishes last (an atomic ticket), from
-// 32-bit partial accumulators in `partials`. sk_tiles == 0: plain persistent tiles.
+// 32-bit partial accumulators in `partials`. Each pair works through its stream-K
+// range before its whole-K tiles. sk_tiles == 0: plain persistent tiles.
 struct SkParams {
   int dp_tiles;
   int sk_tiles;

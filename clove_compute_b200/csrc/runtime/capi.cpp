@@ -196,8 +196,11 @@ int clove_set_dispatch_override(int path, int bn, int split) {
 // ---------------------------------------------------------------------------
 // FP16
 // ---------------------------------------------------------------------------
+// peer != nullptr: the N-split replicated output (PeerOut); only the tensor-core
+// tile kernels store it, so any other path returns CLOVE_ERR_UNSUPPORTED untouched.
 static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
-                          float beta, cudaStream_t s, const char** chosen) {
+                          float beta, cudaStream_t s, const char** chosen,
+                          const PeerTargets* peer = nullptr) {
   if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
   if (M == 0 || N == 0) return CLOVE_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
@@ -218,6 +221,7 @@ static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, i
   if ((path == 1 || path == 4) && !tc_ok) path = 0;
   if (path == 2 && !gemv_ok) path = 0;
   if (path == 0) path = (gemv_ok && N < 16) ? 2 : (tc_ok ? 1 : 3);
+  if (peer != nullptr && path != 1 && path != 4) return CLOVE_ERR_UNSUPPORTED;
   if (path == 2) {
     if (chosen) *chosen = "gemv_f16";
     return launch_gemv_f16(A, B, C, M, N, K, alpha, beta, dev, s);
@@ -233,8 +237,19 @@ static int gemm_fp16_impl(const void* A, const void* B, void* C, int M, int N, i
   ep.alpha = alpha;
   ep.beta = beta;
   ep.c_in = static_cast<const __half*>(C);
-  if (plan.pair) return launch_gemm_tc2(kTcF16, A, B, C, M, N, K, ep, dev, s);
-  return launch_gemm_tc(kTcF16, plan.bn, plan.split, 2, A, B, C, M, N, K, ep, dev, s);
+  if (plan.pair) return launch_gemm_tc2(kTcF16, A, B, C, M, N, K, ep, dev, s, nullptr, peer);
+  return launch_gemm_tc(kTcF16, plan.bn, plan.split, 2, A, B, C, M, N, K, ep, dev, s, 1, peer);
+}
+
+extern "C++" {  // internal C++ entry (nsplit.cpp), inside this file's extern "C" block
+namespace clove {
+namespace rt {
+int gemm_fp16_replicated(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                         const PeerTargets& peer, cudaStream_t s) {
+  return gemm_fp16_impl(A, B, C, M, N, K, alpha, 0.f, s, nullptr, &peer);
+}
+}  // namespace rt
+}  // namespace clove
 }
 
 int clove_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,

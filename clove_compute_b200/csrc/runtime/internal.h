@@ -48,6 +48,16 @@ bool ws_disabled();
 // instead of the default direct-load one.
 bool ws2_selected();
 
+// Replicated output of an N-split fp16 GEMM (kern::PeerOut): the row-major
+// [M, ldc] C of every rank, mapped into this process; this rank's columns start
+// at col0. The tile launchers encode one TMA store map per rank from it.
+struct PeerTargets {
+  int count;
+  int ldc;
+  int col0;
+  void* dst[8];
+};
+
 // Tile shape chosen for a tensor-core call (capi.cpp).
 struct TcPlan {
   int bn;
@@ -64,7 +74,8 @@ enum TcOp { kTcF16 = 0, kTcI8 = 1 };
 // persistent launch (split must be 1).
 int launch_gemm_tc(int op, int bn, int split, int out_bytes, const void* A, const void* B,
                    void* C, int M, int N, int K, const kern::EpiParams& ep,
-                   const DeviceInfo& dev, cudaStream_t stream, int batch = 1);
+                   const DeviceInfo& dev, cudaStream_t stream, int batch = 1,
+                   const PeerTargets* peer = nullptr);
 // Stream-K schedule of the CTA-pair kernel (kern::SkParams); pairs = CTA pairs to
 // launch. force: 0 auto, 1 never, 2 whenever the tiles leave a partial wave.
 struct SkPlan {
@@ -75,7 +86,7 @@ SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force);
 // B2 != nullptr: fp16 GLU, C = silu(A . B) * (A . B2) (256 x 128 output tiles).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
-                    const void* B2 = nullptr);
+                    const void* B2 = nullptr, const PeerTargets* peer = nullptr);
 // True when (op, bn, split, out_bytes) is an instantiated kernel.
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();

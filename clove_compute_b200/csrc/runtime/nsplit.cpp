@@ -8,9 +8,16 @@
 // (padded) C shards into a stream-ordered staging buffer, then a re-layout kernel
 // scatters the column blocks into row-major C [M,N].
 //
+// A replicated C registered with clove_nsplit_register_output (every rank's C
+// mapped into every rank through CUDA IPC) skips the collective altogether: the
+// fp16 GEMM's epilogue stores each finished tile into all ranks' C over NVLink
+// while the remaining tiles compute, and a one-warp kernel then exchanges
+// completion flags (system-scope release / acquire on IPC-mapped flag arrays).
+//
 // NCCL is opened with dlopen on first use so that loading this library never pins
 // an NCCL build into the process (PyTorch ships its own; whichever libnccl.so.2 is
 // already loaded is reused).
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -18,23 +25,46 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "internal.h"
+#include "../kernels/params.h"
 
 namespace clove {
+namespace kern {
+struct PeerSync;
+}  // namespace kern
 namespace rt {
 int launch_relayout_columns(const void* staging, void* C, int M, int N, int P, int Nmax,
                             int elem_bytes, cudaStream_t stream);
+int launch_peer_signal_wait(int nranks, int rank, unsigned long long* epoch,
+                            unsigned long long* const* flags, cudaStream_t stream);
+int gemm_fp16_replicated(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                         const PeerTargets& peer, cudaStream_t s);
 }  // namespace rt
 }  // namespace clove
 
 using namespace clove::rt;
+using clove::kern::kMaxPeers;
+
+namespace {
+// One IPC-shared buffer: this rank's pointer and every rank's, mapped here.
+struct SharedBuf {
+  void* local = nullptr;
+  size_t bytes = 0;
+  void* opened[kMaxPeers] = {};  // IPC mapping bases (to close), null for this rank
+  void* ptr[kMaxPeers] = {};     // every rank's buffer as seen from this process
+};
+}  // namespace
 
 struct clove_nsplit_ctx {
   ncclComm_t comm;
   int rank;
   int nranks;
   int device;
+  std::vector<SharedBuf> outputs;  // registered replicated outputs
+  SharedBuf flags;                 // [nranks] completion flags + this rank's epoch
+  bool flags_ready = false;
 };
 
 namespace {
@@ -126,9 +156,197 @@ int gather_columns(clove_nsplit_ctx* ctx, const void* C_shard, void* C_full, int
   return rc ? rc : rc2;
 }
 
+// ---- CUDA IPC sharing of device buffers among the ranks ------------------------
+
+typedef CUresult (*PfnMemGetAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+PfnMemGetAddressRange g_get_range = nullptr;
+std::once_flag g_range_once;
+
+struct IpcRecord {
+  cudaIpcMemHandle_t handle;
+  unsigned long long offset;  // of the shared pointer inside its allocation
+  unsigned long long bytes;
+};
+
+// Collective: every rank passes a device pointer of `bytes` bytes (any offset inside
+// a cudaMalloc allocation, such as a PyTorch tensor); on return out->ptr[q] is rank
+// q's pointer mapped into this process.
+int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* out) {
+  std::call_once(g_range_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_get_range = reinterpret_cast<PfnMemGetAddressRange>(fn);
+  });
+  if (g_get_range == nullptr) return fail(CLOVE_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  const int P = ctx->nranks;
+  IpcRecord mine = {};
+  CUdeviceptr base = 0;
+  size_t range = 0;
+  if (g_get_range(&base, &range, reinterpret_cast<CUdeviceptr>(local)) != CUDA_SUCCESS)
+    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer is not device memory of this process");
+  mine.offset = reinterpret_cast<CUdeviceptr>(local) - base;
+  mine.bytes = bytes;
+  if (mine.offset + bytes > range)
+    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer runs past its allocation");
+  int rc = check_cuda(cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)),
+                      "cudaIpcGetMemHandle (buffer must come from cudaMalloc)");
+  if (rc) return rc;
+  // All-gather the records through NCCL on a private stream.
+  cudaStream_t s = nullptr;
+  rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc) return rc;
+  std::vector<IpcRecord> all(P);
+  void* dbuf = nullptr;
+  rc = check_cuda(cudaMalloc(&dbuf, sizeof(IpcRecord) * (P + 1)), "cudaMalloc(ipc records)");
+  if (!rc)
+    rc = check_cuda(cudaMemcpyAsync(static_cast<char*>(dbuf) + sizeof(IpcRecord) * P, &mine,
+                                    sizeof(mine), cudaMemcpyHostToDevice, s),
+                    "cudaMemcpyAsync(ipc record)");
+  if (!rc)
+    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(dbuf) + sizeof(IpcRecord) * P, dbuf,
+                                     sizeof(IpcRecord), ncclChar, ctx->comm, s),
+                    "ncclAllGather(ipc records)");
+  if (!rc)
+    rc = check_cuda(cudaMemcpyAsync(all.data(), dbuf, sizeof(IpcRecord) * P,
+                                    cudaMemcpyDeviceToHost, s),
+                    "cudaMemcpyAsync(ipc records)");
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(ipc records)");
+  if (dbuf) cudaFree(dbuf);
+  cudaStreamDestroy(s);
+  if (rc) return rc;
+  SharedBuf sb;
+  sb.local = local;
+  sb.bytes = bytes;
+  for (int q = 0; q < P && !rc; ++q) {
+    if (all[q].bytes != bytes) {
+      rc = fail(CLOVE_ERR_INVALID_ARG, "ranks registered buffers of different sizes");
+    } else if (q == ctx->rank) {
+      sb.ptr[q] = local;
+    } else {
+      void* b = nullptr;
+      rc = check_cuda(cudaIpcOpenMemHandle(&b, all[q].handle, cudaIpcMemLazyEnablePeerAccess),
+                      "cudaIpcOpenMemHandle");
+      if (!rc) {
+        sb.opened[q] = b;
+        sb.ptr[q] = static_cast<char*>(b) + all[q].offset;
+      }
+    }
+  }
+  if (rc) {
+    for (int q = 0; q < P; ++q)
+      if (sb.opened[q]) cudaIpcCloseMemHandle(sb.opened[q]);
+    return rc;
+  }
+  *out = sb;
+  return CLOVE_OK;
+}
+
+void close_shared(SharedBuf* sb) {
+  for (int q = 0; q < kMaxPeers; ++q)
+    if (sb->opened[q]) cudaIpcCloseMemHandle(sb->opened[q]);
+  *sb = SharedBuf();
+}
+
+// Collective barrier on the communicator (one tiny all-gather, host-synchronous).
+int host_barrier(clove_nsplit_ctx* ctx) {
+  cudaStream_t s = nullptr;
+  int rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc) return rc;
+  void* d = nullptr;
+  rc = check_cuda(cudaMalloc(&d, 4 * (ctx->nranks + 1)), "cudaMalloc(barrier)");
+  if (!rc)
+    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(d) + 4 * ctx->nranks, d, 4, ncclChar,
+                                     ctx->comm, s),
+                    "ncclAllGather(barrier)");
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(barrier)");
+  if (d) cudaFree(d);
+  cudaStreamDestroy(s);
+  return rc;
+}
+
+const SharedBuf* find_output(const clove_nsplit_ctx* ctx, const void* C_full) {
+  for (const SharedBuf& b : ctx->outputs)
+    if (b.local == C_full) return &b;
+  return nullptr;
+}
+
+// Replicated fp16 output without a collective (see the file comment). Returns
+// CLOVE_ERR_UNSUPPORTED, with nothing launched, when the shapes or the kernel the
+// dispatch picks cannot store into the replicated C directly; the caller then
+// falls back to the all-gather.
+int gemm_fp16_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const void* A,
+                       const void* B_shard, void* C_shard, int M, int N, int K, float alpha,
+                       cudaStream_t s) {
+  const int P = ctx->nranks;
+  const int col0 = clove_nsplit_col_begin(N, P, ctx->rank);
+  const int Nr = shard_cols(N, P, ctx->rank);
+  if (P > kMaxPeers || N % 8 != 0 || col0 % 8 != 0 || Nr % 8 != 0 || Nr == 0 ||
+      out.bytes < static_cast<size_t>(M) * N * 2)
+    return CLOVE_ERR_UNSUPPORTED;
+  PeerTargets peer = {};
+  peer.count = P;
+  peer.ldc = N;
+  peer.col0 = col0;
+  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
+  int rc = gemm_fp16_replicated(A, B_shard, C_shard, M, Nr, K, alpha, peer, s);
+  if (rc) return rc;
+  unsigned long long* fl[kMaxPeers] = {};
+  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
+  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
+  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+}
+
 }  // namespace
 
 extern "C" {
+
+int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes) {
+  if (ctx == nullptr || C_full == nullptr || bytes == 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "bad register_output arguments");
+  if (ctx->nranks > kMaxPeers)
+    return fail(CLOVE_ERR_UNSUPPORTED, "replicated output supports up to %d ranks", kMaxPeers);
+  if ((reinterpret_cast<uintptr_t>(C_full) & 15u) != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "replicated C must be 16-byte aligned");
+  if (find_output(ctx, C_full) != nullptr)
+    return fail(CLOVE_ERR_INVALID_ARG, "buffer already registered");
+  int rc = CLOVE_OK;
+  if (!ctx->flags_ready) {
+    // Flag slots [kMaxPeers] then this rank's epoch, zeroed before anyone signals.
+    void* f = nullptr;
+    const size_t fb = sizeof(unsigned long long) * (kMaxPeers + 1);
+    rc = check_cuda(cudaMalloc(&f, fb), "cudaMalloc(flags)");
+    if (!rc) rc = check_cuda(cudaMemset(f, 0, fb), "cudaMemset(flags)");
+    if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(flags)");
+    if (!rc) rc = share_buffer(ctx, f, fb, &ctx->flags);
+    if (rc) {
+      if (f) cudaFree(f);
+      return rc;
+    }
+    ctx->flags_ready = true;
+  }
+  SharedBuf sb;
+  rc = share_buffer(ctx, C_full, bytes, &sb);
+  if (rc) return rc;
+  ctx->outputs.push_back(sb);
+  return CLOVE_OK;
+}
+
+int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full) {
+  if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
+  for (size_t i = 0; i < ctx->outputs.size(); ++i) {
+    if (ctx->outputs[i].local == C_full) {
+      int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(unregister)");
+      close_shared(&ctx->outputs[i]);
+      ctx->outputs.erase(ctx->outputs.begin() + static_cast<long>(i));
+      // No rank frees its buffer while another still has it mapped.
+      const int rc2 = host_barrier(ctx);
+      return rc ? rc : rc2;
+    }
+  }
+  return fail(CLOVE_ERR_INVALID_ARG, "buffer is not registered");
+}
 
 int clove_nsplit_col_begin(int N, int nranks, int rank) {
   if (nranks <= 0) return 0;
@@ -172,7 +390,23 @@ int clove_nsplit_init(clove_nsplit_ctx** ctx, int nranks, int rank, const uint8_
 int clove_nsplit_destroy(clove_nsplit_ctx* ctx) {
   if (ctx == nullptr) return CLOVE_OK;
   int rc = CLOVE_OK;
-  if (g_nccl.handle) rc = check_nccl(g_nccl.CommDestroy(ctx->comm), "ncclCommDestroy");
+  if (!ctx->outputs.empty() || ctx->flags_ready) {
+    rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(destroy)");
+    for (SharedBuf& b : ctx->outputs) close_shared(&b);
+    ctx->outputs.clear();
+    if (ctx->flags_ready) {
+      void* f = ctx->flags.local;
+      close_shared(&ctx->flags);
+      const int rc2 = host_barrier(ctx);  // peers unmapped our flags before we free them
+      cudaFree(f);
+      if (!rc) rc = rc2;
+      ctx->flags_ready = false;
+    }
+  }
+  if (g_nccl.handle) {
+    const int rc3 = check_nccl(g_nccl.CommDestroy(ctx->comm), "ncclCommDestroy");
+    if (!rc) rc = rc3;
+  }
   delete ctx;
   return rc;
 }
@@ -190,6 +424,12 @@ int clove_nsplit_gemm_fp16(clove_nsplit_ctx* ctx, const void* A, const void* B_s
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int Nr = shard_cols(N, ctx->nranks, ctx->rank);
+  if (replicate_C && C_full != nullptr && K > 0) {
+    if (const SharedBuf* out = find_output(ctx, C_full)) {
+      const int rc = gemm_fp16_to_peers(ctx, *out, A, B_shard, C_shard, M, N, K, alpha, s);
+      if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
+    }
+  }
   int rc = Nr > 0 ? clove_gemm_fp16(A, B_shard, C_shard, M, Nr, K, alpha, 0.f, stream) : CLOVE_OK;
   if (rc || !replicate_C) return rc;
   if (C_full == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "C_full is NULL with replicate_C");

@@ -3,9 +3,12 @@
 Rank r owns columns ``[col_begin(N, P, r), col_begin(N, P, r+1))`` of B and C
 (rows of B_q for the K-packed INT4 layout); A is replicated. Each rank runs the
 single-GPU kernel on its shard; with ``replicate_C`` the shards are all-gathered
-over NCCL (NVLink) into the full row-major C on every rank. The NCCL
-communicator belongs to the C library; its unique id is exchanged through the
-torch.distributed store of the already-initialised process group.
+over NCCL (NVLink) into the full row-major C on every rank. A C registered with
+``register_output`` (a collective that maps it into every rank through CUDA IPC)
+is instead filled by the fp16 GEMM's own epilogue, which stores each finished
+tile into every rank's copy over NVLink. The NCCL communicator belongs to the C
+library; its unique id is exchanged through the torch.distributed store of the
+already-initialised process group.
 """
 from __future__ import annotations
 
@@ -40,11 +43,27 @@ class NSplit:
         ctx = ctypes.c_void_p()
         check(lib().clove_nsplit_init(ctypes.byref(ctx), self.nranks, self.rank, uid))
         self._ctx = ctx
+        self._outputs = {}
 
     def close(self) -> None:
         if getattr(self, "_ctx", None) is not None and self._ctx.value:
             check(lib().clove_nsplit_destroy(self._ctx))
             self._ctx = None
+            self._outputs = {}
+
+    def register_output(self, C_full: torch.Tensor) -> None:
+        """Collective: every rank registers its own [M, N] fp16 replicated output in
+        the same order; gemm_fp16(..., C_full=C_full, replicate_C=True) then writes
+        every rank's copy from the GEMM epilogue (no all-gather)."""
+        _need(C_full, "C_full", torch.float16, 2)
+        check(lib().clove_nsplit_register_output(self._ctx, _ptr(C_full),
+                                                 C_full.numel() * C_full.element_size()))
+        self._outputs[C_full.data_ptr()] = C_full  # keeps the memory alive while mapped
+
+    def unregister_output(self, C_full: torch.Tensor) -> None:
+        """Collective: unmaps C_full on every rank."""
+        check(lib().clove_nsplit_unregister_output(self._ctx, _ptr(C_full)))
+        self._outputs.pop(C_full.data_ptr(), None)
 
     def __del__(self):
         try:

@@ -189,6 +189,19 @@ int clove_nsplit_init(clove_nsplit_ctx** ctx, int nranks, int rank, const uint8_
 int clove_nsplit_destroy(clove_nsplit_ctx* ctx);
 int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
 
+/* Collective (every rank, same order, same byte count): maps this rank's
+ * replicated-output buffer C_full (device memory from cudaMalloc, at any offset,
+ * e.g. a PyTorch tensor; 16-byte aligned) into every other rank through CUDA IPC.
+ * Afterwards clove_nsplit_gemm_fp16 with replicate_C = 1 and this C_full stores
+ * each finished fp16 tile straight into every rank's C_full over NVLink (no
+ * all-gather, no staging) and ends with a cross-rank completion signal; shapes
+ * it cannot serve that way (N, a shard edge or N_r not a multiple of 8, or a
+ * kernel without the tile epilogue) still take the NCCL all-gather. At most 8
+ * ranks. (Extension; no counterpart in the reference.) */
+int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes);
+/* Collective: unmaps C_full everywhere; returns once no rank maps it any more. */
+int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full);
+
 /* B_shard [K, N_r] row-major; C_shard [M, N_r]; C_full [M,N] (only with
  * replicate_C, may be NULL otherwise). */
 int clove_nsplit_gemm_fp16(clove_nsplit_ctx* ctx, const void* A, const void* B_shard,

@@ -76,3 +76,86 @@ def test_nsplit_two_gpus(clove_lib, cuda):
     for r in range(2):
         assert res[r][0] == "ok", res[r]
         assert all(e < 2e-3 for e in res[r][1]), res[r]
+
+
+def _worker_fused(rank, world, port, q):
+    """Replicated C through the GEMM epilogue (clove_nsplit_register_output)."""
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import clove_compute_b200 as cc
+        import oracle
+        from clove_compute_b200 import workloads as wl
+        ns = cc.NSplit(rank, world)
+        out = []
+        # (M, N, K): CTA-pair tiles, the one-SM tile kernel, a ragged M, and
+        # N = 1000 whose shard edge (500) is not a multiple of 8 -> all-gather.
+        for (M, N, K) in [(2048, 2048, 1024), (512, 2048, 1024), (300, 1024, 512),
+                          (256, 1000, 512)]:
+            A, B = wl.fp16_operands(M, N, K, seed=M + N)
+            c0, c1 = ns.cols(N)
+            Ad = torch.from_numpy(A).cuda()
+            Bs = torch.from_numpy(np.ascontiguousarray(B[:, c0:c1])).cuda()
+            C_full = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+            ns.register_output(C_full)
+            ref = oracle.gemm_fp16(A, B)
+            for _ in range(2):  # the completion epochs advance call by call
+                C_full.fill_(float("nan"))
+                dist.barrier()
+                ns.gemm_fp16(Ad, Bs, N, C_full=C_full, replicate_C=True)
+                torch.cuda.synchronize()
+                h = C_full.cpu().numpy().astype(np.float64)
+                out.append(float(np.linalg.norm(h - ref) / np.linalg.norm(ref)))
+            # Replays of a captured call (the epoch lives on the device).
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    ns.gemm_fp16(Ad, Bs, N, C_full=C_full, replicate_C=True, stream=s)
+            for _ in range(3):
+                C_full.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
+                g.replay()
+                torch.cuda.synchronize()
+                h = C_full.cpu().numpy().astype(np.float64)
+                out.append(float(np.linalg.norm(h - ref) / np.linalg.norm(ref)))
+            del g
+            dist.barrier()
+            ns.unregister_output(C_full)
+        err = cc.device_error()
+        ns.close()
+        q.put((rank, "ok", out + [float(err)]))
+    except Exception as e:
+        q.put((rank, "error", repr(e)[:300]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nsplit_replicated_output_two_gpus(clove_lib, cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_fused, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (k, v)) for r, k, v in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert res[r][0] == "ok", res[r]
+        errs, dev_err = res[r][1][:-1], res[r][1][-1]
+        assert dev_err == 0, res[r]
+        assert all(e < 2e-3 for e in errs), res[r]  # NaN fill: any tile left unwritten fails
