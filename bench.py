@@ -433,6 +433,70 @@ def _secondary(cc, torch, peaks):
     return out
 
 
+def _replicated(cc, torch, dist, world, rank):
+    """Config 4's FFN up (11008 x 2048 x 4096) split over the ranks' token columns with
+    the output C [11008, 2048] replicated on every rank: the shard GEMM alone, the
+    GEMM whose epilogue stores every tile into all ranks' C (registered output, CUDA
+    IPC over NVLink), and the shard GEMM + NCCL all-gather + re-layout. Per call,
+    device time (CUDA events, max over ranks), median of 3 batches of 20 calls."""
+    M, N, K = UP
+    ns = cc.NSplit(rank, world)
+    c0, c1 = ns.cols(N)
+    g = torch.Generator(device="cuda").manual_seed(7)  # same operands on every rank
+    A = (torch.randn((M, K), device="cuda", generator=g) / K ** 0.5).half()
+    B = torch.randn((K, N), device="cuda", generator=g).half()
+    Bs = B[:, c0:c1].contiguous()
+    Cs = torch.empty((M, c1 - c0), dtype=torch.float16, device="cuda")
+    Cn = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    Cf = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    err = ""
+    try:
+        ns.register_output(Cf)
+    except Exception as e:  # reported below; every rank then skips the fused path
+        err = repr(e)[:200]
+    ok = torch.tensor([0 if err else 1], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    fns = {"shard_only": lambda: ns.gemm_fp16(A, Bs, N, C_shard=Cs),
+           "nccl_all_gather": lambda: ns.gemm_fp16(A, Bs, N, C_shard=Cs, C_full=Cn,
+                                                   replicate_C=True)}
+    if ok.item():
+        fns["epilogue_to_peers"] = lambda: ns.gemm_fp16(A, Bs, N, C_shard=Cs, C_full=Cf,
+                                                        replicate_C=True)
+    times = {k: [] for k in fns}
+    for _ in range(3):
+        for k, fn in fns.items():
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                fn()
+            e1.record()
+            e1.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1e3 / 20], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times[k].append(t.item())
+    out = {"shape": {"M": M, "N": N, "K": K, "columns_per_rank": c1 - c0},
+           "us_per_call": {k: round(statistics.median(v), 2) for k, v in times.items()},
+           "replicated_bytes_per_rank": M * N * 2}
+    if ok.item():
+        same = torch.tensor([1 if torch.equal(Cn, Cf) else 0], device="cuda")
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        out["epilogue_equals_all_gather"] = bool(same.item())
+        t_f = out["us_per_call"]["epilogue_to_peers"]
+        out["TFLOPS_epilogue_to_peers"] = round(2 * M * N * K / t_f * 1e-6, 1)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.unregister_output(Cf)
+    else:
+        out["epilogue_to_peers"] = f"unavailable: {err or 'another rank could not register'}"
+    out["device_error"] = cc.device_error()
+    ns.close()
+    return out
+
+
 def run_case(args):
     """Profiling mode (--case): a few plain launches of one secondary configuration,
     no graphs, no output; the command line ncu captures."""
@@ -637,6 +701,10 @@ def run_gpu(args):
         }
     if world == 1 and rank == 0 and not args.no_secondary:
         line["secondary"] = _secondary(cc, torch, peaks)
+    if world > 1 and not args.no_secondary:
+        rep = _replicated(cc, torch, dist, world, rank)  # collective: every rank
+        if rank == 0:
+            line["replicated_output"] = rep
     if world == 1 and rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = _cpu_ffn_sample(args.cpu_frac, min_seconds=10.0, max_reps=400)
     if rank == 0:

@@ -170,7 +170,9 @@ struct IpcRecord {
 
 // Collective: every rank passes a device pointer of `bytes` bytes (any offset inside
 // a cudaMalloc allocation, such as a PyTorch tensor); on return out->ptr[q] is rank
-// q's pointer mapped into this process.
+// q's pointer mapped into this process. Every rank reaches the all-gather even when
+// its own part failed (it then sends an empty record), so that a local error never
+// leaves the other ranks waiting inside NCCL; all ranks then fail together.
 int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* out) {
   std::call_once(g_range_once, [] {
     void* fn = nullptr;
@@ -179,23 +181,28 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
             cudaSuccess && q == cudaDriverEntryPointSuccess)
       g_get_range = reinterpret_cast<PfnMemGetAddressRange>(fn);
   });
-  if (g_get_range == nullptr) return fail(CLOVE_ERR_CUDA, "cuMemGetAddressRange unavailable");
   const int P = ctx->nranks;
   IpcRecord mine = {};
+  int local_rc = CLOVE_OK;
   CUdeviceptr base = 0;
   size_t range = 0;
-  if (g_get_range(&base, &range, reinterpret_cast<CUdeviceptr>(local)) != CUDA_SUCCESS)
-    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer is not device memory of this process");
-  mine.offset = reinterpret_cast<CUdeviceptr>(local) - base;
-  mine.bytes = bytes;
-  if (mine.offset + bytes > range)
-    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer runs past its allocation");
-  int rc = check_cuda(cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)),
-                      "cudaIpcGetMemHandle (buffer must come from cudaMalloc)");
-  if (rc) return rc;
+  if (g_get_range == nullptr) {
+    local_rc = fail(CLOVE_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  } else if (g_get_range(&base, &range, reinterpret_cast<CUdeviceptr>(local)) != CUDA_SUCCESS) {
+    local_rc = fail(CLOVE_ERR_INVALID_ARG, "shared buffer is not device memory of this process");
+  } else if (reinterpret_cast<CUdeviceptr>(local) - base + bytes > range) {
+    local_rc = fail(CLOVE_ERR_INVALID_ARG, "shared buffer runs past its allocation");
+  } else {
+    local_rc = check_cuda(cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)),
+                          "cudaIpcGetMemHandle (buffer must come from cudaMalloc)");
+  }
+  if (local_rc == CLOVE_OK) {
+    mine.offset = reinterpret_cast<CUdeviceptr>(local) - base;
+    mine.bytes = bytes;
+  }
   // All-gather the records through NCCL on a private stream.
   cudaStream_t s = nullptr;
-  rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+  int rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
   if (rc) return rc;
   std::vector<IpcRecord> all(P);
   void* dbuf = nullptr;
@@ -216,13 +223,15 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
   if (dbuf) cudaFree(dbuf);
   cudaStreamDestroy(s);
   if (rc) return rc;
+  if (local_rc) return local_rc;
+  for (int q = 0; q < P; ++q)
+    if (all[q].bytes != bytes)
+      return fail(CLOVE_ERR_INVALID_ARG, "rank %d could not share a %zu-byte buffer", q, bytes);
   SharedBuf sb;
   sb.local = local;
   sb.bytes = bytes;
   for (int q = 0; q < P && !rc; ++q) {
-    if (all[q].bytes != bytes) {
-      rc = fail(CLOVE_ERR_INVALID_ARG, "ranks registered buffers of different sizes");
-    } else if (q == ctx->rank) {
+    if (q == ctx->rank) {
       sb.ptr[q] = local;
     } else {
       void* b = nullptr;
@@ -276,15 +285,24 @@ const SharedBuf* find_output(const clove_nsplit_ctx* ctx, const void* C_full) {
 // CLOVE_ERR_UNSUPPORTED, with nothing launched, when the shapes or the kernel the
 // dispatch picks cannot store into the replicated C directly; the caller then
 // falls back to the all-gather.
+//
+// Every rank must take the same route (a rank on the all-gather would wait in NCCL
+// for ranks that never join). The route therefore depends only on (M, N, K, P):
+// equal shards whose width and offsets are multiples of 8 (N % 8P == 0); the tile
+// plan for the shard [M, N/P] is the same on every rank; and operand alignment,
+// which could differ between ranks, is an error here rather than a fallback.
 int gemm_fp16_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const void* A,
                        const void* B_shard, void* C_shard, int M, int N, int K, float alpha,
                        cudaStream_t s) {
   const int P = ctx->nranks;
-  const int col0 = clove_nsplit_col_begin(N, P, ctx->rank);
-  const int Nr = shard_cols(N, P, ctx->rank);
-  if (P > kMaxPeers || N % 8 != 0 || col0 % 8 != 0 || Nr % 8 != 0 || Nr == 0 ||
+  if (P > kMaxPeers || N % (8 * P) != 0 || M <= 0 || K % 8 != 0 ||
       out.bytes < static_cast<size_t>(M) * N * 2)
     return CLOVE_ERR_UNSUPPORTED;
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(A) || !a16(B_shard) || !a16(C_shard))
+    return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned A, B_shard, C_shard");
+  const int col0 = clove_nsplit_col_begin(N, P, ctx->rank);
+  const int Nr = N / P;
   PeerTargets peer = {};
   peer.count = P;
   peer.ldc = N;

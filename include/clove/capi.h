@@ -176,7 +176,9 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
 /* The sharded calls compute C_r = A . B_r on this rank's GPU with the          */
 /* single-GPU kernels (no communication). With replicate_C = 1 they then        */
 /* all-gather every rank's C_r over NCCL into the full row-major C [M,N] on     */
-/* every rank. The communicator is created by clove_nsplit_init.                */
+/* every rank, or, for an fp16 C_full registered with                           */
+/* clove_nsplit_register_output, store it there from the GEMM epilogue.         */
+/* The communicator is created by clove_nsplit_init.                            */
 /* ------------------------------------------------------------------------- */
 typedef struct clove_nsplit_ctx clove_nsplit_ctx;
 
