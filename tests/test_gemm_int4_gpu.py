@@ -159,3 +159,27 @@ def test_stream_read_hook(clove_lib, cuda):
     assert int(sink[0]) == 0  # XOR of an even number of equal words is 0, not the sentinel
     with pytest.raises(ValueError):
         clove_lib.debug_stream_read(buf[:17], sink)
+
+
+def test_tc_int4_extreme_codes_exact(clove_lib, oracle_mod, cuda):
+    """Largest |G|: every code 15 against zero point 0 on one operand and code 0
+    against zero point 15 on the other (each product -225, G = -28800), and the
+    mirrored signs: the tensor-core group accumulators stay exact."""
+    M = N = 128
+    K = 1024
+    for (ca, za, cb, zb) in [(15, 0, 0, 15), (15, 0, 15, 0), (0, 15, 0, 15)]:
+        Aq = np.full((M, K // 2), ca * 17, np.uint8)
+        Bq = np.full((N, K // 2), cb * 17, np.uint8)
+        As = np.full((M, K // 128), 0.01, np.float16)
+        Bs = np.full((N, K // 128), 0.02, np.float16)
+        Az = np.full((M, K // 128), za, np.float16)
+        Bz = np.full((N, K // 128), zb, np.float16)
+        args = [dev(x) for x in (Aq, As, Az, Bq, Bs, Bz)]
+        clove_lib.set_dispatch_override(1, 0, 0)
+        C, G = clove_lib.debug_int4_group_acc(*args)
+        Gref = oracle_mod.int4_group_acc(Aq, Az, Bq, Bz, K)
+        np.testing.assert_array_equal(host(G), Gref)
+        assert abs(int(Gref.flat[0])) == 28800
+        ref = oracle_mod.gemm_int4(Aq, As, Az, Bq, Bs, Bz, K)
+        assert rel_fro(host(C), ref) < TOL_TIGHT
+    assert clove_lib.device_error() == 0
