@@ -433,12 +433,13 @@ def _secondary(cc, torch, peaks):
     return out
 
 
-def _replicated(cc, torch, dist, world, rank):
+def _replicated(cc, torch, dist, world, rank, wl, np):
     """Config 4's FFN up (11008 x 2048 x 4096) split over the ranks' token columns with
-    the output C [11008, 2048] replicated on every rank: the shard GEMM alone, the
-    GEMM whose epilogue stores every tile into all ranks' C (registered output, CUDA
-    IPC over NVLink), and the shard GEMM + NCCL all-gather + re-layout. Per call,
-    device time (CUDA events, max over ranks), median of 3 batches of 20 calls."""
+    the output C [11008, 2048] replicated on every rank, and config 5's INT4 8192^3
+    with the weight rows sharded and C [8192, 8192] replicated: the shard GEMM alone,
+    the GEMM whose epilogue stores every tile into all ranks' C (registered output,
+    CUDA IPC over NVLink), and the shard GEMM + NCCL all-gather + re-layout. Per
+    call, device time (CUDA events, max over ranks), median of 3 batches."""
     M, N, K = UP
     ns = cc.NSplit(rank, world)
     c0, c1 = ns.cols(N)
@@ -492,6 +493,58 @@ def _replicated(cc, torch, dist, world, rank):
         ns.unregister_output(Cf)
     else:
         out["epilogue_to_peers"] = f"unavailable: {err or 'another rank could not register'}"
+    del A, B, Bs, Cs, Cn, Cf
+    # Config 5: INT4 8192^3 with B's rows (weights) sharded, C [8192, 8192] replicated.
+    n = 8192
+    op = wl.int4_operands(n, n, n, seed=0)
+    c0, c1 = ns.cols(n)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    a4 = [t(op.A_q), t(op.A_scale), t(op.A_zero)]
+    b4 = [t(op.B_q[c0:c1]), t(op.B_scale[c0:c1]), t(op.B_zero[c0:c1])]
+    Cs = torch.empty((n, c1 - c0), dtype=torch.float16, device="cuda")
+    Cn = torch.empty((n, n), dtype=torch.float16, device="cuda")
+    Cf = torch.empty((n, n), dtype=torch.float16, device="cuda")
+    err4 = ""
+    try:
+        ns.register_output(Cf)
+    except Exception as e:
+        err4 = repr(e)[:200]
+    ok4 = torch.tensor([0 if err4 else 1], device="cuda")
+    dist.all_reduce(ok4, op=dist.ReduceOp.MIN)
+    fns = {"shard_only": lambda: ns.gemm_int4(*a4, *b4, n, C_shard=Cs),
+           "nccl_all_gather": lambda: ns.gemm_int4(*a4, *b4, n, C_shard=Cs, C_full=Cn,
+                                                   replicate_C=True)}
+    if ok4.item():
+        fns["epilogue_to_peers"] = lambda: ns.gemm_int4(*a4, *b4, n, C_shard=Cs, C_full=Cf,
+                                                        replicate_C=True)
+    times = {k: [] for k in fns}
+    for _ in range(3):
+        for k, fn in fns.items():
+            fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                fn()
+            e1.record()
+            e1.synchronize()
+            tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / 5], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            times[k].append(tt.item())
+    out4 = {"shape": {"M": n, "N": n, "K": n, "columns_per_rank": c1 - c0},
+            "us_per_call": {k: round(statistics.median(v), 2) for k, v in times.items()},
+            "TOPS_shard_only": round(2 * n ** 3 / statistics.median(times["shard_only"]) * 1e-6, 1)}
+    if ok4.item():
+        same = torch.tensor([1 if torch.equal(Cn, Cf) else 0], device="cuda")
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        out4["epilogue_equals_all_gather"] = bool(same.item())
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.unregister_output(Cf)
+    else:
+        out4["epilogue_to_peers"] = f"unavailable: {err4 or 'another rank could not register'}"
+    out["int4_8192_config5"] = out4
     out["device_error"] = cc.device_error()
     ns.close()
     return out
@@ -702,7 +755,7 @@ def run_gpu(args):
     if world == 1 and rank == 0 and not args.no_secondary:
         line["secondary"] = _secondary(cc, torch, peaks)
     if world > 1 and not args.no_secondary:
-        rep = _replicated(cc, torch, dist, world, rank)  # collective: every rank
+        rep = _replicated(cc, torch, dist, world, rank, wl, np)  # collective: every rank
         if rank == 0:
             line["replicated_output"] = rep
     if world == 1 and rank == 0 and not args.no_cpu:

@@ -38,7 +38,8 @@ bool gemm_int4_tc_eligible(const uint8_t* Aq, const void* As, const void* Az, co
 
 int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                         const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int M, int N,
-                        int K, const DeviceInfo& dev, cudaStream_t stream) {
+                        int K, const DeviceInfo& dev, cudaStream_t stream,
+                        const PeerTargets* peer_targets) {
   using S = kern::I4Shape;
   const int NG = K / 128;
   CUtensorMap tAq, tBq, tAs, tAz, tBs, tBz, tC;
@@ -62,9 +63,14 @@ int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const
     if (rc) return rc;
     g_attr_set[dbg].fetch_or(bit, std::memory_order_acq_rel);
   }
+  kern::PeerOut peer = {};
+  if (peer_targets != nullptr) {
+    rc = encode_peer_maps(*peer_targets, M, N, 64, 128, &peer);
+    if (rc) return rc;
+  }
   const dim3 grid((N + S::BN - 1) / S::BN, (M + S::BM - 1) / S::BM, 1);
   kernel<<<grid, S::THREADS, S::SMEM_BYTES, stream>>>(tAq, tBq, tAs, tAz, tBs, tBz, tC, M, N, K,
-                                                      Gdbg);
+                                                      Gdbg, peer);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     cudaFuncAttributes fa{};

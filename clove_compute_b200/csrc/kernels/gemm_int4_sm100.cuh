@@ -34,6 +34,7 @@
 // Zero points must be integer codes in [0, 15].
 #pragma once
 
+#include "params.h"
 #include "sm100_ptx.cuh"
 
 namespace clove {
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
                         const __grid_constant__ CUtensorMap tmBs,
                         const __grid_constant__ CUtensorMap tmBz,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
-                        int32_t* __restrict__ Gdbg) {
+                        int32_t* __restrict__ Gdbg, const __grid_constant__ PeerOut peer) {
   using S = I4Shape;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = dev::align_smem_1024(smem_raw);
@@ -399,8 +400,13 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       __syncwarp();
       if (lane == 0) {
         dev::tma_store_2d(&tmC, stg, n0 + h * 64, m0 + static_cast<int>(q) * 32);
+        // Replicated output of an N-split: the same staged slab to every rank's C.
+        for (int d = 0; d < peer.count; ++d)
+          dev::tma_store_2d(&peer.maps[d], stg, peer.col0 + n0 + h * 64,
+                            m0 + static_cast<int>(q) * 32);
         dev::bulk_commit_group();
         dev::bulk_wait_group<0>();
+        if (peer.count > 0) __threadfence_system();  // before the cross-rank signal
       }
       __syncwarp();
     }

@@ -17,9 +17,6 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_tc)
 
-int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int swizzle,
-                     kern::PeerOut* out);
-
 }  // namespace rt
 }  // namespace clove
 

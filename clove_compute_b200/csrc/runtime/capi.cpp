@@ -462,7 +462,7 @@ int clove_debug_int8_acc(const int8_t* A_q, const int8_t* B_q, int32_t* acc, int
 // ---------------------------------------------------------------------------
 static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                           const void* Bs, const void* Bz, void* C, int32_t* G, int M, int N, int K,
-                          cudaStream_t s, const char** chosen) {
+                          cudaStream_t s, const char** chosen, const PeerTargets* peer = nullptr) {
   if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
   if (M == 0 || N == 0) return CLOVE_OK;
   if (K % CLOVE_INT4_GROUP_SIZE != 0)
@@ -486,6 +486,7 @@ static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, con
   if (path == 1 && !tc_ok) path = 0;
   if (path == 2 && !(gemv_n_ok || gemv_m_ok)) path = 0;
   if (path == 0) path = (gemv_n_ok || gemv_m_ok) ? 2 : (tc_ok ? 1 : 3);
+  if (peer != nullptr && (path != 1 || G != nullptr)) return CLOVE_ERR_UNSUPPORTED;
   if (path == 2) {
     if (gemv_n_ok && (N <= M || !gemv_m_ok)) {
       if (chosen) *chosen = "gemv_int4";
@@ -499,10 +500,22 @@ static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, con
   }
   if (path == 1) {
     if (chosen) *chosen = "tc_int4";
-    return launch_gemm_int4_tc(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, dev, s);
+    return launch_gemm_int4_tc(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, dev, s, peer);
   }
   if (chosen) *chosen = "simt_int4";
   return launch_simt_i4(Aq, As, Az, Bq, Bs, Bz, C, G, M, N, K, s);
+}
+
+extern "C++" {  // internal C++ entry (nsplit.cpp), inside this file's extern "C" block
+namespace clove {
+namespace rt {
+int gemm_int4_replicated(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                         const void* Bs, const void* Bz, void* C, int M, int N, int K,
+                         const PeerTargets& peer, cudaStream_t s) {
+  return gemm_int4_impl(Aq, As, Az, Bq, Bs, Bz, C, nullptr, M, N, K, s, nullptr, &peer);
+}
+}  // namespace rt
+}  // namespace clove
 }
 
 int clove_gemm_int4(const uint8_t* A_q, const void* A_scale, const void* A_zero,

@@ -11,6 +11,7 @@
 namespace clove {
 namespace kern {
 struct EpiParams;
+struct PeerOut;
 struct GemvI8Epi;
 struct SimtEpi;
 }  // namespace kern
@@ -133,7 +134,11 @@ int read_clear_error_simt();
 // Gdbg (may be NULL): exact group accumulators G [M,N,K/128] for tests.
 int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                         const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int M, int N,
-                        int K, const DeviceInfo& dev, cudaStream_t stream);
+                        int K, const DeviceInfo& dev, cudaStream_t stream,
+                        const PeerTargets* peer = nullptr);
+// TMA store maps of a replicated output (gemm_tc_sm100.cu).
+int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int swizzle,
+                     kern::PeerOut* out);
 bool gemm_int4_tc_eligible(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                            const void* Bs, const void* Bz, const void* C, int M, int N, int K);
 int read_clear_error_int4();

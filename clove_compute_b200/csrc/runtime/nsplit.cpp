@@ -41,6 +41,9 @@ int launch_peer_signal_wait(int nranks, int rank, unsigned long long* epoch,
                             unsigned long long* const* flags, cudaStream_t stream);
 int gemm_fp16_replicated(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                          const PeerTargets& peer, cudaStream_t s);
+int gemm_int4_replicated(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                         const void* Bs, const void* Bz, void* C, int M, int N, int K,
+                         const PeerTargets& peer, cudaStream_t s);
 }  // namespace rt
 }  // namespace clove
 
@@ -316,6 +319,36 @@ int gemm_fp16_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const void* 
   return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
 }
 
+// INT4 (config 5's sharded weights): the same route through the INT4 tensor-core
+// kernel's epilogue. Rank-independent conditions keep every rank on the tile
+// kernel: equal shards (N % 8P == 0) wider than the decode GEMV's 8 columns, M > 8,
+// K % 1024 == 0 (the kernel's TMA row pitches), 16-byte aligned operands.
+int gemm_int4_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const uint8_t* A_q,
+                       const void* A_scale, const void* A_zero, const uint8_t* B_q,
+                       const void* B_scale, const void* B_zero, void* C_shard, int M, int N,
+                       int K, cudaStream_t s) {
+  const int P = ctx->nranks;
+  if (P > kMaxPeers || N % (8 * P) != 0 || N / P <= 8 || M <= 8 || K % 1024 != 0 ||
+      out.bytes < static_cast<size_t>(M) * N * 2)
+    return CLOVE_ERR_UNSUPPORTED;
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(A_q) || !a16(A_scale) || !a16(A_zero) || !a16(B_q) || !a16(B_scale) ||
+      !a16(B_zero) || !a16(C_shard))
+    return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned operands");
+  PeerTargets peer = {};
+  peer.count = P;
+  peer.ldc = N;
+  peer.col0 = clove_nsplit_col_begin(N, P, ctx->rank);
+  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
+  int rc = gemm_int4_replicated(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C_shard, M, N / P, K,
+                                peer, s);
+  if (rc) return rc;
+  unsigned long long* fl[kMaxPeers] = {};
+  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
+  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
+  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+}
+
 }  // namespace
 
 extern "C" {
@@ -461,6 +494,13 @@ int clove_nsplit_gemm_int4(clove_nsplit_ctx* ctx, const uint8_t* A_q, const void
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int Nr = shard_cols(N, ctx->nranks, ctx->rank);
+  if (replicate_C && C_full != nullptr && K > 0) {
+    if (const SharedBuf* out = find_output(ctx, C_full)) {
+      const int rc = gemm_int4_to_peers(ctx, *out, A_q, A_scale, A_zero, B_q_shard, B_scale_shard,
+                                        B_zero_shard, C_shard, M, N, K, s);
+      if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
+    }
+  }
   int rc = Nr > 0 ? clove_gemm_int4(A_q, A_scale, A_zero, B_q_shard, B_scale_shard, B_zero_shard,
                                     C_shard, M, Nr, K, stream)
                   : CLOVE_OK;

@@ -130,6 +130,24 @@ def _worker_fused(rank, world, port, q):
             del g
             dist.barrier()
             ns.unregister_output(C_full)
+        # INT4 with B rows sharded (config 5's layout), through the INT4 kernel's
+        # epilogue: M, N/P > 8 and K % 1024 == 0 keep every rank on the tile kernel.
+        M, N, K = 256, 512, 2048
+        op = wl.int4_operands(M, N, K, seed=9)
+        c0, c1 = ns.cols(N)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        C_full = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        ns.register_output(C_full)
+        ref = oracle.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K)
+        dist.barrier()
+        ns.gemm_int4(t(op.A_q), t(op.A_scale), t(op.A_zero), t(op.B_q[c0:c1]),
+                     t(op.B_scale[c0:c1]), t(op.B_zero[c0:c1]), N, C_full=C_full,
+                     replicate_C=True)
+        torch.cuda.synchronize()
+        h = C_full.cpu().numpy().astype(np.float64)
+        out.append(float(np.linalg.norm(h - ref) / np.linalg.norm(ref)))
+        dist.barrier()
+        ns.unregister_output(C_full)
         err = cc.device_error()
         ns.close()
         q.put((rank, "ok", out + [float(err)]))
