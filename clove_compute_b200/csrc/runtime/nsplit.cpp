@@ -60,6 +60,16 @@ struct SharedBuf {
 };
 }  // namespace
 
+// One IPC mapping of a peer allocation. Several shared buffers can live in one
+// allocation (tensors of one caching-allocator segment), and a handle can be
+// opened only once per process, so mappings are shared and counted.
+struct IpcMapping {
+  int rank;
+  cudaIpcMemHandle_t handle;
+  void* base;
+  int refs;
+};
+
 struct clove_nsplit_ctx {
   ncclComm_t comm;
   int rank;
@@ -68,6 +78,7 @@ struct clove_nsplit_ctx {
   std::vector<SharedBuf> outputs;  // registered replicated outputs
   SharedBuf flags;                 // [nranks] completion flags + this rank's epoch
   bool flags_ready = false;
+  std::vector<IpcMapping> mappings;
 };
 
 namespace {
@@ -171,6 +182,40 @@ struct IpcRecord {
   unsigned long long bytes;
 };
 
+int open_mapping(clove_nsplit_ctx* ctx, int q, const cudaIpcMemHandle_t& h, void** base) {
+  for (IpcMapping& m : ctx->mappings) {
+    if (m.rank == q && memcmp(&m.handle, &h, sizeof(h)) == 0) {
+      ++m.refs;
+      *base = m.base;
+      return CLOVE_OK;
+    }
+  }
+  void* b = nullptr;
+  const int rc = check_cuda(cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess),
+                            "cudaIpcOpenMemHandle");
+  if (rc) return rc;
+  ctx->mappings.push_back(IpcMapping{q, h, b, 1});
+  *base = b;
+  return CLOVE_OK;
+}
+
+void close_shared(clove_nsplit_ctx* ctx, SharedBuf* sb) {
+  for (int q = 0; q < kMaxPeers; ++q) {
+    if (sb->opened[q] == nullptr) continue;
+    for (size_t i = 0; i < ctx->mappings.size(); ++i) {
+      IpcMapping& m = ctx->mappings[i];
+      if (m.rank == q && m.base == sb->opened[q]) {
+        if (--m.refs == 0) {
+          cudaIpcCloseMemHandle(m.base);
+          ctx->mappings.erase(ctx->mappings.begin() + static_cast<long>(i));
+        }
+        break;
+      }
+    }
+  }
+  *sb = SharedBuf();
+}
+
 // Collective: every rank passes a device pointer of `bytes` bytes (any offset inside
 // a cudaMalloc allocation, such as a PyTorch tensor); on return out->ptr[q] is rank
 // q's pointer mapped into this process. Every rank reaches the all-gather even when
@@ -238,8 +283,7 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
       sb.ptr[q] = local;
     } else {
       void* b = nullptr;
-      rc = check_cuda(cudaIpcOpenMemHandle(&b, all[q].handle, cudaIpcMemLazyEnablePeerAccess),
-                      "cudaIpcOpenMemHandle");
+      rc = open_mapping(ctx, q, all[q].handle, &b);
       if (!rc) {
         sb.opened[q] = b;
         sb.ptr[q] = static_cast<char*>(b) + all[q].offset;
@@ -247,18 +291,11 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
     }
   }
   if (rc) {
-    for (int q = 0; q < P; ++q)
-      if (sb.opened[q]) cudaIpcCloseMemHandle(sb.opened[q]);
+    close_shared(ctx, &sb);
     return rc;
   }
   *out = sb;
   return CLOVE_OK;
-}
-
-void close_shared(SharedBuf* sb) {
-  for (int q = 0; q < kMaxPeers; ++q)
-    if (sb->opened[q]) cudaIpcCloseMemHandle(sb->opened[q]);
-  *sb = SharedBuf();
 }
 
 // Collective barrier on the communicator (one tiny all-gather, host-synchronous).
@@ -389,7 +426,7 @@ int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full) {
   for (size_t i = 0; i < ctx->outputs.size(); ++i) {
     if (ctx->outputs[i].local == C_full) {
       int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(unregister)");
-      close_shared(&ctx->outputs[i]);
+      close_shared(ctx, &ctx->outputs[i]);
       ctx->outputs.erase(ctx->outputs.begin() + static_cast<long>(i));
       // No rank frees its buffer while another still has it mapped.
       const int rc2 = host_barrier(ctx);
@@ -443,11 +480,11 @@ int clove_nsplit_destroy(clove_nsplit_ctx* ctx) {
   int rc = CLOVE_OK;
   if (!ctx->outputs.empty() || ctx->flags_ready) {
     rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(destroy)");
-    for (SharedBuf& b : ctx->outputs) close_shared(&b);
+    for (SharedBuf& b : ctx->outputs) close_shared(ctx, &b);
     ctx->outputs.clear();
     if (ctx->flags_ready) {
       void* f = ctx->flags.local;
-      close_shared(&ctx->flags);
+      close_shared(ctx, &ctx->flags);
       const int rc2 = host_barrier(ctx);  // peers unmapped our flags before we free them
       cudaFree(f);
       if (!rc) rc = rc2;

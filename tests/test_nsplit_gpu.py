@@ -130,6 +130,28 @@ def _worker_fused(rank, world, port, q):
             del g
             dist.barrier()
             ns.unregister_output(C_full)
+        # Two registered outputs inside one allocation (one IPC mapping per peer,
+        # shared by both registrations), used alternately.
+        M, N, K = 512, 1024, 512
+        A, B = wl.fp16_operands(M, N, K, seed=77)
+        c0, c1 = ns.cols(N)
+        Ad = torch.from_numpy(A).cuda()
+        Bs = torch.from_numpy(np.ascontiguousarray(B[:, c0:c1])).cuda()
+        buf = torch.full((2 * M * N,), float("nan"), dtype=torch.float16, device="cuda")
+        C1, C2 = buf[:M * N].view(M, N), buf[M * N:].view(M, N)
+        ns.register_output(C1)
+        ns.register_output(C2)
+        ref = oracle.gemm_fp16(A, B)
+        dist.barrier()
+        ns.gemm_fp16(Ad, Bs, N, C_full=C2, replicate_C=True)
+        ns.gemm_fp16(Ad, Bs, N, C_full=C1, replicate_C=True)
+        torch.cuda.synchronize()
+        for Cx in (C1, C2):
+            h = Cx.cpu().numpy().astype(np.float64)
+            out.append(float(np.linalg.norm(h - ref) / np.linalg.norm(ref)))
+        dist.barrier()
+        ns.unregister_output(C1)
+        ns.unregister_output(C2)
         # INT4 with B rows sharded (config 5's layout), through the INT4 kernel's
         # epilogue: M, N/P > 8 and K % 1024 == 0 keep every rank on the tile kernel.
         M, N, K = 256, 512, 2048
