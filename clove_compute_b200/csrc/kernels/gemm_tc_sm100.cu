@@ -308,7 +308,7 @@ SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force) {
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
                     const void* B2, const PeerTargets* peer) {
-  if (peer != nullptr && (B2 != nullptr || op != kTcF16)) return CLOVE_ERR_UNSUPPORTED;
+  if (peer != nullptr && B2 != nullptr) return CLOVE_ERR_UNSUPPORTED;
   using SF = kern::Tc2Shape<kern::OpF16>;
   using SI = kern::Tc2Shape<kern::OpI8>;
   const bool f16 = op == kTcF16;

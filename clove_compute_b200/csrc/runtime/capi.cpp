@@ -366,7 +366,8 @@ int clove_swiglu_fused(const void* input, const void* W_gate, const void* W_up, 
 // mode: 1 per-tensor, 2 row/col, 3 raw int32 accumulators.
 static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int N, int K, int mode,
                           float scale, int za, int zb, const float* rs, const float* cs,
-                          cudaStream_t s, const char** chosen) {
+                          cudaStream_t s, const char** chosen,
+                          const PeerTargets* peer = nullptr) {
   if (M < 0 || N < 0 || K < 0) return fail(CLOVE_ERR_INVALID_ARG, "negative size");
   if (M == 0 || N == 0) return CLOVE_OK;
   if (A == nullptr || B == nullptr || C == nullptr)
@@ -388,6 +389,7 @@ static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int 
   if ((path == 1 || path == 4) && !tc_ok) path = 0;
   if (path == 2 && !gemv_ok) path = 0;
   if (path == 0) path = gemv_ok ? 2 : (tc_ok ? 1 : 3);
+  if (peer != nullptr && (path == 2 || path == 3 || out_bytes != 2)) return CLOVE_ERR_UNSUPPORTED;
   if (path == 2) {
     if (chosen) *chosen = "gemv_int8";
     kern::GemvI8Epi ep{mode, scale, rs, cs, za, zb};
@@ -428,9 +430,10 @@ static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int 
   }
   if (!rc) {
     if (plan.pair && out_bytes == 2)
-      rc = launch_gemm_tc2(kTcI8, A, B, C, M, N, K, ep, dev, s);
+      rc = launch_gemm_tc2(kTcI8, A, B, C, M, N, K, ep, dev, s, nullptr, peer);
     else
-      rc = launch_gemm_tc(kTcI8, plan.bn, plan.split, out_bytes, A, B, C, M, N, K, ep, dev, s);
+      rc = launch_gemm_tc(kTcI8, plan.bn, plan.split, out_bytes, A, B, C, M, N, K, ep, dev, s, 1,
+                          peer);
   }
   if (sums != nullptr) {
     const int rc2 = check_cuda(cudaFreeAsync(sums, s), "cudaFreeAsync(zero-point sums)");
@@ -509,6 +512,11 @@ static int gemm_int4_impl(const uint8_t* Aq, const void* As, const void* Az, con
 extern "C++" {  // internal C++ entry (nsplit.cpp), inside this file's extern "C" block
 namespace clove {
 namespace rt {
+int gemm_int8_rowcol_replicated(const int8_t* A, const int8_t* B, void* C, int M, int N, int K,
+                                const float* rs, const float* cs, const PeerTargets& peer,
+                                cudaStream_t s) {
+  return gemm_int8_impl(A, B, C, M, N, K, 2, 0.f, 0, 0, rs, cs, s, nullptr, &peer);
+}
 int gemm_int4_replicated(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                          const void* Bs, const void* Bz, void* C, int M, int N, int K,
                          const PeerTargets& peer, cudaStream_t s) {

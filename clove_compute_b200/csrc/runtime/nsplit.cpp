@@ -44,6 +44,9 @@ int gemm_fp16_replicated(const void* A, const void* B, void* C, int M, int N, in
 int gemm_int4_replicated(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                          const void* Bs, const void* Bz, void* C, int M, int N, int K,
                          const PeerTargets& peer, cudaStream_t s);
+int gemm_int8_rowcol_replicated(const int8_t* A, const int8_t* B, void* C, int M, int N, int K,
+                                const float* rs, const float* cs, const PeerTargets& peer,
+                                cudaStream_t s);
 }  // namespace rt
 }  // namespace clove
 
@@ -386,6 +389,32 @@ int gemm_int4_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const uint8_
   return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
 }
 
+// INT8 with per-row / per-column scales: the tile kernels' epilogue again. The
+// tile kernels need N_r % 16 == 0 (N % 16P == 0), N_r > 8 keeps the GEMV away;
+// a split-K plan (the same on every rank) declines and all ranks gather instead.
+int gemm_int8_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const int8_t* A_q,
+                       const int8_t* B_q, const float* rs, const float* cs, void* C_shard, int M,
+                       int N, int K, cudaStream_t s) {
+  const int P = ctx->nranks;
+  if (P > kMaxPeers || N % (16 * P) != 0 || N / P <= 8 || K % 16 != 0 || M <= 0 ||
+      out.bytes < static_cast<size_t>(M) * N * 2)
+    return CLOVE_ERR_UNSUPPORTED;
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(A_q) || !a16(B_q) || !a16(C_shard))
+    return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned operands");
+  PeerTargets peer = {};
+  peer.count = P;
+  peer.ldc = N;
+  peer.col0 = clove_nsplit_col_begin(N, P, ctx->rank);
+  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
+  int rc = gemm_int8_rowcol_replicated(A_q, B_q, C_shard, M, N / P, K, rs, cs, peer, s);
+  if (rc) return rc;
+  unsigned long long* fl[kMaxPeers] = {};
+  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
+  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
+  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+}
+
 }  // namespace
 
 extern "C" {
@@ -553,7 +582,14 @@ int clove_nsplit_gemm_int8_rowcol(clove_nsplit_ctx* ctx, const int8_t* A_q, cons
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int Nr = shard_cols(N, ctx->nranks, ctx->rank);
-  int rc = Nr > 0 ? clove_gemm_int8_rowcol(A_q, B_q_shard, C_shard, M, Nr, K, A_row_scale,
+    if (replicate_C && C_full != nullptr && K > 0) {
+    if (const SharedBuf* out = find_output(ctx, C_full)) {
+      const int rc = gemm_int8_to_peers(ctx, *out, A_q, B_q_shard, A_row_scale,
+                                        B_col_scale_shard, C_shard, M, N, K, s);
+      if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
+    }
+  }
+  int rc = Nr > 0 ? clove_gemm_int8_rowcol(q, B_q_shard, C_shard, M, Nr, K, A_row_scale,
                                            B_col_scale_shard, stream)
                   : CLOVE_OK;
   if (rc || !replicate_C) return rc;

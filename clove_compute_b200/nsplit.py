@@ -5,7 +5,7 @@ Rank r owns columns ``[col_begin(N, P, r), col_begin(N, P, r+1))`` of B and C
 single-GPU kernel on its shard; with ``replicate_C`` the shards are all-gathered
 over NCCL (NVLink) into the full row-major C on every rank. A C registered with
 ``register_output`` (a collective that maps it into every rank through CUDA IPC)
-is instead filled by the fp16 or INT4 GEMM's own epilogue, which stores each
+is instead filled by the GEMM's own epilogue (fp16, INT8 row/col, INT4), which stores each
 finished tile into every rank's copy over NVLink. The NCCL communicator belongs to the C
 library; its unique id is exchanged through the torch.distributed store of the
 already-initialised process group.

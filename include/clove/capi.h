@@ -194,13 +194,14 @@ int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
 /* Collective (every rank, same order, same byte count): maps this rank's
  * replicated-output buffer C_full (device memory from cudaMalloc, at any offset,
  * e.g. a PyTorch tensor; 16-byte aligned) into every other rank through CUDA IPC.
- * Afterwards clove_nsplit_gemm_fp16 / clove_nsplit_gemm_int4 with replicate_C = 1
- * and this C_full store each finished tile straight into every rank's C_full over
+ * Afterwards clove_nsplit_gemm_fp16 / _int8_rowcol / _int4 with replicate_C = 1 and
+ * this C_full store each finished tile straight into every rank's C_full over
  * NVLink (no all-gather, no staging) and end with a cross-rank completion signal.
- * The route depends only on (M, N, K, nranks): N % (8 nranks) == 0 (equal shards)
- * and a shard the tile kernels take (INT4: N/nranks > 8, M > 8, K % 1024 == 0);
- * other shapes, and INT8, still take the NCCL all-gather. Operands must then be
- * 16-byte aligned. At most 8 ranks. (Extension; no counterpart in the reference.) */
+ * The route depends only on (M, N, K, nranks): equal shards (N % 8P == 0; INT8
+ * N % 16P == 0) that the tile kernels take (N/P > 8; INT4 also M > 8 and
+ * K % 1024 == 0; INT8 no cluster split-K); other shapes still take the NCCL
+ * all-gather. Operands must then be 16-byte aligned. At most 8 ranks.
+ * (Extension; no counterpart in the reference.) */
 int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes);
 /* Collective: unmaps C_full everywhere; returns once no rank maps it any more. */
 int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full);

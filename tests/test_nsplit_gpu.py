@@ -152,6 +152,22 @@ def _worker_fused(rank, world, port, q):
         dist.barrier()
         ns.unregister_output(C1)
         ns.unregister_output(C2)
+        # INT8 with per-row / per-column scales through the tile kernels' epilogue.
+        M, N, K = 512, 1024, 1024
+        A8, B8, sA, sB = wl.int8_operands(M, N, K, seed=12)
+        c0, c1 = ns.cols(N)
+        t8 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        C_full = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        ns.register_output(C_full)
+        dist.barrier()
+        ns.gemm_int8_rowcol(t8(A8), t8(B8[:, c0:c1]), t8(sA), t8(sB[c0:c1]), N, C_full=C_full,
+                            replicate_C=True)
+        torch.cuda.synchronize()
+        ref = oracle.gemm_int8_rowcol(A8, B8, sA, sB).astype(np.float64)
+        h = C_full.cpu().numpy().astype(np.float64)
+        out.append(float(np.linalg.norm(h - ref) / np.linalg.norm(ref)))
+        dist.barrier()
+        ns.unregister_output(C_full)
         # INT4 with B rows sharded (config 5's layout), through the INT4 kernel's
         # epilogue: M, N/P > 8 and K % 1024 == 0 keep every rank on the tile kernel.
         M, N, K = 256, 512, 2048
