@@ -582,14 +582,14 @@ int clove_nsplit_gemm_int8_rowcol(clove_nsplit_ctx* ctx, const int8_t* A_q, cons
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int Nr = shard_cols(N, ctx->nranks, ctx->rank);
-    if (replicate_C && C_full != nullptr && K > 0) {
+  if (replicate_C && C_full != nullptr && K > 0) {
     if (const SharedBuf* out = find_output(ctx, C_full)) {
       const int rc = gemm_int8_to_peers(ctx, *out, A_q, B_q_shard, A_row_scale,
                                         B_col_scale_shard, C_shard, M, N, K, s);
       if (rc != CLOVE_ERR_UNSUPPORTED) return rc;
     }
   }
-  int rc = Nr > 0 ? clove_gemm_int8_rowcol(q, B_q_shard, C_shard, M, Nr, K, A_row_scale,
+  int rc = Nr > 0 ? clove_gemm_int8_rowcol(A_q, B_q_shard, C_shard, M, Nr, K, A_row_scale,
                                            B_col_scale_shard, stream)
                   : CLOVE_OK;
   if (rc || !replicate_C) return rc;
