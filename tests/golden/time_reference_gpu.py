@@ -113,4 +113,4 @@ def main(out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "ref_gpu.json"))
+    main(sys.argv[1] if len(sys.argv) > 1 else "ref_gpu.json")
