@@ -149,3 +149,22 @@ def test_stream_k_plans_for_the_ffn_shapes(clove_lib):
     assert clove_lib.debug_stream_k_plan(1024, 74, 128)["sk_tiles"] == 0
     assert clove_lib.debug_stream_k_plan(100, 74, 64, 1)["sk_tiles"] == 0
     assert clove_lib.debug_stream_k_plan(5, 74, 64)["pairs"] == 5
+
+
+def test_cxx_runtime_call_sites_compile_and_link(clove_lib, tmp_path):
+    """The reference runtime's linear-layer calls (inference.cu:139-194) compile
+    against include/clove/kernels/gemm.cuh and link against the library, as a C++
+    integration would (nvcc cross-compiles; the binary is not run here)."""
+    import shutil
+    import subprocess
+    nvcc = "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else shutil.which("nvcc")
+    if nvcc is None:
+        pytest.skip("nvcc not available")
+    lib_dir = os.path.dirname(clove_lib.library_path())
+    exe = str(tmp_path / "runtime_linear_layers")
+    cmd = [nvcc, "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-I" + os.path.join(ROOT, "include"), os.path.join(ROOT, "tests", "cxx", "runtime_linear_layers.cu"),
+           "-o", exe, "-L" + lib_dir, "-lclove_b200", "-Xlinker", "-rpath=" + lib_dir]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert os.path.exists(exe)
