@@ -388,6 +388,28 @@ def _secondary(cc, torch, peaks):
         del graphs, W, X, Cf
     out["ffn_vs_cublas_us"] = dict(ffn_cmp, note="per call, same box and operands, interleaved")
 
+    # The four fp16 shapes the reference's README publishes timings for (its own
+    # kernel, hardware unstated): decode 1x4096x4096, batch32 32x4096x4096,
+    # prefill128 128x4096x4096 and 4096^3, as M x N x K of C[M,N] = A[M,K].B[K,N].
+    readme = {}
+    for name, (M, N, K) in (("decode_1x4096x4096", (1, 4096, 4096)),
+                            ("batch32_32x4096x4096", (32, 4096, 4096)),
+                            ("prefill128_128x4096x4096", (128, 4096, 4096)),
+                            ("square_4096", (4096, 4096, 4096))):
+        gen.manual_seed(M + 7)
+        copies = max(2, min(24, int(300e6 // (2 * (M * K + K * N))) + 1))
+        Ad = [(torch.randn((M, K), device="cuda", generator=gen) / K ** 0.5).half()
+              for _ in range(copies)]
+        Bd = [(torch.randn((K, N), device="cuda", generator=gen)).half() for _ in range(copies)]
+        Cr = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        t = timeit(lambda i: cc.gemm_fp16(Ad[i], Bd[i], Cr), copies, 200)
+        readme[name] = {"kernel": cc.describe_dispatch("fp16", M, N, K),
+                        "ms": round(t * 1e3, 5), "TFLOPS": round(2 * M * N * K / t / 1e12, 2)}
+        del Ad, Bd
+    out["reference_readme_shapes"] = dict(
+        readme, note="the reference README's published ms (hardware unstated): 0.042, 0.891, "
+                     "2.847, 5.234")
+
     # config 1 and the square sweep (fp16, 1024-16384), int8 square sweep
     for n in (1024, 2048, 4096, 8192, 16384):
         # Timing-only operands: the config distribution N(0,1)/sqrt(K), drawn on the
