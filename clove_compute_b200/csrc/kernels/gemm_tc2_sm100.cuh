@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(192, 1)
     const int row_in_tile = static_cast<int>(q * 32 + lane);
     uint8_t* stg_base = epi_base + (warp - 2) * (2 * 4096);
     uint32_t stg_count = 0;
-    uint32_t sk_phase = 0;
+    uint32_t ph0 = 0, ph1 = 0;  // completed phases of skbar[0] / skbar[1]
     int it = 0;
     Tc2Sched sched(pair, pairs, sk, kb_total);
     Tc2Work w;
@@ -291,8 +291,90 @@ __global__ void __launch_bounds__(192, 1)
           // slot, laid out [column quad][row] so that a warp's 16-byte stores
           // cover 512 contiguous bytes, then take a ticket; the last of the
           // tile's contributors sums every slot in contributor order and runs
-          // the epilogue.
+          // the epilogue. The tile's first K piece (j = 0) usually finishes last
+          // (it closes this pair's stream-K range; the other pieces open theirs):
+          // if every other contributor has already parked its partial, it sums
+          // them onto its own accumulator straight from TMEM and parks nothing,
+          // in the same order, so both routes give the same bits.
           constexpr size_t kSlot = static_cast<size_t>(S::BN) * S::BM;  // words per CTA and piece
+          const int tix = w.sk_idx * 2 + static_cast<int>(rank);
+          const uint32_t* slot0 =
+              sk.partials + (static_cast<size_t>(w.sk_idx) * sk.max_contrib * 2 + rank) * kSlot;
+          bool ok = true;
+          bool fast = false;
+          if (w.j == 0) {
+            if (warp == 2 && lane == 0) {
+              int t;
+              asm volatile("ld.acquire.gpu.global.b32 %0, [%1];"
+                           : "=r"(t)
+                           : "l"(sk.tickets + tix)
+                           : "memory");
+              *sk_last = t == w.nc - 1 ? 2 : 0;
+              dev::mbar_arrive(&skbar[1]);
+            }
+            ok = __all_sync(0xffffffffu, dev::mbar_wait(&skbar[1], ph1 & 1u, abort_flag));
+            ++ph1;
+            if (!ok) break;
+            fast = *sk_last == 2;
+          }
+          // Sums slots [j_from, nc) onto v (v already holds the earlier terms
+          // when j_from > 0).
+          auto add_slots = [&](uint32_t (&v)[S::CHUNK], int c0, int j_from) {
+#pragma unroll 1
+            for (int jj = j_from; jj < w.nc; ++jj) {
+              const uint32_t* src =
+                  slot0 + static_cast<size_t>(jj) * 2 * kSlot + ((c0 / 4) * S::BM + row_in_tile) * 4;
+              uint4 x[S::CHUNK / 4];
+#pragma unroll
+              for (int qd = 0; qd < S::CHUNK / 4; ++qd)
+                x[qd] = __ldcg(reinterpret_cast<const uint4*>(src + qd * S::BM * 4));
+#pragma unroll
+              for (int qd = 0; qd < S::CHUNK / 4; ++qd) {
+                const uint32_t e[4] = {x[qd].x, x[qd].y, x[qd].z, x[qd].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  uint32_t& d = v[4 * qd + i];
+                  if (jj == 0)
+                    d = e[i];
+                  else if constexpr (Op::kInt)
+                    d += e[i];
+                  else
+                    d = __float_as_uint(__uint_as_float(d) + __uint_as_float(e[i]));
+                }
+              }
+            }
+          };
+          if (fast) {
+            __threadfence();
+#pragma unroll 1
+            for (int c0 = 0; c0 < S::BN; c0 += S::CHUNK) {
+              uint32_t v[S::CHUNK];
+#pragma unroll
+              for (int j = 0; j < S::CHUNK; j += 16) {
+                uint32_t t[16];
+                dev::tmem_ld_x16(t_row + c0 + j, t);
+                dev::tmem_ld_wait();
+#pragma unroll
+                for (int u = 0; u < 16; ++u) v[j + u] = t[u];
+              }
+              if (c0 + S::CHUNK >= S::BN) {
+                dev::tc_fence_before_sync();
+                __syncwarp();
+                if (lane == 0) {
+                  if (leader)
+                    dev::mbar_arrive(&tempty[buf]);
+                  else
+                    dev::mbar_arrive_remote(&tempty[buf], 0);
+                }
+              }
+              add_slots(v, c0, 1);
+              store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
+                                           stg_base, stg_count, &tmC,
+                                           m0 + static_cast<int>(q) * 32);
+            }
+            if (*abort_flag) break;
+            continue;
+          }
           uint32_t* part = sk.partials +
                            ((static_cast<size_t>(w.sk_idx) * sk.max_contrib + w.j) * 2 + rank) * kSlot;
 #pragma unroll 1
@@ -319,48 +401,25 @@ __global__ void __launch_bounds__(192, 1)
               dev::mbar_arrive_remote(&tempty[buf], 0);
             dev::mbar_arrive(&skbar[0]);
           }
-          bool ok = dev::mbar_wait(&skbar[0], sk_phase & 1u, abort_flag);
+          ok = dev::mbar_wait(&skbar[0], ph0 & 1u, abort_flag);
+          ++ph0;
           if (warp == 2 && lane == 0 && ok) {
             __threadfence();
-            const int old = atomicAdd(&sk.tickets[w.sk_idx * 2 + static_cast<int>(rank)], 1);
+            const int old = atomicAdd(&sk.tickets[tix], 1);
             *sk_last = old == w.nc - 1 ? 1 : 0;
             dev::mbar_arrive(&skbar[1]);
           }
           ok = __all_sync(0xffffffffu, ok);
-          ok = ok && dev::mbar_wait(&skbar[1], sk_phase & 1u, abort_flag);
+          ok = ok && dev::mbar_wait(&skbar[1], ph1 & 1u, abort_flag);
           ok = __all_sync(0xffffffffu, ok);
-          ++sk_phase;
+          ++ph1;
           if (!ok) break;
-          if (*sk_last) {
+          if (*sk_last == 1) {
             __threadfence();
-            const uint32_t* slot0 =
-                sk.partials + (static_cast<size_t>(w.sk_idx) * sk.max_contrib * 2 + rank) * kSlot;
 #pragma unroll 1
             for (int c0 = 0; c0 < S::BN; c0 += S::CHUNK) {
               uint32_t v[S::CHUNK];
-#pragma unroll 1
-              for (int jj = 0; jj < w.nc; ++jj) {
-                const uint32_t* src =
-                    slot0 + static_cast<size_t>(jj) * 2 * kSlot + ((c0 / 4) * S::BM + row_in_tile) * 4;
-                uint4 x[S::CHUNK / 4];
-#pragma unroll
-                for (int qd = 0; qd < S::CHUNK / 4; ++qd)
-                  x[qd] = __ldcg(reinterpret_cast<const uint4*>(src + qd * S::BM * 4));
-#pragma unroll
-                for (int qd = 0; qd < S::CHUNK / 4; ++qd) {
-                  const uint32_t e[4] = {x[qd].x, x[qd].y, x[qd].z, x[qd].w};
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    uint32_t& d = v[4 * qd + i];
-                    if (jj == 0)
-                      d = e[i];
-                    else if constexpr (Op::kInt)
-                      d += e[i];
-                    else
-                      d = __float_as_uint(__uint_as_float(d) + __uint_as_float(e[i]));
-                  }
-                }
-              }
+              add_slots(v, c0, 0);
               store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
                                            stg_base, stg_count, &tmC,
                                            m0 + static_cast<int>(q) * 32);
