@@ -80,7 +80,9 @@ struct clove_nsplit_ctx {
   int device;
   std::vector<SharedBuf> outputs;  // registered replicated outputs
   SharedBuf flags;                 // [nranks] completion flags + this rank's epoch
-  bool flags_ready = false;
+  void* flags_mem = nullptr;       // this rank's flag array (cudaMalloc)
+  bool flags_ready = false;        // every rank's flag array is mapped here
+  bool ipc_used = false;           // a registration was attempted (same on every rank)
   std::vector<IpcMapping> mappings;
 };
 
@@ -219,12 +221,9 @@ void close_shared(clove_nsplit_ctx* ctx, SharedBuf* sb) {
   *sb = SharedBuf();
 }
 
-// Collective: every rank passes a device pointer of `bytes` bytes (any offset inside
-// a cudaMalloc allocation, such as a PyTorch tensor); on return out->ptr[q] is rank
-// q's pointer mapped into this process. Every rank reaches the all-gather even when
-// its own part failed (it then sends an empty record), so that a local error never
-// leaves the other ranks waiting inside NCCL; all ranks then fail together.
-int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* out) {
+// The IPC record of a device pointer (any offset inside a cudaMalloc allocation,
+// such as a PyTorch tensor). Local only.
+int make_record(void* local, size_t bytes, IpcRecord* rec) {
   std::call_once(g_range_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
@@ -232,65 +231,76 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
             cudaSuccess && q == cudaDriverEntryPointSuccess)
       g_get_range = reinterpret_cast<PfnMemGetAddressRange>(fn);
   });
-  const int P = ctx->nranks;
-  IpcRecord mine = {};
-  int local_rc = CLOVE_OK;
+  *rec = IpcRecord();
   CUdeviceptr base = 0;
   size_t range = 0;
-  if (g_get_range == nullptr) {
-    local_rc = fail(CLOVE_ERR_CUDA, "cuMemGetAddressRange unavailable");
-  } else if (g_get_range(&base, &range, reinterpret_cast<CUdeviceptr>(local)) != CUDA_SUCCESS) {
-    local_rc = fail(CLOVE_ERR_INVALID_ARG, "shared buffer is not device memory of this process");
-  } else if (reinterpret_cast<CUdeviceptr>(local) - base + bytes > range) {
-    local_rc = fail(CLOVE_ERR_INVALID_ARG, "shared buffer runs past its allocation");
-  } else {
-    local_rc = check_cuda(cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)),
-                          "cudaIpcGetMemHandle (buffer must come from cudaMalloc)");
-  }
-  if (local_rc == CLOVE_OK) {
-    mine.offset = reinterpret_cast<CUdeviceptr>(local) - base;
-    mine.bytes = bytes;
-  }
-  // All-gather the records through NCCL on a private stream.
+  if (g_get_range == nullptr) return fail(CLOVE_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  if (g_get_range(&base, &range, reinterpret_cast<CUdeviceptr>(local)) != CUDA_SUCCESS)
+    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer is not device memory of this process");
+  if (reinterpret_cast<CUdeviceptr>(local) - base + bytes > range)
+    return fail(CLOVE_ERR_INVALID_ARG, "shared buffer runs past its allocation");
+  const int rc = check_cuda(cudaIpcGetMemHandle(&rec->handle, reinterpret_cast<void*>(base)),
+                            "cudaIpcGetMemHandle (buffer must come from cudaMalloc)");
+  if (rc) return rc;
+  rec->offset = reinterpret_cast<CUdeviceptr>(local) - base;
+  rec->bytes = bytes;
+  return CLOVE_OK;
+}
+
+// Collective: all-gathers `n` bytes from every rank into all[P * n] (host memory)
+// through NCCL on a private stream.
+int all_gather_host(clove_nsplit_ctx* ctx, const void* mine, size_t n, void* all) {
+  const int P = ctx->nranks;
   cudaStream_t s = nullptr;
   int rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
   if (rc) return rc;
-  std::vector<IpcRecord> all(P);
   void* dbuf = nullptr;
-  rc = check_cuda(cudaMalloc(&dbuf, sizeof(IpcRecord) * (P + 1)), "cudaMalloc(ipc records)");
+  rc = check_cuda(cudaMalloc(&dbuf, n * (P + 1)), "cudaMalloc(all-gather)");
   if (!rc)
-    rc = check_cuda(cudaMemcpyAsync(static_cast<char*>(dbuf) + sizeof(IpcRecord) * P, &mine,
-                                    sizeof(mine), cudaMemcpyHostToDevice, s),
-                    "cudaMemcpyAsync(ipc record)");
+    rc = check_cuda(cudaMemcpyAsync(static_cast<char*>(dbuf) + n * P, mine, n,
+                                    cudaMemcpyHostToDevice, s),
+                    "cudaMemcpyAsync(all-gather in)");
   if (!rc)
-    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(dbuf) + sizeof(IpcRecord) * P, dbuf,
-                                     sizeof(IpcRecord), ncclChar, ctx->comm, s),
-                    "ncclAllGather(ipc records)");
+    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(dbuf) + n * P, dbuf, n, ncclChar,
+                                     ctx->comm, s),
+                    "ncclAllGather(host records)");
   if (!rc)
-    rc = check_cuda(cudaMemcpyAsync(all.data(), dbuf, sizeof(IpcRecord) * P,
-                                    cudaMemcpyDeviceToHost, s),
-                    "cudaMemcpyAsync(ipc records)");
-  if (!rc) rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(ipc records)");
+    rc = check_cuda(cudaMemcpyAsync(all, dbuf, n * P, cudaMemcpyDeviceToHost, s),
+                    "cudaMemcpyAsync(all-gather out)");
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(all-gather)");
   if (dbuf) cudaFree(dbuf);
   cudaStreamDestroy(s);
-  if (rc) return rc;
-  if (local_rc) return local_rc;
-  for (int q = 0; q < P; ++q)
-    if (all[q].bytes != bytes)
-      return fail(CLOVE_ERR_INVALID_ARG, "rank %d could not share a %zu-byte buffer", q, bytes);
+  return rc;
+}
+
+// Collective: true on every rank iff every rank passed ok. A failed exchange
+// counts as not ok.
+bool all_ok(clove_nsplit_ctx* ctx, bool ok) {
+  int mine = ok ? 1 : 0;
+  std::vector<int> all(ctx->nranks, 0);
+  if (all_gather_host(ctx, &mine, sizeof(int), all.data()) != CLOVE_OK) return false;
+  for (int v : all)
+    if (v != 1) return false;
+  return true;
+}
+
+// Maps every other rank's buffer of the all-gathered records into this process.
+int open_shared(clove_nsplit_ctx* ctx, void* local, size_t bytes, const IpcRecord* all,
+                SharedBuf* out) {
   SharedBuf sb;
   sb.local = local;
   sb.bytes = bytes;
-  for (int q = 0; q < P && !rc; ++q) {
+  int rc = CLOVE_OK;
+  for (int q = 0; q < ctx->nranks && !rc; ++q) {
     if (q == ctx->rank) {
       sb.ptr[q] = local;
-    } else {
-      void* b = nullptr;
-      rc = open_mapping(ctx, q, all[q].handle, &b);
-      if (!rc) {
-        sb.opened[q] = b;
-        sb.ptr[q] = static_cast<char*>(b) + all[q].offset;
-      }
+      continue;
+    }
+    void* b = nullptr;
+    rc = open_mapping(ctx, q, all[q].handle, &b);
+    if (!rc) {
+      sb.opened[q] = b;
+      sb.ptr[q] = static_cast<char*>(b) + all[q].offset;
     }
   }
   if (rc) {
@@ -303,19 +313,9 @@ int share_buffer(clove_nsplit_ctx* ctx, void* local, size_t bytes, SharedBuf* ou
 
 // Collective barrier on the communicator (one tiny all-gather, host-synchronous).
 int host_barrier(clove_nsplit_ctx* ctx) {
-  cudaStream_t s = nullptr;
-  int rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
-  if (rc) return rc;
-  void* d = nullptr;
-  rc = check_cuda(cudaMalloc(&d, 4 * (ctx->nranks + 1)), "cudaMalloc(barrier)");
-  if (!rc)
-    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(d) + 4 * ctx->nranks, d, 4, ncclChar,
-                                     ctx->comm, s),
-                    "ncclAllGather(barrier)");
-  if (!rc) rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(barrier)");
-  if (d) cudaFree(d);
-  cudaStreamDestroy(s);
-  return rc;
+  int mine = 0;
+  std::vector<int> all(ctx->nranks);
+  return all_gather_host(ctx, &mine, sizeof(int), all.data());
 }
 
 const SharedBuf* find_output(const clove_nsplit_ctx* ctx, const void* C_full) {
@@ -419,50 +419,85 @@ int gemm_int8_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const int8_t
 
 extern "C" {
 
+// Registration and its undoing are collective, and each takes the same collective
+// steps on every rank whatever happens locally: local failures travel in the
+// exchanged status instead of returning early (a rank that skipped a collective
+// would leave the others waiting in NCCL), and a registration counts only if
+// every rank mapped everything, so all ranks agree on which outputs take the
+// epilogue route.
 int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes) {
-  if (ctx == nullptr || C_full == nullptr || bytes == 0)
-    return fail(CLOVE_ERR_INVALID_ARG, "bad register_output arguments");
-  if (ctx->nranks > kMaxPeers)
-    return fail(CLOVE_ERR_UNSUPPORTED, "replicated output supports up to %d ranks", kMaxPeers);
-  if ((reinterpret_cast<uintptr_t>(C_full) & 15u) != 0)
-    return fail(CLOVE_ERR_INVALID_ARG, "replicated C must be 16-byte aligned");
-  if (find_output(ctx, C_full) != nullptr)
-    return fail(CLOVE_ERR_INVALID_ARG, "buffer already registered");
-  int rc = CLOVE_OK;
-  if (!ctx->flags_ready) {
+  if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
+  ctx->ipc_used = true;
+  const size_t fb = sizeof(unsigned long long) * (kMaxPeers + 1);
+  int lrc = CLOVE_OK;
+  if (C_full == nullptr || bytes == 0)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "bad register_output arguments");
+  else if (ctx->nranks > kMaxPeers)
+    lrc = fail(CLOVE_ERR_UNSUPPORTED, "replicated output supports up to %d ranks", kMaxPeers);
+  else if ((reinterpret_cast<uintptr_t>(C_full) & 15u) != 0)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "replicated C must be 16-byte aligned");
+  else if (find_output(ctx, C_full) != nullptr)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "buffer already registered");
+  if (!lrc && ctx->flags_mem == nullptr) {
     // Flag slots [kMaxPeers] then this rank's epoch, zeroed before anyone signals.
     void* f = nullptr;
-    const size_t fb = sizeof(unsigned long long) * (kMaxPeers + 1);
-    rc = check_cuda(cudaMalloc(&f, fb), "cudaMalloc(flags)");
-    if (!rc) rc = check_cuda(cudaMemset(f, 0, fb), "cudaMemset(flags)");
-    if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(flags)");
-    if (!rc) rc = share_buffer(ctx, f, fb, &ctx->flags);
-    if (rc) {
-      if (f) cudaFree(f);
-      return rc;
-    }
+    lrc = check_cuda(cudaMalloc(&f, fb), "cudaMalloc(flags)");
+    if (!lrc) lrc = check_cuda(cudaMemset(f, 0, fb), "cudaMemset(flags)");
+    if (!lrc) lrc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(flags)");
+    if (!lrc)
+      ctx->flags_mem = f;
+    else if (f)
+      cudaFree(f);
+  }
+  struct Entry {
+    IpcRecord flags, out;
+    int status;
+  } mine = {};
+  if (!lrc) lrc = make_record(ctx->flags_mem, fb, &mine.flags);
+  if (!lrc) lrc = make_record(C_full, bytes, &mine.out);
+  mine.status = lrc == CLOVE_OK ? 1 : 0;
+  std::vector<Entry> all(ctx->nranks);
+  int rc = all_gather_host(ctx, &mine, sizeof(Entry), all.data());
+  if (rc) return rc;
+  bool ok = true;
+  for (const Entry& e : all) ok = ok && e.status == 1 && e.out.bytes == bytes;
+  if (!ok) return lrc ? lrc : fail(CLOVE_ERR_INVALID_ARG, "another rank could not register");
+  SharedBuf flags, out;
+  std::vector<IpcRecord> fr(ctx->nranks), orr(ctx->nranks);
+  for (int q = 0; q < ctx->nranks; ++q) {
+    fr[q] = all[q].flags;
+    orr[q] = all[q].out;
+  }
+  int orc = CLOVE_OK;
+  if (!ctx->flags_ready) orc = open_shared(ctx, ctx->flags_mem, fb, fr.data(), &flags);
+  if (!orc) orc = open_shared(ctx, C_full, bytes, orr.data(), &out);
+  if (!all_ok(ctx, orc == CLOVE_OK)) {
+    if (flags.local != nullptr) close_shared(ctx, &flags);
+    if (out.local != nullptr) close_shared(ctx, &out);
+    return orc ? orc : fail(CLOVE_ERR_CUDA, "another rank could not map the shared buffers");
+  }
+  if (!ctx->flags_ready) {
+    ctx->flags = flags;
     ctx->flags_ready = true;
   }
-  SharedBuf sb;
-  rc = share_buffer(ctx, C_full, bytes, &sb);
-  if (rc) return rc;
-  ctx->outputs.push_back(sb);
+  ctx->outputs.push_back(out);
   return CLOVE_OK;
 }
 
 int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full) {
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
-  for (size_t i = 0; i < ctx->outputs.size(); ++i) {
-    if (ctx->outputs[i].local == C_full) {
-      int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(unregister)");
-      close_shared(ctx, &ctx->outputs[i]);
-      ctx->outputs.erase(ctx->outputs.begin() + static_cast<long>(i));
-      // No rank frees its buffer while another still has it mapped.
-      const int rc2 = host_barrier(ctx);
-      return rc ? rc : rc2;
-    }
-  }
-  return fail(CLOVE_ERR_INVALID_ARG, "buffer is not registered");
+  long idx = -1;
+  for (size_t i = 0; i < ctx->outputs.size(); ++i)
+    if (ctx->outputs[i].local == C_full) idx = static_cast<long>(i);
+  if (!all_ok(ctx, idx >= 0))
+    return idx < 0 ? fail(CLOVE_ERR_INVALID_ARG, "buffer is not registered")
+                   : fail(CLOVE_ERR_INVALID_ARG, "buffer is not registered on another rank");
+  int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(unregister)");
+  close_shared(ctx, &ctx->outputs[static_cast<size_t>(idx)]);
+  ctx->outputs.erase(ctx->outputs.begin() + idx);
+  // No rank frees its buffer while another still has it mapped.
+  const int rc2 = host_barrier(ctx);
+  return rc ? rc : rc2;
 }
 
 int clove_nsplit_col_begin(int N, int nranks, int rank) {
@@ -507,18 +542,16 @@ int clove_nsplit_init(clove_nsplit_ctx** ctx, int nranks, int rank, const uint8_
 int clove_nsplit_destroy(clove_nsplit_ctx* ctx) {
   if (ctx == nullptr) return CLOVE_OK;
   int rc = CLOVE_OK;
-  if (!ctx->outputs.empty() || ctx->flags_ready) {
+  if (ctx->ipc_used) {  // the same on every rank, so all take the barrier below
     rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(destroy)");
     for (SharedBuf& b : ctx->outputs) close_shared(ctx, &b);
     ctx->outputs.clear();
-    if (ctx->flags_ready) {
-      void* f = ctx->flags.local;
-      close_shared(ctx, &ctx->flags);
-      const int rc2 = host_barrier(ctx);  // peers unmapped our flags before we free them
-      cudaFree(f);
-      if (!rc) rc = rc2;
-      ctx->flags_ready = false;
-    }
+    if (ctx->flags_ready) close_shared(ctx, &ctx->flags);
+    ctx->flags_ready = false;
+    const int rc2 = host_barrier(ctx);  // peers unmapped our buffers before they are freed
+    if (ctx->flags_mem) cudaFree(ctx->flags_mem);
+    ctx->flags_mem = nullptr;
+    if (!rc) rc = rc2;
   }
   if (g_nccl.handle) {
     const int rc3 = check_nccl(g_nccl.CommDestroy(ctx->comm), "ncclCommDestroy");

@@ -55,14 +55,27 @@ class NSplit:
         """Collective: every rank registers its own [M, N] fp16 replicated output in
         the same order; gemm_fp16(..., C_full=C_full, replicate_C=True) then writes
         every rank's copy from the GEMM epilogue (no all-gather)."""
-        _need(C_full, "C_full", torch.float16, 2)
-        check(lib().clove_nsplit_register_output(self._ctx, _ptr(C_full),
-                                                 C_full.numel() * C_full.element_size()))
+        # A rank whose argument is bad still takes part (with a null pointer, which
+        # fails the registration on every rank) so that no rank waits alone.
+        err, ptr, nbytes = None, None, 0
+        try:
+            _need(C_full, "C_full", torch.float16, 2)
+            ptr, nbytes = _ptr(C_full), C_full.numel() * C_full.element_size()
+        except Exception as e:  # raised after the collective call
+            err = e
+        rc = lib().clove_nsplit_register_output(self._ctx, ptr, nbytes)
+        if err is not None:
+            raise err
+        check(rc)
         self._outputs[C_full.data_ptr()] = C_full  # keeps the memory alive while mapped
 
     def unregister_output(self, C_full: torch.Tensor) -> None:
         """Collective: unmaps C_full on every rank."""
-        check(lib().clove_nsplit_unregister_output(self._ctx, _ptr(C_full)))
+        try:
+            ptr = _ptr(C_full)
+        except Exception:
+            ptr = None  # still takes part; fails on every rank
+        check(lib().clove_nsplit_unregister_output(self._ctx, ptr))
         self._outputs.pop(C_full.data_ptr(), None)
 
     def __del__(self):

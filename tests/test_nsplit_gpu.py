@@ -94,6 +94,15 @@ def _worker_fused(rank, world, port, q):
         from clove_compute_b200 import workloads as wl
         ns = cc.NSplit(rank, world)
         out = []
+        # A local failure on one rank (a misaligned C on rank 1) fails the collective
+        # registration on every rank, and nobody is left inside a collective.
+        buf = torch.zeros(256 * 256 + 8, dtype=torch.float16, device="cuda")
+        bad = (buf[1:1 + 256 * 256] if rank == 1 else buf[:256 * 256]).view(256, 256)
+        try:
+            ns.register_output(bad)
+            out.append(1.0)  # must not happen: fails the error check below
+        except Exception:
+            pass
         # (M, N, K): CTA-pair tiles, the one-SM tile kernel, a ragged M, and
         # N = 1000 whose shard edge (500) is not a multiple of 8 -> all-gather.
         for (M, N, K) in [(2048, 2048, 1024), (512, 2048, 1024), (300, 1024, 512),
