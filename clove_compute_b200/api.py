@@ -221,6 +221,16 @@ def debug_stream_read(src, out, stream=None) -> None:
                                         _stream(stream)))
 
 
+def debug_peer_wait_timeout(words: torch.Tensor, timeout_ns: int, stream=None) -> None:
+    """Runs the N-split's cross-rank completion wait for a two-rank group whose
+    other rank never signals (``words``: 8 int64 of device scratch); the bounded
+    wait runs out after ``timeout_ns`` and records device error 1."""
+    _need(words, "words", torch.int64, 1)
+    if words.numel() < 8:
+        raise ValueError("words needs 8 elements")
+    check(lib().clove_debug_peer_wait_timeout(_ptr(words), int(timeout_ns), _stream(stream)))
+
+
 def debug_stream_k_plan(tiles: int, pairs: int, kb_total: int, force: int = 0) -> dict:
     """The CTA-pair kernel's stream-K schedule for `tiles` output tiles of kb_total
     K blocks on `pairs` CTA pairs (host only; force 0 auto, 1 never, 2 always)."""

@@ -84,12 +84,15 @@ int launch_scale_f16(void* C, long long n, float beta, cudaStream_t stream) {
 namespace clove {
 namespace rt {
 
+// timeout_ns 0: the product bound (2 s).
 int launch_peer_signal_wait(int nranks, int rank, unsigned long long* epoch,
-                            unsigned long long* const* flags, cudaStream_t stream) {
+                            unsigned long long* const* flags, unsigned long long timeout_ns,
+                            cudaStream_t stream) {
   if (nranks > kern::kMaxPeers) return fail(CLOVE_ERR_UNSUPPORTED, "too many ranks");
   kern::PeerSync ps = {};
   ps.nranks = nranks;
   ps.rank = rank;
+  ps.timeout_ns = timeout_ns ? timeout_ns : dev::kWaitTimeoutNs;
   ps.epoch = epoch;
   for (int q = 0; q < nranks; ++q) ps.flags[q] = flags[q];
   kern::peer_signal_wait_kernel<<<1, 32, 0, stream>>>(ps);

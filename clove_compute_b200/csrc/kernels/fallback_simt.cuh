@@ -170,10 +170,11 @@ __global__ void relayout_columns_kernel(const uint16_t* __restrict__ staging,
 // that preceded this kernel on the stream are visible first) and waits until
 // every other rank's slot in its own array holds >= e (system-scope acquire).
 // All ranks make the same calls in the same order, so the epochs agree, also
-// when the kernel is replayed from a CUDA graph. The wait gives up after 2 s and
-// records a timeout instead of hanging.
+// when the kernel is replayed from a CUDA graph. The wait gives up after
+// timeout_ns (2 s in the product) and records a timeout instead of hanging.
 struct PeerSync {
   int nranks, rank;
+  unsigned long long timeout_ns;
   unsigned long long* epoch;                    // this rank's counter
   unsigned long long* flags[kMaxPeers];         // flags[q]: rank q's array [nranks]
 };
@@ -187,23 +188,9 @@ __global__ void peer_signal_wait_kernel(PeerSync ps) {
   }
   e = __shfl_sync(0xffffffffu, e, 0);
   __threadfence_system();
-  if (lane < ps.nranks)
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ps.flags[lane] + ps.rank), "l"(e)
-                 : "memory");
-  if (lane < ps.nranks && lane != ps.rank) {
-    const unsigned long long* f = ps.flags[ps.rank] + lane;
-    const uint64_t t0 = dev::globaltimer_ns();
-    for (;;) {
-      unsigned long long v;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
-      if (v >= e) break;
-      if (dev::globaltimer_ns() - t0 > dev::kWaitTimeoutNs) {
-        dev::record_error(dev::kDevErrWaitTimeout);
-        break;
-      }
-      __nanosleep(128);
-    }
-  }
+  if (lane < ps.nranks) dev::st_release_sys_u64(ps.flags[lane] + ps.rank, e);
+  if (lane < ps.nranks && lane != ps.rank)
+    dev::wait_flag_geq(ps.flags[ps.rank] + lane, e, ps.timeout_ns);
   __syncwarp();
 }
 

@@ -301,6 +301,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     const uint32_t q = warp & 3u;
     const int h = static_cast<int>(warp - 10) >> 2;  // column half of the tile
     const int row = static_cast<int>(q * 32 + lane);
+    // Replicated output: announce that this rank reached the call (every earlier
+    // kernel on its stream, the readers of its C included, has completed: this
+    // kernel has no programmatic dependence); the remote stores wait below until
+    // every rank has.
+    unsigned long long ready_e = 0;
+    if (peer.count > 0 && lane == 0) ready_e = dev::peer_ready_publish(peer);
     float2 acc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.f, 0.f);
@@ -400,8 +406,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       __syncwarp();
       if (lane == 0) {
         dev::tma_store_2d(&tmC, stg, n0 + h * 64, m0 + static_cast<int>(q) * 32);
-        // Replicated output of an N-split: the same staged slab to every rank's C.
-        for (int d = 0; d < peer.count; ++d)
+        // Replicated output of an N-split: the same staged slab to every rank's C,
+        // once every rank is ready to receive it (none after a timeout).
+        const int peer_n = peer.count > 0 && dev::peer_ready_wait(peer, ready_e) ? peer.count : 0;
+        for (int d = 0; d < peer_n; ++d)
           dev::tma_store_2d(&peer.maps[d], stg, peer.col0 + n0 + h * 64,
                             m0 + static_cast<int>(q) * 32);
         dev::bulk_commit_group();

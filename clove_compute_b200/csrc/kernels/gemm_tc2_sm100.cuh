@@ -265,6 +265,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t stg_count = 0;
     uint32_t ph0 = 0, ph1 = 0;  // completed phases of skbar[0] / skbar[1]
     int it = 0;
+    // Replicated output: no remote store before every rank has reached this call.
+    const int peer_n = peer_ready_warp(ep.peer, lane, abort_flag);
     Tc2Sched sched(pair, pairs, sk, kb_total);
     Tc2Work w;
     for (; sched.next(w); ++it) {
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(192, 1)
               add_slots(v, c0, 1);
               store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
                                            stg_base, stg_count, &tmC,
-                                           m0 + static_cast<int>(q) * 32);
+                                           m0 + static_cast<int>(q) * 32, peer_n);
             }
             if (*abort_flag) break;
             continue;
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(192, 1)
               add_slots(v, c0, 0);
               store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
                                            stg_base, stg_count, &tmC,
-                                           m0 + static_cast<int>(q) * 32);
+                                           m0 + static_cast<int>(q) * 32, peer_n);
             }
           }
           if (*abort_flag) break;
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         store_chunk<Op, 2, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr, lane,
-                                     stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32);
+                                     stg_base, stg_count, &tmC, m0 + static_cast<int>(q) * 32, peer_n);
       }
       if (*abort_flag) break;
     }

@@ -219,9 +219,18 @@ namespace rt {
 int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int swizzle,
                      kern::PeerOut* out) {
   if (pt.count > kern::kMaxPeers) return fail(CLOVE_ERR_UNSUPPORTED, "too many ranks");
+  if (pt.count > 1 && (pt.ready_in == nullptr || pt.epoch == nullptr))
+    return fail(CLOVE_ERR_INVALID_ARG, "replicated output without its ready handshake");
   out->count = pt.count;
   out->col0 = pt.col0;
+  out->rank = pt.rank;
+  out->ready_in = pt.ready_in;
+  out->epoch = pt.epoch;
+  for (int d = 0; d < kern::kMaxPeers; ++d)
+    out->ready_slot[d] = d < pt.count ? pt.ready_slot[d] : nullptr;
   for (int d = 0; d < pt.count; ++d) {
+    if (d != pt.rank && pt.ready_slot[d] == nullptr)
+      return fail(CLOVE_ERR_INVALID_ARG, "replicated output without its ready handshake");
     const int rc = encode_tmap_2d(&out->maps[d], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pt.dst[d],
                                   static_cast<uint64_t>(pt.col0) + N, M,
                                   static_cast<uint64_t>(pt.ldc) * 2, box_cols, 32, swizzle);
@@ -307,7 +316,7 @@ SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force) {
 // CTA-pair 256 x 256 tile kernel (fp16 C only).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
-                    const void* B2, const PeerTargets* peer) {
+                    const void* B2, const PeerTargets* peer, bool allow_stream_k) {
   if (peer != nullptr && B2 != nullptr) return CLOVE_ERR_UNSUPPORTED;
   using SF = kern::Tc2Shape<kern::OpF16>;
   using SI = kern::Tc2Shape<kern::OpI8>;
@@ -387,7 +396,7 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
   const int kb_total = (K + bk - 1) / bk;
   const Override ov = get_override();
   const SkPlan plan = plan_stream_k(tiles, resident, kb_total,
-                                    glu ? 1 : ov.path == 4 ? ov.split : 0);
+                                    (glu || !allow_stream_k) ? 1 : ov.path == 4 ? ov.split : 0);
   skp.dp_tiles = plan.dp_tiles;
   skp.sk_tiles = plan.sk_tiles;
   skp.max_contrib = plan.max_contrib;

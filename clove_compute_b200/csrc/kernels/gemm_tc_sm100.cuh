@@ -181,6 +181,21 @@ __device__ __forceinline__ void epi_pack(const uint32_t (&v)[CHUNK], const EpiPa
   }
 }
 
+// Receiver-ready handshake of a replicated output (PeerOut), once per epilogue
+// warp before its first store: the number of ranks to store to (all of them, or
+// none after a timeout, which also raises the CTA's abort flag so every role
+// unwinds). 0 without a replicated output.
+__device__ __forceinline__ int peer_ready_warp(const PeerOut& po, uint32_t lane,
+                                               volatile int* abort_flag) {
+  if (po.count <= 0) return 0;
+  int ok = 1;
+  if (lane == 0) ok = dev::peer_ready_gate(po) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) return po.count;
+  if (lane == 0) *abort_flag = 1;
+  return 0;
+}
+
 // Epilogue of one CHUNK-column slice of a 32-row warp slab: epi_pack on this
 // thread's row, swizzled staging, TMA store of the warp's slab.
 template <class Op, int OUT_BYTES, int CHUNK>
@@ -189,7 +204,7 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
                                             float row_scale, int32_t row_corr, uint32_t lane,
                                             uint8_t* stg_base, uint32_t& stg_count,
                                             const CUtensorMap* tmC, int store_row0,
-                                            int plane = -1) {
+                                            int peer_n, int plane = -1) {
   constexpr int STG_ROW = CHUNK * OUT_BYTES;
   constexpr int PKTS = STG_ROW / 16;
   uint32_t pk[PKTS][4];
@@ -218,9 +233,10 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
     if constexpr (OUT_BYTES == 2) {
       // Replicated output (never with batch planes): the same staged tile to every
       // rank's C. `ep` is the kernel's __grid_constant__ parameter here, so the
-      // maps are addressed in parameter space.
+      // maps are addressed in parameter space. peer_n is ep.peer.count once the
+      // warp has passed the receiver-ready handshake, 0 if that timed out.
 #pragma unroll 1
-      for (int d = 0; d < ep.peer.count; ++d)
+      for (int d = 0; d < peer_n; ++d)
         dev::tma_store_2d(&ep.peer.maps[d], stg, ep.peer.col0 + ncol0, store_row0);
     }
     dev::bulk_commit_group();
@@ -445,6 +461,8 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t stg_count = 0;
     int it = 0;
     if constexpr (SPLIT) dev::cluster_wait();  // every peer's rbar is initialised
+    // Replicated output: no remote store before every rank has reached this call.
+    const int peer_n = peer_ready_warp(ep.peer, lane, abort_flag);
     for (int tile = tile_first; tile < num_tiles; tile += tile_stride, ++it) {
       int m_blk, n_blk;
       const int plane = tile / tiles_mn;
@@ -601,7 +619,7 @@ __global__ void __launch_bounds__(192, 1)
           }
           store_chunk<Op, OUT_BYTES, S::CHUNK>(v, ep, row, n0 + c0, M, N, K, row_scale, row_corr,
                                                lane, stg_base, stg_count, &tmC,
-                                               m0 + static_cast<int>(q) * 32, plane);
+                                               m0 + static_cast<int>(q) * 32, peer_n, plane);
         }
       }
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);

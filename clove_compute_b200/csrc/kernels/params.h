@@ -21,10 +21,23 @@ enum EpiMode : int {
 // through CUDA IPC; NVLink carries the remote stores), at columns col0 + n. Map d
 // spans columns [0, col0 + N) of rank d's C, so the box clips at this rank's last
 // column. count == 0: no replicated output.
+//
+// Receiver-ready handshake: rank d's C may still be read by rank d's consumers of
+// the previous call when this call starts, so no remote store leaves before every
+// rank has reached this call on its stream. `epoch` counts this rank's completed
+// replicated calls (the completion-signal kernel that follows each call bumps it);
+// at its start the call publishes epoch + 1 into slot `rank` of every rank's
+// ready array (ready_slot[d] = &ready_d[rank], system-scope release) and its
+// epilogue waits until every slot of its own array (ready_in) has reached
+// epoch + 1 before the first remote store (bounded, like every wait here).
 constexpr int kMaxPeers = 8;
 struct PeerOut {
   int count;
   int col0;
+  int rank;
+  unsigned long long* ready_slot[kMaxPeers];
+  const unsigned long long* ready_in;
+  const unsigned long long* epoch;
   CUtensorMap maps[kMaxPeers];
 };
 

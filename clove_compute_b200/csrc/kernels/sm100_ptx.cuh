@@ -478,6 +478,62 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ----------------------------------------------------------------------------
+// Cross-rank flags (system scope: the flag arrays of other ranks are IPC
+// mappings reached over NVLink)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spins until *flag >= target or timeout_ns has passed (then records a timeout
+// and returns false).
+__device__ __forceinline__ bool wait_flag_geq(const unsigned long long* flag,
+                                              unsigned long long target, uint64_t timeout_ns) {
+  if (ld_acquire_sys_u64(flag) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (ld_acquire_sys_u64(flag) >= target) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      record_error(kDevErrWaitTimeout);
+      return false;
+    }
+    __nanosleep(128);
+  }
+}
+
+// Receiver-ready handshake of a replicated-output GEMM (kern::PeerOut), run by
+// one thread of each epilogue warp before that warp's first store. The caller
+// must have passed griddepcontrol.wait (or have been launched without
+// programmatic dependence), so every earlier kernel on this rank's stream -- in
+// particular whatever read this rank's replicated C after the previous call --
+// has completed. Publishes "this rank reached call e" into every rank's ready
+// array (all publishers of a call store the same e, so repeats are harmless), then
+// waits until every rank has published e. False (error recorded) on a timeout.
+template <class PeerOutT>
+__device__ __forceinline__ unsigned long long peer_ready_publish(const PeerOutT& po) {
+  const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(po.epoch) + 1;
+  for (int d = 0; d < po.count; ++d)
+    if (d != po.rank) st_release_sys_u64(po.ready_slot[d], e);
+  return e;
+}
+template <class PeerOutT>
+__device__ __forceinline__ bool peer_ready_wait(const PeerOutT& po, unsigned long long e) {
+  bool ok = true;
+  for (int d = 0; d < po.count && ok; ++d)
+    if (d != po.rank) ok = wait_flag_geq(po.ready_in + d, e, kWaitTimeoutNs);
+  return ok;
+}
+template <class PeerOutT>
+__device__ __forceinline__ bool peer_ready_gate(const PeerOutT& po) {
+  return peer_ready_wait(po, peer_ready_publish(po));
+}
+
 }  // namespace dev
 }  // namespace clove
 

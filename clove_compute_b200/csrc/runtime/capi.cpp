@@ -365,6 +365,38 @@ int clove_swiglu_fused(const void* input, const void* W_gate, const void* W_up, 
 // ---------------------------------------------------------------------------
 // INT8
 // ---------------------------------------------------------------------------
+extern "C++" {  // internal C++ entry (gemm_int8_noalloc.cu)
+namespace clove {
+namespace rt {
+// Kernel family of an int8 call with fp16 C (see internal.h).
+int int8_route(const int8_t* A, const int8_t* B, const void* C, int M, int N, int K,
+               const char** family) {
+  DeviceInfo dev;
+  const int rc = current_device(&dev);
+  if (rc) return rc;
+  const Override ov = get_override();
+  const bool tc_ok = K > 0 && K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) &&
+                     aligned16(C);
+  const bool gemv_ok = K > 0 && N <= 8 && K % 16 == 0 && aligned16(A) &&
+                       gemv_int8_smem(N, K) <= 200 * 1024;
+  int path = ov.path;
+  if ((path == 1 || path == 4) && !tc_ok) path = 0;
+  if (path == 2 && !gemv_ok) path = 0;
+  if (path == 0) path = gemv_ok ? 2 : (tc_ok ? 1 : 3);
+  if (path == 2) {
+    *family = "gemv_int8";
+  } else if (path == 3) {
+    *family = "simt_int8";
+  } else {
+    const TcPlan plan = plan_tc(M, N, K, 1, dev.num_sms);
+    *family = plan.pair ? "tc2_int8" : plan.split > 1 ? "tc_int8_split" : "tc_int8";
+  }
+  return CLOVE_OK;
+}
+}  // namespace rt
+}  // namespace clove
+}  // extern "C++"
+
 // mode: 1 per-tensor, 2 row/col, 3 raw int32 accumulators.
 static int gemm_int8_impl(const int8_t* A, const int8_t* B, void* C, int M, int N, int K, int mode,
                           float scale, int za, int zb, const float* rs, const float* cs,

@@ -65,12 +65,16 @@ extern "C" int clove_gemm_int8_noalloc(const int8_t* A_q, const int8_t* B_q, voi
   if (M == 0 || N == 0) return CLOVE_OK;
   if (A_q == nullptr || B_q == nullptr || C == nullptr)
     return fail(CLOVE_ERR_INVALID_ARG, "null matrix pointer");
-  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  const bool tc_ok = K > 0 && K % 16 == 0 && N % 16 == 0 && a16(A_q) && a16(B_q) && a16(C);
-  // Without zero points, or on shapes the tile kernel cannot take (those go to
-  // the GEMV / SIMT kernels, which keep their sums in registers), the ordinary
-  // entry point allocates nothing.
-  if ((A_zero == 0 && B_zero == 0) || !tc_ok)
+  // The kernel family clove_gemm_int8 would pick for this shape (its automatic
+  // dispatch and the test override alike), so both entry points run the same
+  // kernel and give the same bits.
+  const char* family = nullptr;
+  int rc = int8_route(A_q, B_q, C, M, N, K, &family);
+  if (rc) return rc;
+  // Without zero points, or on the GEMV / SIMT kernels (which keep their sums in
+  // registers), the ordinary entry point allocates nothing.
+  const bool tile = family[0] == 't';
+  if ((A_zero == 0 && B_zero == 0) || !tile)
     return clove_gemm_int8(A_q, B_q, C, M, N, K, A_scale, A_zero, B_scale, B_zero, stream);
   if (static_cast<long long>(M) + N > kNoAllocMaxSums)
     return fail(CLOVE_ERR_UNSUPPORTED,
@@ -78,7 +82,7 @@ extern "C" int clove_gemm_int8_noalloc(const int8_t* A_q, const int8_t* B_q, voi
                 "(use clove_gemm_int8)",
                 static_cast<long long>(M) + N, kNoAllocMaxSums);
   DeviceInfo dev;
-  int rc = current_device(&dev);
+  rc = current_device(&dev);
   if (rc) return rc;
   int32_t* sums = nullptr;
   rc = sums_address(dev.device, &sums);
@@ -97,5 +101,9 @@ extern "C" int clove_gemm_int8_noalloc(const int8_t* A_q, const int8_t* B_q, voi
   ep.zb = B_zero;
   ep.row_sum = sums;
   ep.col_sum = sums + M;
+  // CTA pairs with whole-K tiles only: the stream-K schedule would need a
+  // workspace. Its sums are the same (exact int32), so results do not change.
+  if (family[2] == '2')
+    return launch_gemm_tc2(kTcI8, A_q, B_q, C, M, N, K, ep, dev, s, nullptr, nullptr, false);
   return launch_gemm_tc(kTcI8, plan.bn, plan.split, 2, A_q, B_q, C, M, N, K, ep, dev, s);
 }

@@ -51,12 +51,19 @@ bool ws2_selected();
 
 // Replicated output of an N-split fp16 GEMM (kern::PeerOut): the row-major
 // [M, ldc] C of every rank, mapped into this process; this rank's columns start
-// at col0. The tile launchers encode one TMA store map per rank from it.
+// at col0. The tile launchers encode one TMA store map per rank from it. The
+// receiver-ready handshake (kern::PeerOut) uses ready_slot[q] = slot `rank` of
+// rank q's ready array, ready_in = this rank's ready array and epoch = this
+// rank's count of completed replicated calls.
 struct PeerTargets {
   int count;
   int ldc;
   int col0;
+  int rank;
   void* dst[8];
+  unsigned long long* ready_slot[8];
+  const unsigned long long* ready_in;
+  const unsigned long long* epoch;
 };
 
 // Tile shape chosen for a tensor-core call (capi.cpp).
@@ -66,6 +73,11 @@ struct TcPlan {
   bool pair;  // CTA-pair 256 x 256 kernel
 };
 TcPlan plan_tc(int M, int N, int K, int elem, int num_sms);
+// Kernel family clove_gemm_int8 runs for this shape and these pointers (with the
+// test override applied): "gemv_int8", "simt_int8", "tc2_int8" (CTA pairs),
+// "tc_int8_split" or "tc_int8".
+int int8_route(const int8_t* A, const int8_t* B, const void* C, int M, int N, int K,
+               const char** family);
 
 // ---- tensor-core tile kernels (kernels/gemm_tc_sm100.cu)
 enum TcOp { kTcF16 = 0, kTcI8 = 1 };
@@ -85,9 +97,12 @@ struct SkPlan {
 SkPlan plan_stream_k(int tiles, int pairs, int kb_total, int force);
 // CTA-pair kernel: 256 x 256 tiles on two SMs (fp16 C).
 // B2 != nullptr: fp16 GLU, C = silu(A . B) * (A . B2) (256 x 128 output tiles).
+// allow_stream_k = false keeps whole-K tiles, which need no workspace (the call
+// then allocates nothing).
 int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N, int K,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
-                    const void* B2 = nullptr, const PeerTargets* peer = nullptr);
+                    const void* B2 = nullptr, const PeerTargets* peer = nullptr,
+                    bool allow_stream_k = true);
 // True when (op, bn, split, out_bytes) is an instantiated kernel.
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();

@@ -38,7 +38,8 @@ namespace rt {
 int launch_relayout_columns(const void* staging, void* C, int M, int N, int P, int Nmax,
                             int elem_bytes, cudaStream_t stream);
 int launch_peer_signal_wait(int nranks, int rank, unsigned long long* epoch,
-                            unsigned long long* const* flags, cudaStream_t stream);
+                            unsigned long long* const* flags, unsigned long long timeout_ns,
+                            cudaStream_t stream);
 int gemm_fp16_replicated(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                          const PeerTargets& peer, cudaStream_t s);
 int gemm_int4_replicated(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
@@ -54,6 +55,18 @@ using namespace clove::rt;
 using clove::kern::kMaxPeers;
 
 namespace {
+// Layout of each rank's IPC-shared flag array (unsigned long long words):
+//   [0, kMaxPeers)            done[q]: rank q has finished storing call e into this
+//                             rank's C (written by q's completion-signal kernel)
+//   [kMaxPeers, 2 kMaxPeers)  ready[q]: rank q's stream has reached call e, so q's
+//                             readers of its C from call e-1 have completed
+//                             (written at the start of q's GEMM, kern::PeerOut)
+//   [2 kMaxPeers]             this rank's count of completed replicated calls
+constexpr int kFlagDone = 0;
+constexpr int kFlagReady = kMaxPeers;
+constexpr int kFlagEpoch = 2 * kMaxPeers;
+constexpr size_t kFlagBytes = sizeof(unsigned long long) * (2 * kMaxPeers + 1);
+
 // One IPC-shared buffer: this rank's pointer and every rank's, mapped here.
 struct SharedBuf {
   void* local = nullptr;
@@ -79,7 +92,7 @@ struct clove_nsplit_ctx {
   int nranks;
   int device;
   std::vector<SharedBuf> outputs;  // registered replicated outputs
-  SharedBuf flags;                 // [nranks] completion flags + this rank's epoch
+  SharedBuf flags;                 // FlagLayout: done and ready slots + this rank's epoch
   void* flags_mem = nullptr;       // this rank's flag array (cudaMalloc)
   bool flags_ready = false;        // every rank's flag array is mapped here
   bool ipc_used = false;           // a registration was attempted (same on every rank)
@@ -324,6 +337,33 @@ const SharedBuf* find_output(const clove_nsplit_ctx* ctx, const void* C_full) {
   return nullptr;
 }
 
+// The replicated-output targets of this rank: every rank's C and the ready
+// handshake's flag words.
+PeerTargets peer_targets(const clove_nsplit_ctx* ctx, const SharedBuf& out, int N) {
+  PeerTargets peer = {};
+  peer.count = ctx->nranks;
+  peer.ldc = N;
+  peer.col0 = clove_nsplit_col_begin(N, ctx->nranks, ctx->rank);
+  peer.rank = ctx->rank;
+  unsigned long long* own = static_cast<unsigned long long*>(ctx->flags.local);
+  peer.ready_in = own + kFlagReady;
+  peer.epoch = own + kFlagEpoch;
+  for (int q = 0; q < ctx->nranks; ++q) {
+    peer.dst[q] = out.ptr[q];
+    peer.ready_slot[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]) + kFlagReady + ctx->rank;
+  }
+  return peer;
+}
+
+// The completion signal that follows a replicated-output GEMM on the stream.
+int signal_done(const clove_nsplit_ctx* ctx, cudaStream_t s) {
+  unsigned long long* fl[kMaxPeers] = {};
+  for (int q = 0; q < ctx->nranks; ++q)
+    fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]) + kFlagDone;
+  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kFlagEpoch;
+  return launch_peer_signal_wait(ctx->nranks, ctx->rank, epoch, fl, 0, s);
+}
+
 // Replicated fp16 output without a collective (see the file comment). Returns
 // CLOVE_ERR_UNSUPPORTED, with nothing launched, when the shapes or the kernel the
 // dispatch picks cannot store into the replicated C directly; the caller then
@@ -344,19 +384,9 @@ int gemm_fp16_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const void* 
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!a16(A) || !a16(B_shard) || !a16(C_shard))
     return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned A, B_shard, C_shard");
-  const int col0 = clove_nsplit_col_begin(N, P, ctx->rank);
-  const int Nr = N / P;
-  PeerTargets peer = {};
-  peer.count = P;
-  peer.ldc = N;
-  peer.col0 = col0;
-  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
-  int rc = gemm_fp16_replicated(A, B_shard, C_shard, M, Nr, K, alpha, peer, s);
-  if (rc) return rc;
-  unsigned long long* fl[kMaxPeers] = {};
-  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
-  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
-  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+  const PeerTargets peer = peer_targets(ctx, out, N);
+  const int rc = gemm_fp16_replicated(A, B_shard, C_shard, M, N / P, K, alpha, peer, s);
+  return rc ? rc : signal_done(ctx, s);
 }
 
 // INT4 (config 5's sharded weights): the same route through the INT4 tensor-core
@@ -375,18 +405,10 @@ int gemm_int4_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const uint8_
   if (!a16(A_q) || !a16(A_scale) || !a16(A_zero) || !a16(B_q) || !a16(B_scale) ||
       !a16(B_zero) || !a16(C_shard))
     return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned operands");
-  PeerTargets peer = {};
-  peer.count = P;
-  peer.ldc = N;
-  peer.col0 = clove_nsplit_col_begin(N, P, ctx->rank);
-  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
-  int rc = gemm_int4_replicated(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C_shard, M, N / P, K,
-                                peer, s);
-  if (rc) return rc;
-  unsigned long long* fl[kMaxPeers] = {};
-  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
-  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
-  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+  const PeerTargets peer = peer_targets(ctx, out, N);
+  const int rc = gemm_int4_replicated(A_q, A_scale, A_zero, B_q, B_scale, B_zero, C_shard, M,
+                                      N / P, K, peer, s);
+  return rc ? rc : signal_done(ctx, s);
 }
 
 // INT8 with per-row / per-column scales: the tile kernels' epilogue again. The
@@ -402,17 +424,9 @@ int gemm_int8_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const int8_t
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!a16(A_q) || !a16(B_q) || !a16(C_shard))
     return fail(CLOVE_ERR_INVALID_ARG, "replicated output needs 16-byte aligned operands");
-  PeerTargets peer = {};
-  peer.count = P;
-  peer.ldc = N;
-  peer.col0 = clove_nsplit_col_begin(N, P, ctx->rank);
-  for (int q = 0; q < P; ++q) peer.dst[q] = out.ptr[q];
-  int rc = gemm_int8_rowcol_replicated(A_q, B_q, C_shard, M, N / P, K, rs, cs, peer, s);
-  if (rc) return rc;
-  unsigned long long* fl[kMaxPeers] = {};
-  for (int q = 0; q < P; ++q) fl[q] = static_cast<unsigned long long*>(ctx->flags.ptr[q]);
-  unsigned long long* epoch = static_cast<unsigned long long*>(ctx->flags.local) + kMaxPeers;
-  return launch_peer_signal_wait(P, ctx->rank, epoch, fl, s);
+  const PeerTargets peer = peer_targets(ctx, out, N);
+  const int rc = gemm_int8_rowcol_replicated(A_q, B_q, C_shard, M, N / P, K, rs, cs, peer, s);
+  return rc ? rc : signal_done(ctx, s);
 }
 
 }  // namespace
@@ -428,7 +442,7 @@ extern "C" {
 int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes) {
   if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
   ctx->ipc_used = true;
-  const size_t fb = sizeof(unsigned long long) * (kMaxPeers + 1);
+  const size_t fb = kFlagBytes;
   int lrc = CLOVE_OK;
   if (C_full == nullptr || bytes == 0)
     lrc = fail(CLOVE_ERR_INVALID_ARG, "bad register_output arguments");
@@ -439,7 +453,7 @@ int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t byt
   else if (find_output(ctx, C_full) != nullptr)
     lrc = fail(CLOVE_ERR_INVALID_ARG, "buffer already registered");
   if (!lrc && ctx->flags_mem == nullptr) {
-    // Flag slots [kMaxPeers] then this rank's epoch, zeroed before anyone signals.
+    // Done and ready slots, then this rank's epoch, zeroed before anyone signals.
     void* f = nullptr;
     lrc = check_cuda(cudaMalloc(&f, fb), "cudaMalloc(flags)");
     if (!lrc) lrc = check_cuda(cudaMemset(f, 0, fb), "cudaMemset(flags)");
@@ -498,6 +512,21 @@ int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full) {
   // No rank frees its buffer while another still has it mapped.
   const int rc2 = host_barrier(ctx);
   return rc ? rc : rc2;
+}
+
+int clove_debug_peer_wait_timeout(unsigned long long* words, unsigned long long timeout_ns,
+                                  void* stream) {
+  if (words == nullptr || (reinterpret_cast<uintptr_t>(words) & 7u) != 0 || timeout_ns == 0 ||
+      timeout_ns > 2000000000ull)
+    return fail(CLOVE_ERR_INVALID_ARG, "bad peer-wait test arguments");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = check_cuda(cudaMemsetAsync(words, 0, 8 * sizeof(unsigned long long), s),
+                      "cudaMemsetAsync(peer-wait test)");
+  if (rc) return rc;
+  // Rank 0 of a two-rank group whose second rank never signals: words[0] is the
+  // epoch, words[1..2] rank 0's flag array, words[3..4] the absent rank's.
+  unsigned long long* fl[kMaxPeers] = {words + 1, words + 3};
+  return launch_peer_signal_wait(2, 0, words, fl, timeout_ns, s);
 }
 
 int clove_nsplit_col_begin(int N, int nranks, int rank) {

@@ -49,7 +49,8 @@ const char* clove_last_error_string(void);
 
 /* Reads and clears the device-side error word of the current device (a kernel
  * whose bounded wait expired sets it). Synchronises the device. *code = 0 when
- * no kernel reported an error. */
+ * no kernel reported an error, 1 when a bounded wait expired (mbarrier or
+ * cross-rank flag), 2 when a kernel was launched with a shape it rejects. */
 int clove_get_device_error(int* code);
 
 /* ------------------------------------------------------------------------- */
@@ -141,6 +142,16 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
  * (Measurement hook; no counterpart in the reference.) */
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream);
 
+/* Runs the N-split's cross-rank completion wait for rank 0 of a two-rank group
+ * whose other rank never signals, with a wait limit of timeout_ns (at most 2 s;
+ * the product uses 2 s): the wait runs out, the kernel records device error 1
+ * for clove_get_device_error() and returns, and the context stays usable. words:
+ * 8 device words (8-byte aligned) of scratch, zeroed here. Exercises the failure
+ * path of a bounded cross-GPU wait on one GPU. (Test hook; no counterpart in the
+ * reference, which has no multi-GPU code.) */
+int clove_debug_peer_wait_timeout(unsigned long long* words, unsigned long long timeout_ns,
+                                  void* stream);
+
 /* Stream-K schedule the CTA-pair kernel uses for `tiles` 256 x 256 output tiles of
  * kb_total K blocks on `pairs` co-resident CTA pairs (force: 0 automatic, 1 never,
  * 2 whenever the tiles leave a partial wave). Writes {whole-K tiles, stream-K
@@ -201,6 +212,17 @@ int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
  * N % 16P == 0) that the tile kernels take (N/P > 8; INT4 also M > 8 and
  * K % 1024 == 0; INT8 no cluster split-K); other shapes still take the NCCL
  * all-gather. Operands must then be 16-byte aligned. At most 8 ranks.
+ * Ordering contract of this route, so that a C_full can be reused call after call:
+ *   - every replicated call of one context goes on one stream per rank (or on
+ *     streams ordered by events), in the same order on every rank;
+ *   - when a call returns on the stream, every rank's tiles are in this rank's
+ *     C_full: work queued on the stream afterwards may read it;
+ *   - a call stores into other ranks' C_full only after each of them has reached
+ *     that call on its own stream, i.e. after everything queued on their streams
+ *     before it (the readers of the previous result) has completed. Readers on
+ *     another stream must be joined into the call stream (an event) before the
+ *     next call is queued.
+ * No host barrier is needed between calls.
  * (Extension; no counterpart in the reference.) */
 int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes);
 /* Collective: unmaps C_full everywhere; returns once no rank maps it any more. */

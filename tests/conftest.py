@@ -14,6 +14,15 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 
+def reference_dir():
+    """The reference source tree for the tests that build against it: $CLOVE_REF_DIR,
+    else a `reference` directory beside this repository; None when absent (as on the
+    GPU hosts)."""
+    d = os.environ.get("CLOVE_REF_DIR") or os.path.join(ROOT, "..", "reference")
+    d = os.path.abspath(d)
+    return d if os.path.isdir(os.path.join(d, "src", "kernels")) else None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
 
