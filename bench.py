@@ -123,6 +123,35 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+def _bind_to_gpu_numa(torch, local: int) -> str:
+    """Restricts this process to the CPU cores NVML reports as closest to its GPU,
+    before any pinned host buffer is allocated: the pages of those buffers are then
+    placed on that NUMA node (first touch), so every rank's host<->device copies use
+    its own socket's memory instead of crossing the inter-socket link. Returns a
+    short description for the JSON line."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(local)
+        bus = getattr(props, "pci_bus_id", None)
+        dom = getattr(props, "pci_domain_id", 0)
+        dv = getattr(props, "pci_device_id", 0)
+        if bus is not None:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dv:02x}.0".encode())
+        else:
+            h = pynvml.nvmlDeviceGetHandleByIndex(local)
+        n_words = (os.cpu_count() + 63) // 64
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, n_words)
+        cpus = {w * 64 + b for w, m in enumerate(masks) for b in range(64) if (m >> b) & 1}
+        cpus &= set(os.sched_getaffinity(0))
+        if not cpus:
+            return "unbound: NVML reported no CPUs near the GPU"
+        os.sched_setaffinity(0, cpus)
+        return f"{len(cpus)} cores near the GPU (NVML CPU affinity), pinned buffers first-touched there"
+    except Exception as e:  # report, run unbound
+        return f"unbound: {str(e)[:80]}"
+
+
 # ---------------------------------------------------------------------------
 # CPU reference arm / baseline
 # ---------------------------------------------------------------------------
@@ -410,6 +439,26 @@ def _secondary(cc, torch, peaks):
         readme, note="the reference README's published ms (hardware unstated): 0.042, 0.891, "
                      "2.847, 5.234")
 
+    # Attention (the reference's flash_attention, attention.cu:93-310) at the
+    # Llama-7B prefill shape: 32 heads x 2048 tokens x head_dim 128, causal, fp16,
+    # [batch, heads, seq, 128]; against torch's scaled_dot_product_attention (a
+    # library kernel) on the same tensors, timed interleaved.
+    B, H, S, D = 1, 32, 2048, 128
+    gen.manual_seed(2048)
+    qkv = [torch.randn((B, H, S, D), device="cuda", generator=gen).half() for _ in range(3)]
+    Oa = torch.empty_like(qkv[0])
+    flop = 4.0 * D * B * H * (S * (S + 1) / 2)  # QK^T and PV over the unmasked pairs
+    t_a = timeit(lambda i: cc.flash_attention(*qkv, causal=True, O=Oa), 1, 50)
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    t_t = timeit(lambda i: sdpa(*qkv, is_causal=True), 1, 50)
+    out["attention_causal_1x32x2048x128"] = {
+        "us_per_call": round(t_a * 1e6, 2), "TFLOPS": round(flop / t_a / 1e12, 1),
+        "frac_of_bf16_peak": round(flop / t_a / 1e12 / peaks["bf16_tflops"], 4),
+        "torch_sdpa_us": round(t_t * 1e6, 2),
+        "flop_per_call": flop,
+        "note": "causal; FLOPs count the unmasked (q, k) pairs of both GEMMs"}
+    del qkv, Oa
+
     # config 1 and the square sweep (fp16, 1024-16384), int8 square sweep
     for n in (1024, 2048, 4096, 8192, 16384):
         # Timing-only operands: the config distribution N(0,1)/sqrt(K), drawn on the
@@ -572,6 +621,86 @@ def _replicated(cc, torch, dist, world, rank, wl, np):
     return out
 
 
+def _strong_scaling(cc, torch, dist, world, rank):
+    """Config 4 in the reference runtime's orientation (inference.cu:171-194:
+    activations X[T, H] times weights W[H, I]) with the weights N-split: rank r holds
+    columns [col_begin(N, P, r), col_begin(N, P, r+1)) of W_up [4096, 11008] and of
+    W_down [11008, 4096], so the per-rank weight bytes and FLOPs fall as 1/P while the
+    2048-token batch stays fixed (strong scaling). One step:
+        up    H[2048, 11008] = X[2048, 4096] . W_up      (shard, H replicated on every rank)
+        down  Y[2048, 4096]  = H . W_down                 (shard, Y stays column-sharded)
+    "replicated" stores every up tile into all ranks' H from the GEMM epilogue
+    (registered output); "shard_only" runs the same two shard GEMMs without making H
+    whole (a lower bound). Device time per step, CUDA events, max over ranks,
+    median of 3 batches of 20 steps."""
+    T, Hd, I = 2048, 4096, 11008
+    g = torch.Generator(device="cuda").manual_seed(11)  # the same operands on every rank
+    X = torch.randn((T, Hd), device="cuda", generator=g).half()
+    W_up = (torch.randn((Hd, I), device="cuda", generator=g) / Hd ** 0.5).half()
+    W_dn = (torch.randn((I, Hd), device="cuda", generator=g) / I ** 0.5).half()
+    flop = 2.0 * T * Hd * I * 2
+    out = {"workload": "X[2048,4096].W_up[4096,11008] then H[2048,11008].W_down[11008,4096], "
+                       "weights column-sharded over the ranks", "n_gpus": world,
+           "flop_per_step": flop}
+    if world == 1:
+        H = torch.empty((T, I), dtype=torch.float16, device="cuda")
+        Y = torch.empty((T, Hd), dtype=torch.float16, device="cuda")
+        fns = {"single_gpu": lambda: (cc.gemm_fp16(X, W_up, H), cc.gemm_fp16(H, W_dn, Y))}
+        ns = None
+    else:
+        ns = cc.NSplit(rank, world, tag="clove_nsplit_strong")  # a fresh id under its own key
+        u0, u1 = ns.cols(I)
+        d0, d1 = ns.cols(Hd)
+        Wu = W_up[:, u0:u1].contiguous()
+        Wd = W_dn[:, d0:d1].contiguous()
+        H = torch.empty((T, I), dtype=torch.float16, device="cuda")
+        Hs = torch.empty((T, u1 - u0), dtype=torch.float16, device="cuda")
+        Ys = torch.empty((T, d1 - d0), dtype=torch.float16, device="cuda")
+        err = ""
+        try:
+            ns.register_output(H)
+        except Exception as e:
+            err = repr(e)[:160]
+        ok = torch.tensor([0 if err else 1], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        fns = {"shard_only": lambda: (ns.gemm_fp16(X, Wu, I, C_shard=Hs),
+                                      ns.gemm_fp16(H, Wd, Hd, C_shard=Ys))}
+        if ok.item():
+            fns["replicated"] = lambda: (ns.gemm_fp16(X, Wu, I, C_shard=Hs, C_full=H,
+                                                      replicate_C=True),
+                                         ns.gemm_fp16(H, Wd, Hd, C_shard=Ys))
+        else:
+            out["replicated"] = f"unavailable: {err or 'another rank could not register'}"
+        del W_up, W_dn
+    times = {k: [] for k in fns}
+    for _ in range(3):
+        for k, fn in fns.items():
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                fn()
+            e1.record()
+            e1.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1e3 / 20], device="cuda")
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times[k].append(t.item())
+    out["us_per_step"] = {k: round(statistics.median(v), 2) for k, v in times.items()}
+    out["TFLOPS"] = {k: round(flop / v * 1e-6, 1) for k, v in out["us_per_step"].items()}
+    if ns is not None:
+        if "replicated" in fns:
+            torch.cuda.synchronize()
+            dist.barrier()
+            ns.unregister_output(H)
+        ns.close()
+    return out
+
+
 def run_case(args):
     """Profiling mode (--case): a few plain launches of one secondary configuration,
     no graphs, no output; the command line ncu captures."""
@@ -592,6 +721,10 @@ def run_case(args):
         op = wl.int4_operands(4096, 4096, 4096, seed=0)
         t = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
         fn = lambda: cc.gemm_int4(*t)
+    elif args.case == "attention":
+        g = torch.Generator(device="cuda").manual_seed(2048)
+        t = [torch.randn((1, 32, 2048, 128), device="cuda", generator=g).half() for _ in range(3)]
+        fn = lambda: cc.flash_attention(*t, causal=True)
     elif args.case == "fp16_1024":
         A, B = wl.fp16_operands(1024, 1024, 1024, seed=0)
         t = [dev(A), dev(B)]
@@ -603,6 +736,46 @@ def run_case(args):
     torch.cuda.synchronize()
 
 
+def _summary(line):
+    """The figures that matter, compact, at the end of the JSON line."""
+    sec = line.get("secondary", {})
+    out = {"ffn_tflops": line["value"], "ffn_frac": line["roofline"]["frac"],
+           "e2e_tflops": line["e2e"]["value"]}
+    d = sec.get("int4_decode_4096x1x4096")
+    if d:
+        out["decode_int4_4096"] = {"us": d["us_per_call"], "GBps": d["GBps"],
+                                   "frac": d["roofline"]["frac"],
+                                   "over_floor": d["read_floor"]["decode_over_floor"],
+                                   "prefetch_us": d["weight_prefetch"]["us_per_call"],
+                                   "prefetch_frac": d["weight_prefetch"]["frac"]}
+    gq = sec.get("int4_decode_qkv_3x4096x4096")
+    if gq:
+        out["decode_int4_qkv"] = {"us": gq["us_per_call"], "GBps": gq["GBps"],
+                                  "frac": gq["roofline"]["frac"]}
+    b = sec.get("int8_batch32_4096x32x4096")
+    if b:
+        out["int8_batch32"] = {"us": b["us_per_call"], "GBps": b["GBps"],
+                               "frac": b["roofline"]["frac"]}
+    for n in (4096, 8192):
+        q = sec.get(f"int4_square_{n}")
+        if q:
+            out[f"int4_{n}_TOPS"] = q["TOPS"]
+    at = sec.get("attention_causal_1x32x2048x128")
+    if at:
+        out["attention_causal"] = {"us": at["us_per_call"], "TFLOPS": at["TFLOPS"],
+                                   "torch_sdpa_us": at["torch_sdpa_us"]}
+    f1 = sec.get("fp16_square_1024")
+    if f1:
+        out["fp16_1024_us"] = f1["us_per_call"]
+    fc = sec.get("ffn_vs_cublas_us")
+    if fc:
+        out["ffn_vs_cublas_us"] = {k: [fc[k]["clove"], fc[k]["cublas"]] for k in ("up", "down")}
+    st = line.get("strong_scaling")
+    if st:
+        out["strong_us_per_step"] = st["us_per_step"]
+    return out
+
+
 def run_gpu(args):
     import numpy as np
     import torch
@@ -612,6 +785,7 @@ def run_gpu(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    numa = _bind_to_gpu_numa(torch, local)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
@@ -769,7 +943,8 @@ def run_gpu(args):
                     "h2d_bytes_per_step": X_pin[0].numel() * 2,
                     "d2h_bytes_per_step": out_pin[0].numel() * 2,
                     "ms_per_step": round(t_e2e / args.steps * 1e3, 4),
-                    "overlap": "upload, GEMMs and download on three streams, double-buffered"},
+                    "overlap": "upload, GEMMs and download on three streams, double-buffered",
+                    "host_binding": numa},
             "gpu_launches": 2 * args.steps,
             "clocks": clk.summary(),
             "spot_check_rel_err_vs_torch_fp32": round(spot, 6),
@@ -780,9 +955,14 @@ def run_gpu(args):
         rep = _replicated(cc, torch, dist, world, rank, wl, np)  # collective: every rank
         if rank == 0:
             line["replicated_output"] = rep
+    if not args.no_secondary:
+        strong = _strong_scaling(cc, torch, dist, world, rank)  # collective at N > 1
+        if rank == 0:
+            line["strong_scaling"] = strong
     if world == 1 and rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = _cpu_ffn_sample(args.cpu_frac, min_seconds=10.0, max_reps=400)
     if rank == 0:
+        line["summary"] = _summary(line)  # last key: survives a record that keeps the tail
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -797,7 +977,8 @@ def main():
     ap.add_argument("--impl", choices=["clove", "reference"], default="clove")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096"],
+    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096",
+                                       "attention"],
                     help="profiling mode: warm-up + steps plain launches of one secondary config")
     ap.add_argument("--kernel-only", action="store_true",
                     help="run only the warm-up and timed FFN GEMMs (for ncu), print nothing")

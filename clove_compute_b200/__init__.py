@@ -23,7 +23,7 @@ __all__ = [
     "gemm_fp16", "gemm_fp16_batched", "gemm_int8", "gemm_int8_rowcol", "gemm_int4",
     "debug_int8_acc", "debug_int4_group_acc", "debug_stream_read", "debug_stream_k_plan",
     "debug_peer_wait_timeout", "quantize_int4",
-    "swiglu_fused",
+    "swiglu_fused", "flash_attention",
     "set_dispatch_override",
     "set_weight_prefetch",
     "describe_dispatch",

@@ -34,6 +34,7 @@ SIGNATURES = {
     "clove_gemm_int8_noalloc": ([_P, _P, _P, _I, _I, _I, _F, _I8, _F, _I8, _P], _I),
     "clove_gemm_int8_rowcol": ([_P, _P, _P, _I, _I, _I, _P, _P, _P], _I),
     "clove_gemm_int4": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "clove_flash_attention": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _I, _P], _I),
     "clove_debug_int8_acc": ([_P, _P, _P, _I, _I, _I, _I8, _I8, _P], _I),
     "clove_debug_int4_group_acc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
     "clove_quantize_int4": ([_P, _I, _I, _P, _P, _P, _P], _I),

@@ -195,6 +195,39 @@ def swiglu_fused(X: torch.Tensor, W_gate: torch.Tensor, W_up: torch.Tensor,
     return out
 
 
+def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = True,
+                    scale: float | None = None, layout: str = "bhsd", O: torch.Tensor | None = None,
+                    stream=None) -> torch.Tensor:
+    """O = softmax(scale * Q K^T [causal]) V on the tensor cores (attention.cuh:44-56).
+
+    layout "bhsd": Q, K, V [batch, heads, seq, 128] (the reference's flash_attention);
+    "bshd": [batch, seq, heads, 128] (its runtime's projection outputs). K and V may
+    have fewer heads than Q (grouped-query attention). scale defaults to 1/sqrt(128)."""
+    for t, n in ((Q, "Q"), (K, "K"), (V, "V")):
+        _need(t, n, torch.float16, 4)
+    if layout not in ("bhsd", "bshd"):
+        raise ValueError("layout must be 'bhsd' or 'bshd'")
+    if layout == "bhsd":
+        B, H, S, D = Q.shape
+        Hkv = K.shape[1]
+        kv_shape = (B, Hkv, S, D)
+    else:
+        B, S, H, D = Q.shape
+        Hkv = K.shape[2]
+        kv_shape = (B, S, Hkv, D)
+    if tuple(K.shape) != kv_shape or tuple(V.shape) != kv_shape:
+        raise ValueError(f"K and V must be {kv_shape}")
+    if O is None:
+        O = torch.empty_like(Q)
+    _need(O, "O", torch.float16, 4)
+    if scale is None:
+        scale = 1.0 / D ** 0.5
+    check(lib().clove_flash_attention(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), B, H, Hkv, S, D,
+                                      float(scale), int(bool(causal)),
+                                      0 if layout == "bhsd" else 1, _stream(stream)))
+    return O
+
+
 def quantize_int4(W: torch.Tensor, stream=None):
     """Pack fp16 weights W [rows, K] (K % 128 == 0) into the INT4 layout gemm_int4
     reads: (codes [rows, K/2] uint8, scales [rows, K/128] fp16, zeros [rows, K/128] fp16).

@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -173,8 +174,8 @@ int clove_get_device_error(int* code) {
   int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   if (rc) return rc;
   int v = 0;
-  const int readers[4] = {read_clear_error_tc(), read_clear_error_gemv(), read_clear_error_simt(),
-                          read_clear_error_int4()};
+  const int readers[5] = {read_clear_error_tc(), read_clear_error_gemv(), read_clear_error_simt(),
+                          read_clear_error_int4(), read_clear_error_attn()};
   for (int r : readers) {
     if (r < 0) return fail(CLOVE_ERR_CUDA, "reading the device error word failed");
     if (v == 0 && r != 0) v = r;
@@ -590,6 +591,36 @@ int clove_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* sc
   int rc = current_device(&dev);
   if (rc) return rc;
   return launch_quantize_int4(W, rows, K, codes, scales, zeros, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Attention
+// ---------------------------------------------------------------------------
+int clove_flash_attention(const void* Q, const void* K, const void* V, void* O, int batch,
+                          int num_heads, int num_kv_heads, int seq_len, int head_dim, float scale,
+                          int causal, int layout, void* stream) {
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr)
+    return fail(CLOVE_ERR_INVALID_ARG, "null tensor pointer");
+  if (batch <= 0 || num_heads <= 0 || num_kv_heads <= 0 || seq_len <= 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "batch, heads and seq_len must be positive");
+  if (num_heads % num_kv_heads != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "num_heads (%d) is not a multiple of num_kv_heads (%d)",
+                num_heads, num_kv_heads);
+  if (layout != 0 && layout != 1) return fail(CLOVE_ERR_INVALID_ARG, "layout must be 0 or 1");
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(CLOVE_ERR_INVALID_ARG, "scale must be positive and finite");
+  if (head_dim != 128)
+    return fail(CLOVE_ERR_UNSUPPORTED, "head_dim %d: only 128 is supported (as the reference)",
+                head_dim);
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
+    return fail(CLOVE_ERR_UNSUPPORTED, "attention needs 16-byte aligned tensors");
+  if (num_heads > 65535 || batch > 65535)
+    return fail(CLOVE_ERR_UNSUPPORTED, "at most 65535 heads and batches");
+  DeviceInfo dev;
+  const int rc = current_device(&dev);
+  if (rc) return rc;
+  return launch_attention(Q, K, V, O, batch, num_heads, num_kv_heads, seq_len, scale, causal != 0,
+                          layout, dev, as_stream(stream));
 }
 
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream) {

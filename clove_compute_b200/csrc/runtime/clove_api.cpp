@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstdlib>
 
+#include "clove/kernels/attention_tc.cuh"
 #include "clove/kernels/gemm.cuh"
 
 namespace clove {
@@ -54,6 +55,22 @@ void swiglu_fused(const half* input, const half* W_gate, const half* W_up, half*
   die_on_error(clove_swiglu_fused(input, W_gate, W_up, output, batch_seq, hidden_dim,
                                   intermediate_dim, stream),
                "swiglu_fused");
+}
+
+void flash_attention_tc(const half* Q, const half* K, const half* V, half* O, int batch,
+                        int num_heads, int seq_len, int head_dim, float scale, bool causal,
+                        cudaStream_t stream) {
+  die_on_error(clove_flash_attention(Q, K, V, O, batch, num_heads, num_heads, seq_len, head_dim,
+                                     scale, causal ? 1 : 0, 0, stream),
+               "flash_attention_tc");
+}
+
+void flash_attention_tc_bshd(const half* Q, const half* K, const half* V, half* O, int batch,
+                             int num_heads, int num_kv_heads, int seq_len, int head_dim,
+                             float scale, bool causal, cudaStream_t stream) {
+  die_on_error(clove_flash_attention(Q, K, V, O, batch, num_heads, num_kv_heads, seq_len,
+                                     head_dim, scale, causal ? 1 : 0, 1, stream),
+               "flash_attention_tc_bshd");
 }
 
 }  // namespace clove

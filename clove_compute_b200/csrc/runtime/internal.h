@@ -128,6 +128,14 @@ int launch_stream_read(const void* src, size_t nbytes, uint32_t* out, const Devi
 // out = silu(g) * u over n fp16 elements (kernels/fallback_simt.cu).
 int launch_swiglu_f16(const void* g, const void* u, void* out, long long n, cudaStream_t stream);
 
+// ---- attention (kernels/attention_sm100.cu)
+// head_dim 128; layout 0: [batch, heads, seq, 128], 1: [batch, seq, heads, 128];
+// K / V have kv_heads heads (heads % kv_heads == 0).
+int launch_attention(const void* Q, const void* K, const void* V, void* O, int batch, int heads,
+                     int kv_heads, int seq, float scale, bool causal, int layout,
+                     const DeviceInfo& dev, cudaStream_t stream);
+int read_clear_error_attn();
+
 // ---- INT4 packing tool (kernels/quant_int4.cu)
 int launch_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,
                          cudaStream_t stream);

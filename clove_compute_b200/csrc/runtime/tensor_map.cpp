@@ -48,10 +48,10 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, con
     case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
     default: return fail(CLOVE_ERR_INVALID_ARG, "bad swizzle width %d", swizzle_bytes);
   }
-  cuuint64_t dims[3];
-  cuuint64_t strides[2];
-  const cuuint32_t box[3] = {box_inner, box_outer, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  const cuuint32_t box[4] = {box_inner, box_outer, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) dims[i] = static_cast<cuuint64_t>(dims_in[i]);
   for (int i = 0; i + 1 < rank; ++i) strides[i] = static_cast<cuuint64_t>(strides_in[i]);
   const CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
@@ -85,6 +85,13 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
   const uint64_t dims[3] = {inner, outer, depth};
   const uint64_t strides[2] = {row_stride_bytes, plane_stride_bytes};
   return encode_tmap(map, dtype, elem_bytes, base, 3, dims, strides, box_inner, box_outer,
+                     swizzle_bytes);
+}
+
+int encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   const uint64_t dims[4], const uint64_t strides_bytes[3], uint32_t box_inner,
+                   uint32_t box_outer, int swizzle_bytes) {
+  return encode_tmap(map, dtype, elem_bytes, base, 4, dims, strides_bytes, box_inner, box_outer,
                      swizzle_bytes);
 }
 

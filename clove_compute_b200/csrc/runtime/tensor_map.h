@@ -24,5 +24,13 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, 
                    uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                    int swizzle_bytes);
 
+// A 4D tensor [d3, d2, d1, d0] (d0 contiguous) with arbitrary byte strides of the
+// three outer dimensions, for a box [1, 1, box_outer, box_inner]: e.g. attention
+// operands [batch, heads, seq, head_dim] or [batch, seq, heads, head_dim] viewed as
+// (head_dim, seq, heads, batch) with the matching strides.
+int encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                   const uint64_t dims[4], const uint64_t strides_bytes[3], uint32_t box_inner,
+                   uint32_t box_outer, int swizzle_bytes);
+
 }  // namespace rt
 }  // namespace clove

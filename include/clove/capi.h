@@ -16,6 +16,7 @@
  *   clove_gemm_int8_rowcol (extension: per-row / per-column scales of gemm.cuh:55's formula)
  *   clove_gemm_int4        clove::gemm_int4          gemm.cuh:77-87, gemm_int4.cu:195-216
  *   clove_gemm_fp16_batched clove::gemm_fp16_batched gemm.cuh:93-101, gemm_fp16.cu:366-383
+ *   clove_flash_attention  clove::flash_attention    attention.cuh:44-56, attention.cu:93-310
  *   clove_debug_*          (test hooks: raw int32 accumulators for bit-exact checks)
  *   clove_nsplit_*         (extension: N-split over the GPUs of one node, NCCL all-gather)
  */
@@ -124,6 +125,23 @@ int clove_gemm_int4(const uint8_t* A_q, const void* A_scale, const void* A_zero,
  * code = clamp(rint(w/scale)+zero,0,15). K % 128 == 0; W 8-byte aligned. */
 int clove_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,
                         void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Attention: O = softmax(scale * Q.K^T [causal mask]) . V on the tensor cores  */
+/* (replaces clove::flash_attention, include/clove/kernels/attention.cuh:44-56, */
+/* src/kernels/attention.cu:93-266 and 273-310, whose S = Q.K^T and P.V are     */
+/* CUDA-core loops at attention.cu:185-204).                                    */
+/* Q, O: num_heads heads; K, V: num_kv_heads heads (num_heads a multiple; head  */
+/* h reads kv head h / (num_heads / num_kv_heads), grouped-query attention).   */
+/* layout 0: [batch, heads, seq_len, head_dim] (the reference's flash_attention); */
+/* layout 1: [batch, seq_len, heads, head_dim] (the runtime's q/k/v projection  */
+/* outputs, the layout of its flash_attention_rope). head_dim must be 128 (as   */
+/* the reference); causal masks keys after the query; fp16 in and out, fp32     */
+/* accumulation and softmax. 16-byte aligned tensors; scale > 0.                */
+/* ------------------------------------------------------------------------- */
+int clove_flash_attention(const void* Q, const void* K, const void* V, void* O, int batch,
+                          int num_heads, int num_kv_heads, int seq_len, int head_dim, float scale,
+                          int causal, int layout, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* Test hooks: exact int32 accumulators through the same kernels.              */

@@ -50,6 +50,7 @@ _SIGS = {
     "clove_oracle_gemm_int4_refcompat": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
     "clove_oracle_quantize_int4": ([_P, _I, _I, _P, _P, _P], None),
     "clove_oracle_swiglu": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I], None),
+    "clove_oracle_attention": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _I, _I, _I], None),
 }
 
 
@@ -242,3 +243,29 @@ def swiglu(X, Wg, Wu, rows=None, nthreads=0):
                               _ptr(Wu.view(np.uint16)), _ptr(out.view(np.uint16)), M, N, K, r0, r1,
                               nthreads)
     return out
+
+
+def attention(Q, K, V, causal=True, scale=None, layout="bhsd", refcompat=False, nthreads=0):
+    """O = softmax(scale * Q K^T [causal]) V in fp32, fp16 out: the reference's
+    flash_attention_kernel (attention.cu:93-266) restated, 64-key blocks with its
+    online softmax. layout "bhsd" [batch, heads, seq, D] or "bshd" [batch, seq,
+    heads, D]; K/V may have fewer heads (head h reads kv head h // (H // Hkv)).
+    refcompat=True keeps the reference's phantom zero-score keys that pad a ragged
+    last block in non-causal attention."""
+    Q = np.ascontiguousarray(Q, np.float16)
+    K = np.ascontiguousarray(K, np.float16)
+    V = np.ascontiguousarray(V, np.float16)
+    if layout == "bhsd":
+        B, H, S, D = Q.shape
+        Hkv = K.shape[1]
+    else:
+        B, S, H, D = Q.shape
+        Hkv = K.shape[2]
+    assert K.shape == V.shape and H % Hkv == 0
+    if scale is None:
+        scale = 1.0 / D ** 0.5
+    O = np.zeros_like(Q)
+    lib().clove_oracle_attention(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), B, H, Hkv, S, D,
+                                 float(scale), int(bool(causal)), 0 if layout == "bhsd" else 1,
+                                 int(bool(refcompat)), nthreads)
+    return O

@@ -473,3 +473,81 @@ void clove_oracle_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* 
     free(Wgf);
     free(Wuf);
 }
+
+/* ------------------------------------------------------------------------- */
+/* Attention (reference src/kernels/attention.cu:93-266)                      */
+/* ------------------------------------------------------------------------- */
+static inline int64_t attn_index(int layout, int heads, int seq, int D, int b, int h, int s) {
+    if (layout == 0) return (((int64_t)b * heads + h) * seq + s) * D;
+    return (((int64_t)b * seq + s) * heads + h) * D;
+}
+
+void clove_oracle_attention(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+                            int batch, int heads, int kv_heads, int seq, int D, float scale,
+                            int causal, int layout, int refcompat, int nthreads) {
+    const int group = heads / kv_heads;
+    const int64_t rows = (int64_t)batch * heads * seq;
+    const int BC = 64; /* key block of the reference kernel (FA_BC) */
+#pragma omp parallel num_threads(resolve_threads(nthreads))
+    {
+        float* q = (float*)malloc(sizeof(float) * D);
+        float* acc = (float*)malloc(sizeof(float) * D);
+        float* sblk = (float*)malloc(sizeof(float) * BC);
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t r = 0; r < rows; r++) {
+            const int s_q = (int)(r % seq);
+            const int h = (int)((r / seq) % heads);
+            const int b = (int)(r / ((int64_t)seq * heads));
+            const int hk = h / group;
+            const uint16_t* qrow = Q + attn_index(layout, heads, seq, D, b, h, s_q);
+            for (int d = 0; d < D; d++) q[d] = clove_oracle_h2f(qrow[d]);
+            for (int d = 0; d < D; d++) acc[d] = 0.f;
+            float row_max = -3.402823466e38f, row_sum = 0.f;
+            /* Keys the reference visits: up to the end of the query's 64-row block
+             * for causal attention (all later ones masked), all blocks otherwise. */
+            const int q_start = s_q / 64 * 64;
+            const int k_end = causal ? (seq < q_start + 64 ? seq : q_start + 64) : seq;
+            for (int k0 = 0; k0 < k_end; k0 += BC) {
+                float bmax = -3.402823466e38f;
+                for (int j = 0; j < BC; j++) {
+                    const int key = k0 + j;
+                    float sc;
+                    if (key < seq) {
+                        const uint16_t* krow = K + attn_index(layout, kv_heads, seq, D, b, hk, key);
+                        float sum = 0.f;
+                        for (int d = 0; d < D; d++) sum += q[d] * clove_oracle_h2f(krow[d]);
+                        sc = sum * scale;
+                    } else {
+                        sc = 0.f; /* zero-filled key row */
+                    }
+                    if (causal && s_q < key) sc = -3.402823466e38f;
+                    else if (!causal && key >= seq && !refcompat) sc = -INFINITY; /* absent key */
+                    sblk[j] = sc;
+                    if (sc > bmax) bmax = sc;
+                }
+                const float new_max = fmaxf(row_max, bmax);
+                const float scale_old = expf(row_max - new_max);
+                row_sum *= scale_old;
+                for (int d = 0; d < D; d++) acc[d] *= scale_old;
+                float bsum = 0.f;
+                for (int j = 0; j < BC; j++) {
+                    const int key = k0 + j;
+                    const float p = expf(sblk[j] - new_max);
+                    bsum += p;
+                    if (key < seq && p != 0.f) {
+                        const uint16_t* vrow = V + attn_index(layout, kv_heads, seq, D, b, hk, key);
+                        for (int d = 0; d < D; d++) acc[d] += p * clove_oracle_h2f(vrow[d]);
+                    }
+                }
+                row_sum += bsum;
+                row_max = new_max;
+            }
+            uint16_t* orow = O + attn_index(layout, heads, seq, D, b, h, s_q);
+            const float inv = 1.0f / row_sum;
+            for (int d = 0; d < D; d++) orow[d] = clove_oracle_f2h(acc[d] * inv);
+        }
+        free(q);
+        free(acc);
+        free(sblk);
+    }
+}

@@ -115,6 +115,21 @@ void clove_oracle_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* 
 void clove_oracle_quantize_int4(const uint16_t* W, int rows, int K, uint8_t* codes,
                                 uint16_t* scales, uint16_t* zeros);
 
+/* Attention, the reference's flash_attention_kernel (src/kernels/attention.cu:93-266)
+ * restated: per query row, keys in blocks of 64; S = scale * sum_d q_d k_d (fp32,
+ * d ascending); causal keys after the query set to -FLT_MAX; online softmax with
+ * expf (running max, rescale of the row sum and the fp32 output row by
+ * expf(old_max - new_max)); O = half(acc / sum). head_dim D; K/V heads
+ * kv_heads (head h reads kv head h / (heads / kv_heads)).
+ * layout 0: [batch, heads, seq, D]; 1: [batch, seq, heads, D].
+ * refcompat 1 reproduces the reference's non-causal handling of a ragged last
+ * block: the keys padding seq up to a multiple of 64 are loaded as zeros and
+ * NOT masked, so each adds expf(0 - max) to the row sum (a phantom key with
+ * score 0 and value 0). refcompat 0 is ordinary attention over the seq keys. */
+void clove_oracle_attention(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+                            int batch, int heads, int kv_heads, int seq, int D, float scale,
+                            int causal, int layout, int refcompat, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -332,3 +332,88 @@ def test_swiglu_matches_float64(oracle_mod):
     part = oracle_mod.swiglu(X, Wg, Wu, rows=(2, 5))
     np.testing.assert_array_equal(part[2:5], oracle_mod.swiglu(X, Wg, Wu)[2:5])
     assert not part[:2].any() and not part[5:].any()
+
+
+# ---------------------------------------------------------------------------
+# Attention: the C restatement of the reference's flash_attention_kernel against a
+# float64 numpy statement of attention, and (when present) the reference kernel's
+# own outputs recorded on a B200.
+# ---------------------------------------------------------------------------
+def _np_attention(Q, K, V, causal, scale, layout="bhsd", phantom=0):
+    if layout == "bshd":
+        Q, K, V = (x.transpose(0, 2, 1, 3) for x in (Q, K, V))
+    q, k, v = (x.astype(np.float64) for x in (Q, K, V))
+    H, Hkv, S = q.shape[1], k.shape[1], q.shape[2]
+    k = np.repeat(k, H // Hkv, axis=1)
+    v = np.repeat(v, H // Hkv, axis=1)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    if causal:
+        s[..., np.triu(np.ones((S, S), bool), 1)] = -np.inf
+    mx = s.max(-1, keepdims=True)
+    p = np.exp(s - mx)
+    den = p.sum(-1, keepdims=True) + phantom * np.exp(-mx)  # phantom keys: score 0, value 0
+    o = np.einsum("bhqk,bhkd->bhqd", p, v) / den
+    return o.transpose(0, 2, 1, 3) if layout == "bshd" else o
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,causal,layout", [
+    (1, 2, 2, 64, True, "bhsd"), (1, 1, 1, 150, True, "bhsd"), (2, 2, 2, 128, False, "bhsd"),
+    (1, 4, 2, 90, True, "bshd"), (1, 3, 1, 70, False, "bshd")])
+def test_attention_vs_float64(oracle_mod, B, H, Hkv, S, causal, layout):
+    rng = np.random.default_rng(S + H)
+    shp = (lambda h: (B, h, S, 128)) if layout == "bhsd" else (lambda h: (B, S, h, 128))
+    Q = rng.standard_normal(shp(H)).astype(np.float16)
+    K = rng.standard_normal(shp(Hkv)).astype(np.float16)
+    V = rng.standard_normal(shp(Hkv)).astype(np.float16)
+    scale = 1 / np.sqrt(128)
+    O = oracle_mod.attention(Q, K, V, causal=causal, scale=scale, layout=layout)
+    ref = _np_attention(Q, K, V, causal, scale, layout)
+    assert oracle_mod.rel_frobenius(O, ref) < 1e-3
+
+
+def test_attention_refcompat_phantom_keys(oracle_mod):
+    """Non-causal with a ragged last key block: the reference counts the zero keys that
+    pad seq to a multiple of 64 in the row sum (score 0, value 0)."""
+    rng = np.random.default_rng(3)
+    S = 100
+    Q, K, V = (rng.standard_normal((1, 1, S, 128)).astype(np.float16) for _ in range(3))
+    scale = 1 / np.sqrt(128)
+    O = oracle_mod.attention(Q, K, V, causal=False, scale=scale, refcompat=True)
+    assert oracle_mod.rel_frobenius(O, _np_attention(Q, K, V, False, scale, phantom=28)) < 1e-3
+    # Causal attention masks the padding: refcompat changes nothing there.
+    a = oracle_mod.attention(Q, K, V, causal=True, scale=scale, refcompat=True)
+    b = oracle_mod.attention(Q, K, V, causal=True, scale=scale)
+    assert np.array_equal(a, b)
+
+
+def test_attention_known_answers(oracle_mod):
+    """Identical keys give uniform weights (O = mean of the visible values); one
+    dominant key gives O = its value."""
+    S = 64
+    Q = np.ones((1, 1, S, 128), np.float16)
+    K = np.ones((1, 1, S, 128), np.float16)
+    V = np.tile(np.arange(S, dtype=np.float16)[:, None], (1, 128))[None, None]
+    O = oracle_mod.attention(Q, K, V, causal=True, scale=0.01)
+    want = np.array([np.arange(q + 1).mean() for q in range(S)], np.float64)
+    assert np.allclose(O[0, 0, :, 0].astype(np.float64), want, rtol=2e-3)
+    K2 = np.zeros_like(K)
+    K2[0, 0, 17] = 4.0
+    O2 = oracle_mod.attention(Q, K2, V, causal=False, scale=1.0)
+    assert np.allclose(O2[0, 0, :, 5].astype(np.float64), 17.0, rtol=1e-3)
+
+
+@pytest.mark.parametrize("fname", _golden_files("ref_attn_") or ["<none>"])
+def test_oracle_vs_reference_attention_golden(oracle_mod, fname):
+    """Outputs of the reference flash_attention kernel (run on a B200). The oracle
+    follows its steps (64-key blocks, expf online softmax); the GPU's expf and
+    summation order differ from the host's in the last bits only."""
+    if fname == "<none>":
+        pytest.skip("no reference attention golden vectors generated yet")
+    d = np.load(os.path.join(GOLDEN, fname))
+    causal = bool(d["causal"])
+    O = oracle_mod.attention(d["Q"], d["K"], d["V"], causal=causal, scale=float(d["scale"]),
+                             refcompat=True)
+    ref = d["O_ref"]
+    assert oracle_mod.rel_frobenius(O, ref) < 2e-3
+    diff = np.abs(O.astype(np.float32) - ref.astype(np.float32))
+    assert diff.max() <= 2e-3 * max(1.0, float(np.abs(ref.astype(np.float32)).max()))
