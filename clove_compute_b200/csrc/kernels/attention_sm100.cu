@@ -66,9 +66,10 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, int b
   cudaLaunchAttribute la[1];
   la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   la[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>((seq + S::BQ - 1) / S::BQ),
+  const int n_qt = (seq + S::BQ - 1) / S::BQ;
+  cfg.gridDim = dim3(static_cast<unsigned>((n_qt + S::TILES - 1) / S::TILES),
                      static_cast<unsigned>(heads), static_cast<unsigned>(batch));
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(S::THREADS, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(S::SMEM_BYTES);
   cfg.stream = stream;
   cfg.attrs = la;
