@@ -325,6 +325,37 @@ def _secondary(cc, torch, peaks):
             "note": "clove_debug_stream_read of the same byte count, one launch per call: the "
                     "bandwidth a single kernel of this size reaches, without any math"}}
 
+    # Grouped decode: Q, K and V projection weights of one layer concatenated by rows
+    # (W_qkv [3 * 4096, 4096]) and streamed by one gemm_int4 call,
+    # N = 1; same distributions as config 2.
+    M3 = 3 * 4096
+    op3 = wl.int4_operands(M3, 1, K, seed=3)
+    copies3 = 16
+    Aq3 = [dev(op3.A_q) for _ in range(copies3)]
+    As3 = [dev(op3.A_scale) for _ in range(copies3)]
+    Az3 = [dev(op3.A_zero) for _ in range(copies3)]
+    Bq3, Bs3, Bz3 = dev(op3.B_q), dev(op3.B_scale), dev(op3.B_zero)
+    C3 = torch.empty((M3, 1), dtype=torch.float16, device="cuda")
+    t3 = timeit(lambda i: cc.gemm_int4(Aq3[i], As3[i], Az3[i], Bq3, Bs3, Bz3, C3), copies3, 200)
+    cc.set_weight_prefetch(True)
+    t3_pf = timeit(lambda i: cc.gemm_int4(Aq3[i], As3[i], Az3[i], Bq3, Bs3, Bz3, C3), copies3, 200)
+    cc.set_weight_prefetch(False)
+    nb3 = M3 * K // 2 + 2 * 2 * M3 * K // 128 + K // 2 + 2 * 2 * K // 128 + 2 * M3
+    del Aq3, As3, Az3
+    t3_floor = read_floor(nb3, copies3)
+    out["int4_decode_qkv_3x4096x4096"] = {
+        "kernel": cc.describe_dispatch("int4", M3, 1, K), "us_per_call": round(t3 * 1e6, 3),
+        "GBps": round(nb3 / t3 / 1e9, 1), "bytes_per_call": nb3,
+        "roofline": {"bound": "hbm", "achieved": round(nb3 / t3 / 1e9, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(nb3 / t3 / 1e9 / peaks["hbm_gbs"], 4)},
+        "weight_prefetch": {"us_per_call": round(t3_pf * 1e6, 3),
+                            "GBps": round(nb3 / t3_pf / 1e9, 1),
+                            "frac": round(nb3 / t3_pf / 1e9 / peaks["hbm_gbs"], 4)},
+        "read_floor": {"us_per_call": round(t3_floor * 1e6, 3),
+                       "decode_over_floor": round(t3 / t3_floor, 3)},
+        "note": "W_q, W_k, W_v [4096, 4096] concatenated by rows: one launch, M = 12288, N = 1"}
+
     # config 3: int8 batch-32 with per-row / per-column scales
     M, N, K = 4096, 32, 4096
     A8, B8, sA, sB = wl.int8_operands(M, N, K, seed=0)
@@ -751,7 +782,8 @@ def _summary(line):
     gq = sec.get("int4_decode_qkv_3x4096x4096")
     if gq:
         out["decode_int4_qkv"] = {"us": gq["us_per_call"], "GBps": gq["GBps"],
-                                  "frac": gq["roofline"]["frac"]}
+                                  "frac": gq["roofline"]["frac"],
+                                  "prefetch_frac": gq["weight_prefetch"]["frac"]}
     b = sec.get("int8_batch32_4096x32x4096")
     if b:
         out["int8_batch32"] = {"us": b["us_per_call"], "GBps": b["GBps"],

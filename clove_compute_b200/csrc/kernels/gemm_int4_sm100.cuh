@@ -10,7 +10,9 @@
 // 64 packed bytes) at a time. 18 warps:
 //   warp 0      TMA producer: packed A / B boxes [128 rows x 64 B] (64B swizzle)
 //               into a 4-deep ring; every 8 groups, boxes [128 rows x 8 groups] of
-//               A/B scales and zero points into a 2-slot ring.
+//               A/B scales and zero points into a 2-slot ring (when K % 1024 == 0
+//               and those arrays are 16-byte aligned; otherwise each transform
+//               thread loads its own row's scale and zero point, one group ahead).
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
 //               group into one of four int32 TMEM buffers (a fresh accumulator per
 //               group), so every G leaves the tensor core exact.
@@ -23,8 +25,8 @@
 //               unchanged. Per row they also sum the codes: with R = sum(a - zA),
 //               Cc = sum(b - zB),
 //                 G = D - 16 R - 16 Cc - 32768,   D = sum a'' b''  (u8 x u8 MMA).
-//               They publish, per group, the B scales (fp32), 16 Cc per column and
-//               0x4B400000 - 16 R - 32768 per row.
+//               They publish, per group, the B scales (fp32), 16 Cc per column,
+//               0x4B400000 - 16 R - 32768 per row and the A scales (fp32).
 //   warps 10-17 epilogue: two warps per TMEM lane quarter, 64 columns each, read
 //               16 columns at a time. One 3-input integer add turns D into the fp32
 //               bit pattern of 12582912 + G (exact: |G| < 2^22), one subtraction
@@ -55,7 +57,8 @@ struct I4Shape {
   static constexpr int META_BOX = 128 * 16;           // 128 rows x 8 groups x fp16
   static constexpr int META_BYTES = 4 * META_BOX;     // A scale, A zero, B scale, B zero
   static constexpr int META_SLOTS = 2;
-  static constexpr int SBF_BYTES = SB_SLOTS * 3 * BN * 4;  // per slot: B scales, col/row terms
+  // Per slot (one group): B scales, 16 x column code sums, row terms, A scales.
+  static constexpr int SBF_BYTES = SB_SLOTS * 4 * BN * 4;
   static constexpr int EPI_BYTES = 8 * 4096;          // 8 warps x 32 rows x 128 B
   static constexpr int THREADS = 18 * 32;
   static constexpr int TMEM_COLS = ACC_BUFS * BN;
@@ -79,8 +82,21 @@ struct I4Shape {
 constexpr uint32_t kI4Idesc = dev::make_idesc(2, 0, 0, 0, 0, I4Shape::BN, I4Shape::BM);
 constexpr int32_t kF32Magic = 0x4B400000;  // bit pattern of 12582912.0f = 1.5 * 2^23
 
+// Scales and zero points per row and group, read directly (the TMETA = false
+// variant): Xs / Xz [rows, NG] binary16.
+struct I4Meta {
+  const __half* As;
+  const __half* Az;
+  const __half* Bs;
+  const __half* Bz;
+};
+
 // DBG instantiation writes every exact group accumulator to Gdbg [M,N,K/128].
-template <bool DBG>
+// TMETA: scales and zero points arrive by TMA in boxes of 8 groups (row pitch
+// K/128 * 2 bytes a multiple of 16, i.e. K % 1024 == 0); otherwise each transform
+// thread loads its row's scale and zero point of the next group itself (one group
+// ahead), which serves any K % 128 == 0.
+template <bool DBG, bool TMETA>
 __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     gemm_int4_tc_kernel(const __grid_constant__ CUtensorMap tmAq,
                         const __grid_constant__ CUtensorMap tmBq,
@@ -89,7 +105,8 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
                         const __grid_constant__ CUtensorMap tmBs,
                         const __grid_constant__ CUtensorMap tmBz,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
-                        int32_t* __restrict__ Gdbg, const __grid_constant__ PeerOut peer) {
+                        int32_t* __restrict__ Gdbg, const __grid_constant__ PeerOut peer,
+                        I4Meta meta) {
   using S = I4Shape;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = dev::align_smem_1024(smem_raw);
@@ -133,7 +150,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       dev::mbar_init(&meta_full[i], 1);
-      dev::mbar_init(&meta_empty[i], 16);
+      dev::mbar_init(&meta_empty[i], 8);  // the transform warps
     }
     *abort_flag = 0;
     dev::fence_mbarrier_init();
@@ -163,7 +180,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       uint32_t armed = 0, armed_par = 0;  // packed stages with a load in flight
       uint32_t meta_armed = 0, meta_par = 0;
       for (int g = 0; g < NG; ++g) {
-        if ((g & 7) == 0) {
+        if (TMETA && (g & 7) == 0) {
           const int c = g >> 3;
           const int slot = c & 1;
           if (!dev::mbar_wait<true>(&meta_empty[slot], ((c >> 1) & 1) ^ 1u, abort_flag)) break;
@@ -227,6 +244,17 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     // ------------------------------------------------------------ transform
     const int t = static_cast<int>(((warp - 2) & 3) * 32 + lane);  // row of the A or B tile
     const int opw = static_cast<int>(warp - 2) >> 2;                 // 0: A rows, 1: B rows
+    // Direct scale / zero-point loads (TMETA = false): this thread's row, one group
+    // ahead of its use; rows past the matrix read as scale 0, zero point 0.
+    const int grow = (opw == 0 ? m0 : n0) + t;
+    const bool row_in = grow < (opw == 0 ? M : N);
+    const __half* row_s = (opw == 0 ? meta.As : meta.Bs) + static_cast<size_t>(grow) * NG;
+    const __half* row_z = (opw == 0 ? meta.Az : meta.Bz) + static_cast<size_t>(grow) * NG;
+    __half nxt_s = __float2half(0.f), nxt_z = __float2half(0.f);
+    if (!TMETA && row_in) {
+      nxt_s = row_s[0];
+      nxt_z = row_z[0];
+    }
     for (int g = 0; g < NG; ++g) {
       const int c = g >> 3;
       const int mslot = c & 1;
@@ -234,22 +262,38 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       const int u = g % S::UN_STAGES;
       const int sbs = g % S::SB_SLOTS;
       bool ok = true;
-      if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
+      if (TMETA && (g & 7) == 0)
+        ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&pk_full[s], static_cast<uint32_t>(g / S::PK_STAGES) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&un_empty[u], (static_cast<uint32_t>(g / S::UN_STAGES) & 1u) ^ 1u, abort_flag);
       ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g / S::SB_SLOTS) & 1u) ^ 1u, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (warp == 2 && lane == 0 && g < 32) CLOVE_TRACE_POINT(192 + g);
 
-      const uint8_t* mt = smem + S::OFF_META + mslot * S::META_BYTES;
-      const __half* meta_az = reinterpret_cast<const __half*>(mt + 1 * S::META_BOX);
-      const __half* meta_bs = reinterpret_cast<const __half*>(mt + 2 * S::META_BOX);
-      const __half* meta_bz = reinterpret_cast<const __half*>(mt + 3 * S::META_BOX);
       const int gi = g & 7;
-      const int za = opw == 0 ? __half2int_rn(meta_az[t * 8 + gi]) : 0;
-      const int zb = opw == 1 ? __half2int_rn(meta_bz[t * 8 + gi]) : 0;
-      float* slot = sbf + sbs * 3 * S::BN;  // [B scale][16 Cc][row term]
-      if (opw == 1) slot[t] = __half2float(meta_bs[t * 8 + gi]);
+      float rs;  // this row's scale for group g
+      int rz;    // and its zero point
+      if constexpr (TMETA) {
+        const uint8_t* mt = smem + S::OFF_META + mslot * S::META_BYTES;
+        const __half* meta_s = reinterpret_cast<const __half*>(mt + (opw == 0 ? 0 : 2) * S::META_BOX);
+        const __half* meta_z = reinterpret_cast<const __half*>(mt + (opw == 0 ? 1 : 3) * S::META_BOX);
+        rs = __half2float(meta_s[t * 8 + gi]);
+        rz = __half2int_rn(meta_z[t * 8 + gi]);
+      } else {
+        rs = __half2float(nxt_s);
+        rz = __half2int_rn(nxt_z);
+        if (row_in && g + 1 < NG) {
+          nxt_s = row_s[g + 1];
+          nxt_z = row_z[g + 1];
+        }
+      }
+      const int za = opw == 0 ? rz : 0;
+      const int zb = opw == 1 ? rz : 0;
+      float* slot = sbf + sbs * 4 * S::BN;  // [B scale][16 Cc][row term][A scale]
+      if (opw == 1)
+        slot[t] = rs;
+      else
+        slot[3 * S::BN + t] = rs;
 
       const uint8_t* pk = smem + S::OFF_PK + s * S::PK_BYTES;
       uint8_t* un = smem + S::OFF_UN + u * S::UN_BYTES;
@@ -293,7 +337,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         dev::mbar_arrive(&un_full[u]);
         dev::mbar_arrive(&sb_full[sbs]);
         dev::mbar_arrive(&pk_empty[s]);
-        if (gi == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
+        if (TMETA && (gi == 7 || g == NG - 1)) dev::mbar_arrive(&meta_empty[mslot]);
       }
     }
   } else {
@@ -312,20 +356,16 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.f, 0.f);
     bool ok = true;
     for (int g = 0; g < NG && ok; ++g) {
-      const int c = g >> 3;
-      const int mslot = c & 1;
       const int b = g % S::ACC_BUFS;
       const int sbs = g % S::SB_SLOTS;
-      if ((g & 7) == 0) ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
-      ok = ok && dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g / S::ACC_BUFS) & 1u, abort_flag);
+      ok = dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g / S::ACC_BUFS) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g / S::SB_SLOTS) & 1u, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       if (warp == 10 && lane == 0 && g < 32) CLOVE_TRACE_POINT(224 + g);
       dev::tc_fence_after_sync();
-      const __half* meta_as = reinterpret_cast<const __half*>(smem + S::OFF_META + mslot * S::META_BYTES);
-      const float sa = __half2float(meta_as[row * 8 + (g & 7)]);
-      const float* slot = sbf + sbs * 3 * S::BN;
+      const float* slot = sbf + sbs * 4 * S::BN;
+      const float sa = slot[3 * S::BN + row];
       const float* sb = slot + h * 64;
       const int* colt = reinterpret_cast<const int*>(slot) + S::BN + h * 64;
       const int rowt = reinterpret_cast<const int*>(slot)[2 * S::BN + row];
@@ -387,7 +427,6 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       if (lane == 0) {
         if (warp == 10 && g < 32) CLOVE_TRACE_POINT(128 + g);
         dev::mbar_arrive(&sb_empty[sbs]);
-        if ((g & 7) == 7 || g == NG - 1) dev::mbar_arrive(&meta_empty[mslot]);
       }
     }
     if (ok) {

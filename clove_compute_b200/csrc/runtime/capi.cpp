@@ -689,7 +689,7 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
     }
   } else {
     const bool gemv = (N <= 8 || M <= 8) && K % 128 == 0;
-    const bool tc = K % 1024 == 0 && N % 8 == 0;
+    const bool tc = K % 128 == 0 && N % 8 == 0;
     int path = ov.path ? ov.path : (gemv ? 2 : (tc ? 1 : 3));
     name = path == 2 ? (N <= 8 && (N <= M || M > 8) ? "gemv_int4" : "gemv_int4_t")
                      : path == 1 ? "tc_int4" : "simt_int4";

@@ -16,14 +16,19 @@
 //
 // NCCL is opened with dlopen on first use so that loading this library never pins
 // an NCCL build into the process (PyTorch ships its own; whichever libnccl.so.2 is
-// already loaded is reused).
+// already loaded is reused). The communicator is non-blocking: creation, every
+// collective call and finalisation are polled with ncclCommGetAsyncError under a
+// deadline, so a rank that never joins ends the others' call with
+// CLOVE_ERR_TIMEOUT (communicator aborted) instead of a hang.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -87,7 +92,7 @@ struct IpcMapping {
 };
 
 struct clove_nsplit_ctx {
-  ncclComm_t comm;
+  ncclComm_t comm = nullptr;
   int rank;
   int nranks;
   int device;
@@ -105,6 +110,9 @@ struct NcclApi {
   void* handle = nullptr;
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
@@ -130,13 +138,17 @@ void load_nccl() {
   g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(g_nccl.handle, name))
   CLOVE_SYM(GetUniqueId, "ncclGetUniqueId");
   CLOVE_SYM(CommInitRank, "ncclCommInitRank");
+  CLOVE_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+  CLOVE_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+  CLOVE_SYM(CommFinalize, "ncclCommFinalize");
   CLOVE_SYM(CommDestroy, "ncclCommDestroy");
   CLOVE_SYM(CommAbort, "ncclCommAbort");
   CLOVE_SYM(AllGather, "ncclAllGather");
   CLOVE_SYM(GetErrorString, "ncclGetErrorString");
 #undef CLOVE_SYM
   if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.CommDestroy || !g_nccl.AllGather ||
-      !g_nccl.GetErrorString || !g_nccl.CommAbort) {
+      !g_nccl.GetErrorString || !g_nccl.CommAbort || !g_nccl.CommInitRankConfig ||
+      !g_nccl.CommGetAsyncError || !g_nccl.CommFinalize) {
     g_nccl.error = "libnccl is missing required symbols";
     g_nccl.handle = nullptr;
   }
@@ -152,6 +164,37 @@ int check_nccl(ncclResult_t r, const char* what) {
   if (r == ncclSuccess) return CLOVE_OK;
   return fail(CLOVE_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString(r));
 }
+
+// The communicator is non-blocking: a call may return ncclInProgress, and is done
+// (initialised, or the collective enqueued) once ncclCommGetAsyncError reports
+// anything else. Polls every 200 us up to the deadline; past it the communicator
+// is aborted (so no rank is left waiting on it) and the call fails with
+// CLOVE_ERR_TIMEOUT.
+int settle_nccl(ncclComm_t comm, ncclResult_t r, const char* what, double deadline_s,
+                bool* aborted = nullptr) {
+  if (r != ncclInProgress) return check_nccl(r, what);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t q = g_nccl.CommGetAsyncError(comm, &st);
+    if (q != ncclSuccess) return check_nccl(q, "ncclCommGetAsyncError");
+    if (st != ncclInProgress) return check_nccl(st, what);
+    const double el =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > deadline_s) {
+      g_nccl.CommAbort(comm);
+      if (aborted) *aborted = true;
+      return fail(CLOVE_ERR_TIMEOUT, "%s: not done after %.0f s (a rank missing?); communicator aborted",
+                  what, deadline_s);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+// Deadlines of the non-blocking communicator: creation waits for every rank to
+// join; a collective call only has to be enqueued.
+constexpr double kNcclInitDeadlineS = 120.0;
+constexpr double kNcclCallDeadlineS = 30.0;
 
 int shard_cols(int N, int P, int r) {
   return clove_nsplit_col_begin(N, P, r + 1) - clove_nsplit_col_begin(N, P, r);
@@ -181,8 +224,8 @@ int gather_columns(clove_nsplit_ctx* ctx, const void* C_shard, void* C_full, int
     send = pad;
   }
   if (!rc)
-    rc = check_nccl(g_nccl.AllGather(send, staging, slot / 2, ncclHalf, ctx->comm, s),
-                    "ncclAllGather");
+    rc = settle_nccl(ctx->comm, g_nccl.AllGather(send, staging, slot / 2, ncclHalf, ctx->comm, s),
+                     "ncclAllGather", kNcclCallDeadlineS);
   if (!rc) rc = launch_relayout_columns(staging, C_full, M, N, P, Nmax, elem_bytes, s);
   const int rc2 = check_cuda(cudaFreeAsync(staging, s), "cudaFreeAsync(staging)");
   return rc ? rc : rc2;
@@ -274,9 +317,10 @@ int all_gather_host(clove_nsplit_ctx* ctx, const void* mine, size_t n, void* all
                                     cudaMemcpyHostToDevice, s),
                     "cudaMemcpyAsync(all-gather in)");
   if (!rc)
-    rc = check_nccl(g_nccl.AllGather(static_cast<char*>(dbuf) + n * P, dbuf, n, ncclChar,
-                                     ctx->comm, s),
-                    "ncclAllGather(host records)");
+    rc = settle_nccl(ctx->comm,
+                     g_nccl.AllGather(static_cast<char*>(dbuf) + n * P, dbuf, n, ncclChar,
+                                      ctx->comm, s),
+                     "ncclAllGather(host records)", kNcclCallDeadlineS);
   if (!rc)
     rc = check_cuda(cudaMemcpyAsync(all, dbuf, n * P, cudaMemcpyDeviceToHost, s),
                     "cudaMemcpyAsync(all-gather out)");
@@ -392,13 +436,13 @@ int gemm_fp16_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const void* 
 // INT4 (config 5's sharded weights): the same route through the INT4 tensor-core
 // kernel's epilogue. Rank-independent conditions keep every rank on the tile
 // kernel: equal shards (N % 8P == 0) wider than the decode GEMV's 8 columns, M > 8,
-// K % 1024 == 0 (the kernel's TMA row pitches), 16-byte aligned operands.
+// K % 128 == 0, 16-byte aligned operands.
 int gemm_int4_to_peers(clove_nsplit_ctx* ctx, const SharedBuf& out, const uint8_t* A_q,
                        const void* A_scale, const void* A_zero, const uint8_t* B_q,
                        const void* B_scale, const void* B_zero, void* C_shard, int M, int N,
                        int K, cudaStream_t s) {
   const int P = ctx->nranks;
-  if (P > kMaxPeers || N % (8 * P) != 0 || N / P <= 8 || M <= 8 || K % 1024 != 0 ||
+  if (P > kMaxPeers || N % (8 * P) != 0 || N / P <= 8 || M <= 8 || K % 128 != 0 ||
       out.bytes < static_cast<size_t>(M) * N * 2)
     return CLOVE_ERR_UNSUPPORTED;
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -559,8 +603,16 @@ int clove_nsplit_init(clove_nsplit_ctx** ctx, int nranks, int rank, const uint8_
   rc = check_cuda(cudaGetDevice(&c->device), "cudaGetDevice");
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof(uid));
-  if (!rc) rc = check_nccl(g_nccl.CommInitRank(&c->comm, nranks, uid, rank), "ncclCommInitRank");
+  // Non-blocking creation, polled under a deadline: a rank that never joins turns
+  // into CLOVE_ERR_TIMEOUT on the others instead of a hang.
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  bool aborted = false;
+  if (!rc)
+    rc = settle_nccl(c->comm, g_nccl.CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg),
+                     "ncclCommInitRankConfig", kNcclInitDeadlineS, &aborted);
   if (rc) {
+    if (c->comm != nullptr && !aborted) g_nccl.CommAbort(c->comm);
     delete c;
     return rc;
   }
@@ -582,9 +634,16 @@ int clove_nsplit_destroy(clove_nsplit_ctx* ctx) {
     ctx->flags_mem = nullptr;
     if (!rc) rc = rc2;
   }
-  if (g_nccl.handle) {
-    const int rc3 = check_nccl(g_nccl.CommDestroy(ctx->comm), "ncclCommDestroy");
+  if (g_nccl.handle && ctx->comm != nullptr) {
+    // Finalize (non-blocking: polled under the deadline, aborted past it), then free.
+    bool aborted = false;
+    const int rc3 = settle_nccl(ctx->comm, g_nccl.CommFinalize(ctx->comm), "ncclCommFinalize",
+                                kNcclInitDeadlineS, &aborted);
     if (!rc) rc = rc3;
+    if (!aborted) {
+      const int rc4 = check_nccl(g_nccl.CommDestroy(ctx->comm), "ncclCommDestroy");
+      if (!rc) rc = rc4;
+    }
   }
   delete ctx;
   return rc;

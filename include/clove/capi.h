@@ -227,8 +227,8 @@ int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
  * this C_full store each finished tile straight into every rank's C_full over
  * NVLink (no all-gather, no staging) and end with a cross-rank completion signal.
  * The route depends only on (M, N, K, nranks): equal shards (N % 8P == 0; INT8
- * N % 16P == 0) that the tile kernels take (N/P > 8; INT4 also M > 8 and
- * K % 1024 == 0; INT8 no cluster split-K); other shapes still take the NCCL
+ * N % 16P == 0) that the tile kernels take (N/P > 8; INT4 also M > 8;
+ * INT8 no cluster split-K); other shapes still take the NCCL
  * all-gather. Operands must then be 16-byte aligned. At most 8 ranks.
  * Ordering contract of this route, so that a C_full can be reused call after call:
  *   - every replicated call of one context goes on one stream per rank (or on

@@ -53,6 +53,8 @@ def test_dispatch_description_without_gpu(clove_lib):
     d = clove_lib.describe_dispatch("fp16", 11008, 2048, 4096)
     assert d.startswith("tc2_f16")  # CTA-pair 256x256 tiles for the FFN shape
     assert clove_lib.describe_dispatch("int4", 4096, 1, 4096).startswith("gemv_int4")
+    # INT4 prefill at the FFN down projection's K = 11008 stays on the tensor cores.
+    assert clove_lib.describe_dispatch("int4", 4096, 2048, 11008).startswith("tc_int4")
     assert clove_lib.describe_dispatch("int8", 4096, 32, 4096).startswith("tc_int8")
     assert "split" in clove_lib.describe_dispatch("int8", 4096, 32, 4096)
 

@@ -77,6 +77,40 @@ def test_tc_int4_exact_groups(clove_lib, oracle_mod, cuda, M, N, K):
     _check(clove_lib, oracle_mod, M, N, K, seed=M + N)
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 128, 384), (256, 136, 11008), (130, 256, 1152),
+                                   (4096, 128, 11008)])
+def test_tc_int4_any_group_count(clove_lib, oracle_mod, cuda, M, N, K):
+    """K a multiple of 128 but not of 1024 (e.g. the Llama-7B down projection's
+    K = 11008, 86 groups): the tensor-core kernel reads scales and zero points
+    directly instead of in 8-group TMA boxes; every group accumulator bit-exact."""
+    assert clove_lib.describe_dispatch("int4", M, N, K).startswith("tc_int4")
+    _check(clove_lib, oracle_mod, M, N, K, seed=K + M, check_g=(M * N * K <= 256 * 256 * 11008))
+
+
+def test_tc_int4_unaligned_metadata(clove_lib, oracle_mod, cuda):
+    """Scales and zero points at 2-byte (not 16-byte) aligned addresses, K % 1024 == 0:
+    the direct-load variant again, same exact G."""
+    import torch
+    M, N, K = 256, 256, 2048
+    op = wl.int4_operands(M, N, K, seed=21)
+
+    def off(a):  # the same values one fp16 element past a 16-byte boundary
+        buf = torch.zeros(a.size + 8, dtype=torch.float16, device="cuda")
+        v = buf[1:1 + a.size].view(a.shape)
+        v.copy_(torch.from_numpy(np.ascontiguousarray(a)))
+        return v
+
+    args = (dev(op.A_q), off(op.A_scale), off(op.A_zero), dev(op.B_q), off(op.B_scale),
+            off(op.B_zero))
+    assert args[1].data_ptr() % 16 != 0
+    C2, G = clove_lib.debug_int4_group_acc(*args)
+    Gref = oracle_mod.int4_group_acc(op.A_q, op.A_zero, op.B_q, op.B_zero, K)
+    np.testing.assert_array_equal(host(G), Gref)
+    ref = oracle_mod.gemm_int4(op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero, K)
+    assert rel_fro(host(clove_lib.gemm_int4(*args)), ref) < TOL_TIGHT
+    assert clove_lib.device_error() == 0
+
+
 def test_tc_int4_config5_rows(clove_lib, oracle_mod, cuda):
     """BASELINE config 5 shape (8192^3) on the tensor-core path, checked on a row sample
     against the oracle (the full oracle product takes minutes on the host)."""
