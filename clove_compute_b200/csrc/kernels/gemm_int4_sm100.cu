@@ -79,6 +79,16 @@ int launch_gemm_int4_tc(const uint8_t* Aq, const void* As, const void* Az, const
   }
   const uint64_t bit = 1ull << (dev.device & 63);
   if ((g_attr_set[variant].load(std::memory_order_acquire) & bit) == 0) {
+    // The kernel moves registers between its warpgroups with setmaxnreg, planned for
+    // a launch allocation of S::REGS_LAUNCH per thread: with fewer, an increase
+    // would wait forever, so such a build is refused here rather than launched.
+    cudaFuncAttributes fa{};
+    rc = check_cuda(cudaFuncGetAttributes(&fa, kernel), "cudaFuncGetAttributes(int4)");
+    if (rc) return rc;
+    if (fa.numRegs != S::REGS_LAUNCH)
+      return fail(CLOVE_ERR_UNSUPPORTED,
+                  "gemm_int4_tc: built with %d registers per thread, its register plan needs %d",
+                  fa.numRegs, S::REGS_LAUNCH);
     rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::SMEM_BYTES),
                     "cudaFuncSetAttribute(int4 smem)");

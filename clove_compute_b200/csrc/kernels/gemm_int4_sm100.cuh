@@ -7,7 +7,8 @@
 //   G[m,n,g] = sum_{k in g} (a - zA)(b - zB)   exact in int32.
 //
 // One CTA computes a 128 x 128 tile of C; K advances one group (128 codes,
-// 64 packed bytes) at a time. 18 warps:
+// 64 packed bytes) at a time. 20 warps in four-warp groups (setmaxnreg gives the
+// epilogue 136 registers, the transform 80, the control warps 40):
 //   warp 0      TMA producer: packed A / B boxes [128 rows x 64 B] (64B swizzle)
 //               into a 4-deep ring; every 8 groups, boxes [128 rows x 8 groups] of
 //               A/B scales and zero points into a 2-slot ring (when K % 1024 == 0
@@ -16,7 +17,8 @@
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
 //               group into one of four int32 TMEM buffers (a fresh accumulator per
 //               group), so every G leaves the tensor core exact.
-//   warps 2-9   transform: warps 2-5 unpack row t of the A tile, warps 6-9 row t of
+//   warps 2-3   idle (fill the control warpgroup)
+//   warps 4-11  transform: warps 4-7 unpack row t of the A tile, warps 8-11 row t of
 //               the B tile, into a 128B-swizzled u8 stage (the MMA operand) holding
 //               the biased codes a'' = a - zA + 16 and b'' = b - zB + 16, both in
 //               [1, 31], formed with plain adds (no per-byte carries). Within a
@@ -27,7 +29,7 @@
 //                 G = D - 16 R - 16 Cc - 32768,   D = sum a'' b''  (u8 x u8 MMA).
 //               They publish, per group, the B scales (fp32), 16 Cc per column,
 //               0x4B400000 - 16 R - 32768 per row and the A scales (fp32).
-//   warps 10-17 epilogue: two warps per TMEM lane quarter, 64 columns each, read
+//   warps 12-19 epilogue: two warps per TMEM lane quarter, 64 columns each, read
 //               16 columns at a time. One 3-input integer add turns D into the fp32
 //               bit pattern of 12582912 + G (exact: |G| < 2^22), one subtraction
 //               gives float(G); acc += float(G) * (sA * sB) with packed fp32x2
@@ -60,7 +62,26 @@ struct I4Shape {
   // Per slot (one group): B scales, 16 x column code sums, row terms, A scales.
   static constexpr int SBF_BYTES = SB_SLOTS * 4 * BN * 4;
   static constexpr int EPI_BYTES = 8 * 4096;          // 8 warps x 32 rows x 128 B
-  static constexpr int THREADS = 18 * 32;
+  // 20 warps in warpgroup-aligned roles: warp 0 producer, warp 1 MMA, warps 2-3
+  // idle, warps 4-11 transform, warps 12-19 epilogue.
+  static constexpr int XFORM0 = 4;
+  static constexpr int EPI0 = 12;
+  static constexpr int THREADS = 20 * 32;
+  // Registers: launched at 96 per thread (the cap for 640 threads, 5 warps per
+  // sub-partition); setmaxnreg then moves them to where they are needed -- the
+  // producer / MMA warpgroup down to 40, the transform warpgroups to 80, the
+  // epilogue warpgroups (64 fp32 accumulators plus 32 columns of TMEM loads in
+  // flight per thread) up to 136.
+  static constexpr int REGS_LAUNCH = 96;
+  static constexpr int REGS_CTL = 40;
+  static constexpr int REGS_XFORM = 80;
+  static constexpr int REGS_EPI = 136;
+  static_assert(128 * REGS_CTL + 256 * REGS_XFORM + 256 * REGS_EPI <= THREADS * REGS_LAUNCH,
+                "register split exceeds the launch allocation");
+  // Warp w runs on sub-partition w % 4, which therefore holds one warp of each
+  // warpgroup: one control, two transform, two epilogue warps.
+  static_assert(32 * (REGS_CTL + 2 * REGS_XFORM + 2 * REGS_EPI) <= 16384,
+                "per sub-partition register file");
   static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int OFF_UN = 0;                                      // 1024-aligned
   static constexpr int OFF_PK = OFF_UN + UN_STAGES * UN_BYTES;
@@ -174,6 +195,10 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) CLOVE_TRACE_POINT(0);
 
+  // Roles by warpgroup; each branch first reallocates its registers (one setmaxnreg
+  // executed by all four warps of the group, ahead of the role's code).
+  if (warp < S::XFORM0) {
+    dev::setmaxnreg_dec<S::REGS_CTL>();
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -240,10 +265,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 10) {
+  }  // warps 2-3: idle
+  } else if (warp < S::EPI0) {
     // ------------------------------------------------------------ transform
-    const int t = static_cast<int>(((warp - 2) & 3) * 32 + lane);  // row of the A or B tile
-    const int opw = static_cast<int>(warp - 2) >> 2;                 // 0: A rows, 1: B rows
+    dev::setmaxnreg_dec<S::REGS_XFORM>();
+    const int t = static_cast<int>(((warp - S::XFORM0) & 3) * 32 + lane);  // row of the A or B tile
+    const int opw = static_cast<int>(warp - S::XFORM0) >> 2;                 // 0: A rows, 1: B rows
     // Direct scale / zero-point loads (TMETA = false): this thread's row, one group
     // ahead of its use; rows past the matrix read as scale 0, zero point 0.
     const int grow = (opw == 0 ? m0 : n0) + t;
@@ -268,7 +295,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       ok = ok && dev::mbar_wait(&un_empty[u], (static_cast<uint32_t>(g / S::UN_STAGES) & 1u) ^ 1u, abort_flag);
       ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g / S::SB_SLOTS) & 1u) ^ 1u, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
-      if (warp == 2 && lane == 0 && g < 32) CLOVE_TRACE_POINT(192 + g);
+      if (warp == S::XFORM0 && lane == 0 && g < 32) CLOVE_TRACE_POINT(192 + g);
 
       const int gi = g & 7;
       float rs;  // this row's scale for group g
@@ -333,7 +360,7 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
       __syncwarp();
       if (lane == 0) {
-        if (warp == 2 && g < 32) CLOVE_TRACE_POINT(64 + g);
+        if (warp == S::XFORM0 && g < 32) CLOVE_TRACE_POINT(64 + g);
         dev::mbar_arrive(&un_full[u]);
         dev::mbar_arrive(&sb_full[sbs]);
         dev::mbar_arrive(&pk_empty[s]);
@@ -342,8 +369,9 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    dev::setmaxnreg_inc<S::REGS_EPI>();
     const uint32_t q = warp & 3u;
-    const int h = static_cast<int>(warp - 10) >> 2;  // column half of the tile
+    const int h = static_cast<int>(warp - S::EPI0) >> 2;  // column half of the tile
     const int row = static_cast<int>(q * 32 + lane);
     // Replicated output: announce that this rank reached the call (every earlier
     // kernel on its stream, the readers of its C included, has completed: this
@@ -358,11 +386,11 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
     for (int g = 0; g < NG && ok; ++g) {
       const int b = g % S::ACC_BUFS;
       const int sbs = g % S::SB_SLOTS;
-      ok = dev::mbar_wait(&acc_full[b], static_cast<uint32_t>(g / S::ACC_BUFS) & 1u, abort_flag);
+      ok = dev::mbar_wait<true>(&acc_full[b], static_cast<uint32_t>(g / S::ACC_BUFS) & 1u, abort_flag);
       ok = ok && dev::mbar_wait(&sb_full[sbs], static_cast<uint32_t>(g / S::SB_SLOTS) & 1u, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      if (warp == 10 && lane == 0 && g < 32) CLOVE_TRACE_POINT(224 + g);
+      if (warp == S::EPI0 && lane == 0 && g < 32) CLOVE_TRACE_POINT(224 + g);
       dev::tc_fence_after_sync();
       const float* slot = sbf + sbs * 4 * S::BN;
       const float sa = slot[3 * S::BN + row];
@@ -376,25 +404,26 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       long long t_e0 = clock64();
 #endif
 #pragma unroll
-      for (int qc = 0; qc < 4; ++qc) {  // 16 columns at a time (register budget)
-        uint32_t vv[16];
+      for (int qc = 0; qc < 2; ++qc) {  // 32 columns (two TMEM loads in flight) at a time
+        uint32_t vv[32];
 #ifdef CLOVE_TRACE
         long long t_ld0 = clock64();
 #endif
-        dev::tmem_ld_x16(taddr + qc * 16, vv);
+        dev::tmem_ld_x16(taddr + qc * 32, *reinterpret_cast<uint32_t(*)[16]>(&vv[0]));
+        dev::tmem_ld_x16(taddr + qc * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&vv[16]));
         dev::tmem_ld_wait();
 #ifdef CLOVE_TRACE
-        if (warp == 10 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
+        if (warp == S::EPI0 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
           g_clove_trace[40 + qc] = static_cast<unsigned long long>(clock64() - t_ld0 + (vv[0] & 0));
 #endif
-        if (qc == 3) {
+        if (qc == 1) {
           dev::tc_fence_before_sync();
           __syncwarp();
           if (lane == 0) dev::mbar_arrive(&acc_empty[b]);
         }
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const int col = qc * 16 + j;  // column within this warp's 64
+        for (int j = 0; j < 32; j += 4) {
+          const int col = qc * 32 + j;  // column within this warp's 64
           const float4 s4 = *reinterpret_cast<const float4*>(sb + col);
           const int4 c4 = *reinterpret_cast<const int4*>(colt + col);
           // fp32 bit patterns of 12582912 + G: one 3-input add each.
@@ -420,18 +449,18 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         }
       }
 #ifdef CLOVE_TRACE
-      if (warp == 10 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
+      if (warp == S::EPI0 && lane == 0 && g == 12 && blockIdx.x == 0 && blockIdx.y == 0)
         g_clove_trace[44] = static_cast<unsigned long long>(clock64() - t_e0 + (acc[0].x == 1.5f));
 #endif
       __syncwarp();
       if (lane == 0) {
-        if (warp == 10 && g < 32) CLOVE_TRACE_POINT(128 + g);
+        if (warp == S::EPI0 && g < 32) CLOVE_TRACE_POINT(128 + g);
         dev::mbar_arrive(&sb_empty[sbs]);
       }
     }
     if (ok) {
       // fp16 into a 128B-swizzled staging tile, one TMA store per warp.
-      uint8_t* stg = smem + S::OFF_EPI + (warp - 10) * 4096;
+      uint8_t* stg = smem + S::OFF_EPI + (warp - S::EPI0) * 4096;
       const uint32_t sa_ = dev::smem_u32(stg);
 #pragma unroll
       for (int p = 0; p < 8; ++p) {

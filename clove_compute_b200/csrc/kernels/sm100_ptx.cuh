@@ -522,6 +522,22 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 }
 
 // ----------------------------------------------------------------------------
+// Register reallocation between warpgroups (setmaxnreg): every warp of a
+// warpgroup executes the same one. The sum over the block of the new limits must
+// not exceed what the block was launched with (threads x registers at launch), or
+// an increase waits forever: callers check it with a static_assert and the host
+// checks the launch register count.
+// ----------------------------------------------------------------------------
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ----------------------------------------------------------------------------
 // Cross-rank flags (system scope: the flag arrays of other ranks are IPC
 // mappings reached over NVLink)
 // ----------------------------------------------------------------------------
