@@ -18,6 +18,9 @@ CLOVE_DEFINE_ERROR_READER(read_clear_error_int4)
 extern "C" int clove_trace_read_int4(unsigned long long* out) {
   return static_cast<int>(cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * 256));
 }
+extern "C" int clove_trace_write_int4(const unsigned long long* in) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_clove_trace, in, sizeof(unsigned long long) * 256));
+}
 #endif
 
 namespace clove {

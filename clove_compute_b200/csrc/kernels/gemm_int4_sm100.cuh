@@ -282,12 +282,21 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       nxt_s = row_s[0];
       nxt_z = row_z[0];
     }
+#ifdef CLOVE_TRACE
+    // Development timing of one transform thread (CTA 0, first A warp, lane 0), clock
+    // cycles summed over groups 8-23: waits, unpack, proxy fence, hand-off.
+    const bool xf_probe = blockIdx.x == 0 && blockIdx.y == 0 && warp == S::XFORM0 && lane == 0;
+    long long xt0 = 0, xt1 = 0, xt2 = 0, xt3 = 0;
+#endif
     for (int g = 0; g < NG; ++g) {
       const int c = g >> 3;
       const int mslot = c & 1;
       const int s = g % S::PK_STAGES;
       const int u = g % S::UN_STAGES;
       const int sbs = g % S::SB_SLOTS;
+#ifdef CLOVE_TRACE
+      if (xf_probe) xt0 = clock64();
+#endif
       bool ok = true;
       if (TMETA && (g & 7) == 0)
         ok = dev::mbar_wait(&meta_full[mslot], static_cast<uint32_t>(c >> 1) & 1u, abort_flag);
@@ -296,6 +305,9 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       ok = ok && dev::mbar_wait(&sb_empty[sbs], (static_cast<uint32_t>(g / S::SB_SLOTS) & 1u) ^ 1u, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (warp == S::XFORM0 && lane == 0 && g < 32) CLOVE_TRACE_POINT(192 + g);
+#ifdef CLOVE_TRACE
+      if (xf_probe) xt1 = clock64();
+#endif
 
       const int gi = g & 7;
       float rs;  // this row's scale for group g
@@ -357,9 +369,23 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
         else
           reinterpret_cast<int*>(slot)[S::BN + t] = 16 * r;
       }
+#ifdef CLOVE_TRACE
+      if (xf_probe) xt2 = clock64();
+#endif
       dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+#ifdef CLOVE_TRACE
+      if (xf_probe) xt3 = clock64();
+#endif
       __syncwarp();
       if (lane == 0) {
+#ifdef CLOVE_TRACE
+        if (xf_probe && g >= 8 && g < 24) {
+          g_clove_trace[48] += static_cast<unsigned long long>(xt1 - xt0);  // waits
+          g_clove_trace[49] += static_cast<unsigned long long>(xt2 - xt1);  // unpack
+          g_clove_trace[50] += static_cast<unsigned long long>(xt3 - xt2);  // proxy fence
+          g_clove_trace[51] += static_cast<unsigned long long>(clock64() - xt3);  // hand-off
+        }
+#endif
         if (warp == S::XFORM0 && g < 32) CLOVE_TRACE_POINT(64 + g);
         dev::mbar_arrive(&un_full[u]);
         dev::mbar_arrive(&sb_full[sbs]);
