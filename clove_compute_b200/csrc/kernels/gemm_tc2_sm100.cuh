@@ -312,6 +312,10 @@ __global__ void __launch_bounds__(192, 1)
                            : "l"(sk.tickets + tix)
                            : "memory");
               *sk_last = t == w.nc - 1 ? 2 : 0;
+              // Every other piece has taken its ticket and this one takes none: the
+              // tile is done with its ticket, which goes back to zero for the next
+              // launch (the ticket array is kept between calls, never memset).
+              if (t == w.nc - 1) sk.tickets[tix] = 0;
               dev::mbar_arrive(&skbar[1]);
             }
             ok = __all_sync(0xffffffffu, dev::mbar_wait(&skbar[1], ph1 & 1u, abort_flag));
@@ -409,6 +413,7 @@ __global__ void __launch_bounds__(192, 1)
             __threadfence();
             const int old = atomicAdd(&sk.tickets[tix], 1);
             *sk_last = old == w.nc - 1 ? 1 : 0;
+            if (old == w.nc - 1) sk.tickets[tix] = 0;  // last ticket: reset for the next launch
             dev::mbar_arrive(&skbar[1]);
           }
           ok = __all_sync(0xffffffffu, ok);

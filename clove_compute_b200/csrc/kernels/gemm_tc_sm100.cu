@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cstdint>
 #include <mutex>
+#include <vector>
 
 #include "gemm_tc2_sm100.cuh"
 #include "gemm_tc_sm100.cuh"
@@ -250,6 +251,62 @@ std::atomic<int> g_tc2_clusters[64][3];  // co-resident pairs per device and var
 std::mutex g_sk_pool_mu;
 cudaMemPool_t g_sk_pool[64];
 
+// Stream-K tickets kept between calls, one zeroed array per (device, stream): a
+// tile's last contributor resets its ticket, so the array is zero again when the
+// kernel completes and no per-call memset is needed (a memset between two kernels
+// would also end their programmatic overlap). One array per stream keeps calls on
+// different streams apart. After a kernel failure the arrays are cleared
+// (reset_stream_k_tickets, from clove_get_device_error).
+struct TicketBuf {
+  int device;
+  cudaStream_t stream;
+  int* ptr;
+  size_t count;
+};
+std::mutex g_ticket_mu;
+std::vector<TicketBuf> g_tickets;
+
+// The ticket array for (device, stream) with at least `count` entries; nullptr when
+// it would have to be created while the stream is being captured.
+int stream_tickets(int device, cudaStream_t s, size_t count, bool capturing, int** out) {
+  std::lock_guard<std::mutex> lock(g_ticket_mu);
+  *out = nullptr;
+  for (TicketBuf& t : g_tickets) {
+    if (t.device != device || t.stream != s) continue;
+    if (t.count >= count) {
+      *out = t.ptr;
+      return CLOVE_OK;
+    }
+    if (capturing) return CLOVE_OK;
+    // Grow: the old array is released after the work already queued on the stream.
+    int* np = nullptr;
+    const size_t cap = std::max(count, 2 * t.count);
+    int rc = check_cuda(cudaMalloc(&np, cap * sizeof(int)), "cudaMalloc(stream-K tickets)");
+    if (!rc) rc = check_cuda(cudaMemsetAsync(np, 0, cap * sizeof(int), s), "cudaMemsetAsync(tickets)");
+    if (rc) {
+      if (np) cudaFree(np);
+      return rc;
+    }
+    cudaFreeAsync(t.ptr, s);
+    t.ptr = np;
+    t.count = cap;
+    *out = np;
+    return CLOVE_OK;
+  }
+  if (capturing) return CLOVE_OK;
+  int* np = nullptr;
+  const size_t cap = std::max<size_t>(count, 1024);
+  int rc = check_cuda(cudaMalloc(&np, cap * sizeof(int)), "cudaMalloc(stream-K tickets)");
+  if (!rc) rc = check_cuda(cudaMemsetAsync(np, 0, cap * sizeof(int), s), "cudaMemsetAsync(tickets)");
+  if (rc) {
+    if (np) cudaFree(np);
+    return rc;
+  }
+  g_tickets.push_back(TicketBuf{device, s, np, cap});
+  *out = np;
+  return CLOVE_OK;
+}
+
 int sk_pool(int device, cudaMemPool_t* out) {
   std::lock_guard<std::mutex> lock(g_sk_pool_mu);
   if (g_sk_pool[device & 63] == nullptr) {
@@ -404,29 +461,42 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
 
   void* ws = nullptr;
   if (plan.sk_tiles > 0) {
-    const size_t ticket_bytes = (static_cast<size_t>(plan.sk_tiles) * 2 * sizeof(int) + 255) & ~size_t(255);
+    const size_t n_tickets = static_cast<size_t>(plan.sk_tiles) * 2;
+    const size_t ticket_bytes = (n_tickets * sizeof(int) + 255) & ~size_t(255);
     const size_t part_bytes = static_cast<size_t>(plan.sk_tiles) * plan.max_contrib * 2 *
                               (256 * 128) * sizeof(uint32_t);
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     rc = check_cuda(cudaStreamIsCapturing(stream, &cap), "cudaStreamIsCapturing");
     if (rc) return rc;
-    if (cap == cudaStreamCaptureStatusNone) {
+    const bool capturing = cap != cudaStreamCaptureStatusNone;
+    int* tickets = nullptr;
+    rc = stream_tickets(dev.device, stream, n_tickets, capturing, &tickets);
+    if (rc) return rc;
+    // Partials (and, without a kept ticket array, the tickets) from stream-ordered
+    // scratch: a private pool that keeps its memory, or a graph allocation node of
+    // the graph's own pool under capture.
+    const size_t scratch = part_bytes + (tickets ? 0 : ticket_bytes);
+    if (!capturing) {
       cudaMemPool_t pool;
       rc = sk_pool(dev.device, &pool);
       if (rc) return rc;
-      rc = check_cuda(cudaMallocFromPoolAsync(&ws, ticket_bytes + part_bytes, pool, stream),
+      rc = check_cuda(cudaMallocFromPoolAsync(&ws, scratch, pool, stream),
                       "cudaMallocFromPoolAsync(stream-K)");
-    } else {  // graph capture: an allocation node of the graph's own pool
-      rc = check_cuda(cudaMallocAsync(&ws, ticket_bytes + part_bytes, stream),
-                      "cudaMallocAsync(stream-K)");
+    } else {
+      rc = check_cuda(cudaMallocAsync(&ws, scratch, stream), "cudaMallocAsync(stream-K)");
     }
     if (rc) return rc;
-    skp.tickets = static_cast<int*>(ws);
-    skp.partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ticket_bytes);
-    rc = check_cuda(cudaMemsetAsync(ws, 0, ticket_bytes, stream), "cudaMemsetAsync(stream-K)");
-    if (rc) {
-      cudaFreeAsync(ws, stream);
-      return rc;
+    if (tickets != nullptr) {
+      skp.tickets = tickets;
+      skp.partials = static_cast<uint32_t*>(ws);
+    } else {
+      skp.tickets = static_cast<int*>(ws);
+      skp.partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ticket_bytes);
+      rc = check_cuda(cudaMemsetAsync(ws, 0, ticket_bytes, stream), "cudaMemsetAsync(stream-K)");
+      if (rc) {
+        cudaFreeAsync(ws, stream);
+        return rc;
+      }
     }
   }
   rc = check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "gemm_tc2 launch");
@@ -435,6 +505,18 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
     if (rc == CLOVE_OK) rc = rc2;
   }
   return rc;
+}
+
+void reset_stream_k_tickets() {
+  std::lock_guard<std::mutex> lock(g_ticket_mu);
+  for (TicketBuf& t : g_tickets) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) return;
+    cudaSetDevice(t.device);
+    cudaMemset(t.ptr, 0, t.count * sizeof(int));
+    cudaDeviceSynchronize();
+    cudaSetDevice(cur);
+  }
 }
 
 }  // namespace rt

@@ -68,7 +68,8 @@ struct SkParams {
   int sk_tiles;
   int max_contrib;          // partial slots per stream-K tile
   uint32_t* partials;       // [sk_tiles][max_contrib][2 CTAs][64 column quads][128 rows][4]
-  int* tickets;             // [sk_tiles][2 CTAs], zero at launch
+  int* tickets;             // [sk_tiles][2 CTAs], zero at launch; the tile's last
+                            // contributor sets its ticket back to zero
 };
 
 // Epilogue of the int8 GEMV (modes as EpiMode 1..3).

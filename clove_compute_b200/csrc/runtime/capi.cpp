@@ -180,6 +180,9 @@ int clove_get_device_error(int* code) {
     if (r < 0) return fail(CLOVE_ERR_CUDA, "reading the device error word failed");
     if (v == 0 && r != 0) v = r;
   }
+  // A kernel that gave up may have left stream-K tickets taken: clear them so the
+  // next call starts from zero.
+  if (v != 0) reset_stream_k_tickets();
   *code = v;
   return CLOVE_OK;
 }

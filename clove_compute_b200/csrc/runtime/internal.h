@@ -103,6 +103,8 @@ int launch_gemm_tc2(int op, const void* A, const void* B, void* C, int M, int N,
                     const kern::EpiParams& ep, const DeviceInfo& dev, cudaStream_t stream,
                     const void* B2 = nullptr, const PeerTargets* peer = nullptr,
                     bool allow_stream_k = true);
+// Clears every kept stream-K ticket array (after a kernel failure left tickets set).
+void reset_stream_k_tickets();
 // True when (op, bn, split, out_bytes) is an instantiated kernel.
 bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();

@@ -51,7 +51,9 @@ const char* clove_last_error_string(void);
 /* Reads and clears the device-side error word of the current device (a kernel
  * whose bounded wait expired sets it). Synchronises the device. *code = 0 when
  * no kernel reported an error, 1 when a bounded wait expired (mbarrier or
- * cross-rank flag), 2 when a kernel was launched with a shape it rejects. */
+ * cross-rank flag), 2 when a kernel was launched with a shape it rejects. After an
+ * error it also resets the library's kept stream-K state, so call it before
+ * further GEMMs once a kernel may have failed. */
 int clove_get_device_error(int* code);
 
 /* ------------------------------------------------------------------------- */
