@@ -522,6 +522,18 @@ def _secondary(cc, torch, peaks):
             "TOPS": round(2 * n ** 3 / t / 1e12, 1),
             "frac_of_2x_bf16_peak": round(2 * n ** 3 / t / 1e12 / (2 * peaks["bf16_tflops"]), 4)}
         del t4
+    # INT4 prefill at the Llama-7B down projection's K = 11008 (86 groups: scales and
+    # zero points read directly instead of in 8-group TMA boxes), tokens as N.
+    M4, N4, K4 = 4096, 2048, 11008
+    op = wl.int4_operands(M4, N4, K4, seed=0)
+    t4 = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
+    C = torch.empty((M4, N4), dtype=torch.float16, device="cuda")
+    t = timeit(lambda i: cc.gemm_int4(*t4, C), 1, 40)
+    out["int4_ffn_down_4096x2048x11008"] = {
+        "kernel": cc.describe_dispatch("int4", M4, N4, K4), "us_per_call": round(t * 1e6, 2),
+        "TOPS": round(2 * M4 * N4 * K4 / t / 1e12, 1),
+        "frac_of_2x_bf16_peak": round(2 * M4 * N4 * K4 / t / 1e12 / (2 * peaks["bf16_tflops"]), 4)}
+    del t4
     for n in (4096, 8192, 16384):
         A8, B8, sA, sB = wl.int8_operands(n, n, n, seed=0)
         Ad, Bd, sAd, sBd = dev(A8), dev(B8), dev(sA), dev(sB)
@@ -792,6 +804,9 @@ def _summary(line):
         q = sec.get(f"int4_square_{n}")
         if q:
             out[f"int4_{n}_TOPS"] = q["TOPS"]
+    q = sec.get("int4_ffn_down_4096x2048x11008")
+    if q:
+        out["int4_k11008_TOPS"] = q["TOPS"]
     at = sec.get("attention_causal_1x32x2048x128")
     if at:
         out["attention_causal"] = {"us": at["us_per_call"], "TFLOPS": at["TFLOPS"],
