@@ -61,14 +61,15 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, int b
   }
   int kv_group = heads / kv_heads;
   float scale_log2 = scale * 1.4426950408889634f;  // log2(e)
-  void* args[] = {&tQ, &tK, &tV, &tO, &seq, &kv_group, &scale_log2};
+  void* args[] = {&tQ, &tK, &tV, &tO, &seq, &heads, &kv_group, &scale_log2};
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute la[1];
   la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   la[0].val.programmaticStreamSerializationAllowed = 1;
   const int n_qt = (seq + S::BQ - 1) / S::BQ;
-  cfg.gridDim = dim3(static_cast<unsigned>((n_qt + S::TILES - 1) / S::TILES),
-                     static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  const long long ctas = static_cast<long long>((n_qt + S::TILES - 1) / S::TILES) * heads * batch;
+  if (ctas > 0x7fffffffLL) return fail(CLOVE_ERR_UNSUPPORTED, "attention: %lld CTAs exceed the grid limit", ctas);
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
   cfg.blockDim = dim3(S::THREADS, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(S::SMEM_BYTES);
   cfg.stream = stream;

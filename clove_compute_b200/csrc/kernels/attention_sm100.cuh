@@ -93,8 +93,8 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV,
-                         const __grid_constant__ CUtensorMap tmO, int seq_len, int kv_group,
-                         float scale_log2) {
+                         const __grid_constant__ CUtensorMap tmO, int seq_len, int heads,
+                         int kv_group, float scale_log2) {
   using S = AttnShape;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = dev::align_smem_1024(smem_raw);
@@ -116,11 +116,17 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
   const uint32_t lane = dev::lane_idx();
   const int n_qt = (seq_len + S::BQ - 1) / S::BQ;
   const int n_pairs = (n_qt + 1) / 2;
-  // Causal: the tile pairs with the most key blocks start first.
-  const int pr = CAUSAL ? n_pairs - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
-  const int head = static_cast<int>(blockIdx.y);
+  // One-dimensional grid, rank-major: CTA i takes tile pair rank i / (heads * batch)
+  // of (batch, head) i % (heads * batch). Causal pairs are ranked by key blocks,
+  // most first, so the block scheduler starts every head's heaviest pair before any
+  // lighter one (longest job first) and the light pairs fill the last wave.
+  const int n_bh = static_cast<int>(gridDim.x) / n_pairs;
+  const int rk = static_cast<int>(blockIdx.x) / n_bh;
+  const int bh = static_cast<int>(blockIdx.x) - rk * n_bh;
+  const int pr = CAUSAL ? n_pairs - 1 - rk : rk;
+  const int head = bh % heads;
   const int kv_head = head / kv_group;
-  const int batch = static_cast<int>(blockIdx.z);
+  const int batch = bh / heads;
   // Tile t covers queries [q0 + 128 t, q0 + 128 t + 128).
   const int q0 = pr * S::TILES * S::BQ;
   const int nb0 = attn_blocks<CAUSAL>(2 * pr, seq_len);      // key blocks of tile 0
