@@ -11,6 +11,23 @@ namespace rt {
 
 CLOVE_DEFINE_ERROR_READER(read_clear_error_attn)
 
+}  // namespace rt
+}  // namespace clove
+
+#ifdef CLOVE_TRACE
+// Development builds only: the attention kernel's trace slots.
+extern "C" int clove_trace_read_attn(unsigned long long* out, int n) {
+  return static_cast<int>(
+      cudaMemcpyFromSymbol(out, g_clove_trace, sizeof(unsigned long long) * (n < 256 ? n : 256)));
+}
+extern "C" int clove_trace_write_attn(const unsigned long long* in) {
+  return static_cast<int>(cudaMemcpyToSymbol(g_clove_trace, in, sizeof(unsigned long long) * 256));
+}
+#endif
+
+namespace clove {
+namespace rt {
+
 namespace {
 std::atomic<uint64_t> g_attn_attr[2];
 

@@ -9,25 +9,35 @@
 //
 // One CTA computes two consecutive 128-query tiles of one (batch, head), which share
 // every K and V tile; keys advance 128 at a time. 10 warps:
-//   warp 0     TMA producer: lane 0 loads both Q tiles once (two 64-column boxes
-//              each, 128B swizzle), then K into a 2-stage ring; lane 1 loads V (one
-//              tile, reloaded once both tiles' P.V have read it).
-//   warp 1     TMEM allocator + MMA issuer (one thread): per key block, S_t = Q_t.K^T
-//              for each tile into its fp32 TMEM buffer (8 x kind::f16 M=128 N=128 K=16,
-//              both operands K-major), and O_t += P_t.V (P K-major from shared memory,
-//              V MN-major) as each tile's P arrives, in the order PV_0(j), QK_0(j+1),
-//              PV_1(j), QK_1(j+1): while one tile's softmax runs, the tensor core works
-//              on the other tile.
+//   warp 0     TMA producer (one thread): both Q tiles once (two 64-column boxes
+//              each, 128B swizzle), then K and V, each in a 2-stage ring, in the
+//              order the tensor core frees their stages (K of block j+2 once both
+//              S of block j are computed, V of block j+2 once both P.V of block j
+//              are), so no load waits behind a buffer that frees later.
+//   warp 1     TMEM allocator + MMA issuer (the warp runs the schedule, one elected
+//              lane issues): per key block, S_t = Q_t.K^T for each tile into its fp32
+//              TMEM buffer (8 x kind::f16 M=128 N=128 K=16, both operands K-major,
+//              from shared memory), and O_t += P_t.V with P_t read from tensor memory
+//              and V (MN-major) from shared memory, in the order PV_0(j), QK_0(j+1),
+//              PV_1(j), QK_1(j+1): while one tile's softmax runs, the tensor core
+//              works on the other tile. P.V starts on keys [0,64) as soon as the
+//              softmax has written them.
 //   warps 2-9  softmax, one warpgroup per tile, one query row per thread (its TMEM
 //              lane): the row of S into registers, mask, row maximum,
-//              p = 2^(s*scale*log2e - m), row sum, P as fp16 into shared memory (the A
-//              operand of P.V, 128B swizzle). The running maximum m is raised only when
-//              a block's maximum exceeds it by more than 8 (in log2 units): then O (in
-//              TMEM) and the row sum are rescaled by 2^(m_old - m_new) before the next
-//              P.V; otherwise the stale m is kept, p stays <= 2^8 and nothing is
-//              rescaled. Numerator and denominator always use the same m, so the result
-//              is the same softmax. At the end: O / l to fp16, staged in shared memory,
-//              TMA-stored.
+//              p = 2^(s*scale*log2e - m), row sum, P as fp16 pairs written back over
+//              the first 64 columns of the tile's S buffer (the A operand of P.V), in
+//              two halves of 64 keys, each handed to the MMA issuer on its own barrier.
+//              The running maximum m is raised only when a block's maximum exceeds
+//              it by more than 8 (in log2 units): then O (in TMEM) and the row sum
+//              are rescaled by 2^(m_old - m_new) before the next P.V; otherwise the
+//              stale m is kept, p stays <= 2^8 and nothing is rescaled. Numerator and
+//              denominator always use the same m, so the result is the same softmax.
+//              At the end: O / l to fp16, staged in shared memory, TMA-stored.
+// Tensor-core ordering carries the TMEM hand-offs: the MMAs of one issuing thread
+// run in issue order, and a tcgen05.commit arrives once all earlier ones complete.
+// So when S_t(j) is complete, P_t(j-1).V has finished reading P_t(j-1) and adding
+// into O_t (the softmax may overwrite S_t with P_t(j) and rescale O_t), and
+// QK_t(j+1), issued after PV_t(j), overwrites P_t(j) only after it has been read.
 // Layouts: Q, K, V, O are 4D tensor maps (head_dim, seq, heads, batch) with any
 // strides, so [batch, heads, seq, head_dim] (the reference's flash_attention) and
 // [batch, seq, heads, head_dim] (its runtime's q/k/v projections) both work; K and V
@@ -46,24 +56,24 @@ struct AttnShape {
   static constexpr int BQ = 128;       // queries per tile (TMEM lanes)
   static constexpr int TILES = 2;      // query tiles per CTA (ping-pong)
   static constexpr int BKV = 128;      // keys per block
-  static constexpr int K_STAGES = 2;
+  static constexpr int STAGES = 2;     // K ring and V ring depth
   static constexpr int HALF_TILE = 128 * 128;          // [128 rows x 64 cols] fp16, 128B swizzle
   static constexpr int TILE = 2 * HALF_TILE;           // [128 rows x 128 cols] fp16
   static constexpr int OFF_Q = 0;                      // Q of tile t at t * TILE
   static constexpr int OFF_K = OFF_Q + TILES * TILE;   // K stage s at OFF_K + s * TILE
-  static constexpr int OFF_V = OFF_K + K_STAGES * TILE;
-  static constexpr int OFF_P = OFF_V + TILE;           // P of tile t at OFF_P + t * TILE
-  static constexpr int OFF_BAR = OFF_P + TILES * TILE;
+  static constexpr int OFF_V = OFF_K + STAGES * TILE;  // V stage s at OFF_V + s * TILE
+  static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
   static constexpr int THREADS = (2 + 4 * TILES) * 32;
-  static constexpr int TMEM_COLS = 512;                // S of tile t at t*128, O at 256 + t*128
+  // S of tile t at columns t*128 (P_t over its first 64), O of tile t at 256 + t*128.
+  static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 256;
   static_assert(SMEM_BYTES <= 232448, "smem budget");
 };
 
 // kind::f16, fp32 accumulate, M = 128, N = 128; S: both operands K-major;
-// O: A (P) K-major, B (V) MN-major.
+// O: A (P, in tensor memory) K-major, B (V) MN-major.
 constexpr uint32_t kAttnIdescS = dev::make_idesc(1, 0, 0, 0, 0, 128, 128);
 constexpr uint32_t kAttnIdescO = dev::make_idesc(1, 0, 0, 0, 1, 128, 128);
 
@@ -88,6 +98,19 @@ __device__ __forceinline__ int attn_blocks(int qt, int seq_len) {
   return CAUSAL ? min(qt + 1, n_kb) : n_kb;
 }
 
+// Development timeline (-DCLOVE_TRACE builds only): clock64 of the first CTA at
+// the point, into trace slot i.
+#ifdef CLOVE_TRACE
+#define ATTN_TRACE(i)                                                             \
+  do {                                                                            \
+    if (blockIdx.x == 0) g_clove_trace[(i)] = clock64();                          \
+  } while (0)
+#else
+#define ATTN_TRACE(i) \
+  do {                \
+  } while (0)
+#endif
+
 template <bool CAUSAL>
 __global__ void __launch_bounds__(AttnShape::THREADS, 1)
     attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -100,14 +123,12 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
   uint8_t* smem = dev::align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   uint64_t* q_full = bars;            // [1]
-  uint64_t* k_full = bars + 1;        // [K_STAGES]
-  uint64_t* k_empty = bars + 3;       // [K_STAGES]
-  uint64_t* v_full = bars + 5;        // [1]
-  uint64_t* v_empty = bars + 6;       // [1]
-  uint64_t* s_full = bars + 7;        // [TILES]
-  uint64_t* s_empty = bars + 9;       // [TILES]
-  uint64_t* p_full = bars + 11;       // [TILES]
-  uint64_t* p_empty = bars + 13;      // [TILES]
+  uint64_t* k_full = bars + 1;        // [STAGES]
+  uint64_t* k_empty = bars + 3;       // [STAGES]
+  uint64_t* v_full = bars + 5;        // [STAGES]
+  uint64_t* v_empty = bars + 7;       // [STAGES]
+  uint64_t* s_full = bars + 9;        // [TILES]
+  uint64_t* p_full = bars + 11;       // [TILES][2]: keys [0,64) and [64,128) of P_t
   uint64_t* o_full = bars + 15;       // [TILES]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -136,17 +157,16 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
 
   if (threadIdx.x == 0) {
     dev::mbar_init(q_full, 1);
-    for (int st = 0; st < S::K_STAGES; ++st) {
+    for (int st = 0; st < S::STAGES; ++st) {
       dev::mbar_init(&k_full[st], 1);
       dev::mbar_init(&k_empty[st], 1);
+      dev::mbar_init(&v_full[st], 1);
+      dev::mbar_init(&v_empty[st], 1);
     }
-    dev::mbar_init(v_full, 1);
-    dev::mbar_init(v_empty, 1);
     for (int t = 0; t < S::TILES; ++t) {
       dev::mbar_init(&s_full[t], 1);
-      dev::mbar_init(&s_empty[t], 4);
-      dev::mbar_init(&p_full[t], 4);
-      dev::mbar_init(&p_empty[t], 1);
+      dev::mbar_init(&p_full[2 * t], 4);
+      dev::mbar_init(&p_full[2 * t + 1], 4);
       dev::mbar_init(&o_full[t], 1);
     }
     *abort_flag = 0;
@@ -170,12 +190,10 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
   // tail; no global memory is touched before it completes.
   dev::allow_dependent_launch();
   dev::grid_dependency_wait();
+  if (threadIdx.x == 0) ATTN_TRACE(0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // Lane 0: both Q tiles, then K in a 2-stage ring (block j+1's K loads while block
-    // j's is in use). Lane 1: V, a single tile reloaded once both tiles' P.V have read
-    // it, which leaves a softmax's worth of time before the next P.V needs it.
     if (lane == 0) {
       dev::mbar_arrive_expect_tx(q_full, n_tiles * S::TILE);
       for (int t = 0; t < n_tiles; ++t) {
@@ -183,40 +201,38 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
         dev::tma_load_4d(q_dst, &tmQ, q_full, 0, q0 + t * S::BQ, head, batch);
         dev::tma_load_4d(q_dst + S::HALF_TILE, &tmQ, q_full, 64, q0 + t * S::BQ, head, batch);
       }
-      uint32_t k_armed = 0, k_par = 0;
-      for (int j = 0; j < nb; ++j) {
-        const int ks = j & 1;
-        const uint32_t kph = static_cast<uint32_t>(j >> 1) & 1u;
-        if (!dev::mbar_wait<true>(&k_empty[ks], kph ^ 1u, abort_flag)) break;
-        uint8_t* k_dst = smem + S::OFF_K + ks * S::TILE;
-        dev::mbar_arrive_expect_tx(&k_full[ks], S::TILE);
-        dev::tma_load_4d(k_dst, &tmK, &k_full[ks], 0, j * S::BKV, kv_head, batch);
-        dev::tma_load_4d(k_dst + S::HALF_TILE, &tmK, &k_full[ks], 64, j * S::BKV, kv_head, batch);
-        k_armed |= 1u << ks;
-        k_par = (k_par & ~(1u << ks)) | (kph << ks);
+      // Ring slot of block j: stage j & 1, used for the (j >> 1)-th time. Blocks 0
+      // and 1 find their stages free; block j + 2 waits for block j's release.
+      uint32_t armed = 0, par = 0;  // bit s: K stage s, bit 2 + s: V stage s
+      auto load = [&](const CUtensorMap* tm, uint64_t* full, uint64_t* empty, int off, int j,
+                      int bit) -> bool {
+        const int st = j & 1;
+        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+        if (!dev::mbar_wait<true>(&empty[st], ph ^ 1u, abort_flag)) return false;
+        uint8_t* dst = smem + off + st * S::TILE;
+        dev::mbar_arrive_expect_tx(&full[st], S::TILE);
+        dev::tma_load_4d(dst, tm, &full[st], 0, j * S::BKV, kv_head, batch);
+        dev::tma_load_4d(dst + S::HALF_TILE, tm, &full[st], 64, j * S::BKV, kv_head, batch);
+        armed |= 1u << (bit + st);
+        par = (par & ~(1u << (bit + st))) | (ph << (bit + st));
+        return true;
+      };
+      bool go = true;
+      for (int j = 0; j < nb && j < 2 && go; ++j) go = load(&tmK, k_full, k_empty, S::OFF_K, j, 0);
+      for (int j = 0; j < nb && j < 2 && go; ++j) go = load(&tmV, v_full, v_empty, S::OFF_V, j, 2);
+      for (int j = 2; j < nb && go; ++j) {
+        go = load(&tmK, k_full, k_empty, S::OFF_K, j, 0);
+        go = go && load(&tmV, v_full, v_empty, S::OFF_V, j, 2);
       }
       if (*abort_flag) {
         // Error unwinding: every load still in flight lands before the CTA exits.
         volatile int no_abort = 0;
         dev::mbar_wait<true>(q_full, 0u, &no_abort);
-        for (int st = 0; st < S::K_STAGES; ++st)
-          if (k_armed & (1u << st)) dev::mbar_wait<true>(&k_full[st], (k_par >> st) & 1u, &no_abort);
-      }
-    } else if (lane == 1) {
-      bool v_armed = false;
-      uint32_t v_par = 0;
-      for (int j = 0; j < nb; ++j) {
-        const uint32_t ph = static_cast<uint32_t>(j) & 1u;
-        if (!dev::mbar_wait<true>(v_empty, ph ^ 1u, abort_flag)) break;
-        dev::mbar_arrive_expect_tx(v_full, S::TILE);
-        dev::tma_load_4d(smem + S::OFF_V, &tmV, v_full, 0, j * S::BKV, kv_head, batch);
-        dev::tma_load_4d(smem + S::OFF_V + S::HALF_TILE, &tmV, v_full, 64, j * S::BKV, kv_head, batch);
-        v_armed = true;
-        v_par = ph;
-      }
-      if (*abort_flag && v_armed) {
-        volatile int no_abort = 0;
-        dev::mbar_wait<true>(v_full, v_par, &no_abort);
+        for (int st = 0; st < S::STAGES; ++st) {
+          if (armed & (1u << st)) dev::mbar_wait<true>(&k_full[st], (par >> st) & 1u, &no_abort);
+          if (armed & (4u << st))
+            dev::mbar_wait<true>(&v_full[st], (par >> (2 + st)) & 1u, &no_abort);
+        }
       }
     }
     __syncwarp();
@@ -224,60 +240,81 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     // Software-pipelined over the key blocks: PV_0(j), QK_0(j+1), PV_1(j), QK_1(j+1),
     // so each tile's next S = Q.K^T is queued on the tensor core right behind its
-    // P.V while the other tile's softmax still runs.
-    if (lane == 0) {
-      const uint32_t v_addr = dev::smem_u32(smem + S::OFF_V);
-      bool ok = dev::mbar_wait(q_full, 0u, abort_flag);
-      int k_seen = -1;  // last key block whose K arrival has been waited for
-      auto qk = [&](int t, int j) {
-        const int ks = j & 1;
-        if (k_seen < j) {
-          ok = ok && dev::mbar_wait(&k_full[ks], static_cast<uint32_t>(j >> 1) & 1u, abort_flag);
-          k_seen = j;
-        }
-        ok = ok && dev::mbar_wait(&s_empty[t], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag);
-        if (!ok) return;
-        dev::tc_fence_after_sync();
-        const uint32_t q_addr = dev::smem_u32(smem + S::OFF_Q + t * S::TILE);
-        const uint32_t k_addr = dev::smem_u32(smem + S::OFF_K + ks * S::TILE);
-        const uint32_t s_tmem = tmem_base + static_cast<uint32_t>(t) * S::BKV;
+    // P.V while the other tile's softmax still runs. The whole warp runs the loop
+    // (waits, descriptor arithmetic stay warp-uniform) and one elected lane issues
+    // every MMA and commit: at N = 128 each MMA is 64 tensor-core cycles, so the
+    // issue path has to keep up.
+    const bool leader = dev::elect_one();
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, dev::mbar_wait(bar, parity, abort_flag));
+    };
+    bool ok = wait_all(q_full, 0u);
+    auto qk = [&](int t, int j) {
+      if (!ok) return;
+      const uint32_t q_addr = dev::smem_u32(smem + S::OFF_Q + t * S::TILE);
+      const uint32_t k_addr = dev::smem_u32(smem + S::OFF_K + (j & 1) * S::TILE);
+      const uint32_t s_tmem = tmem_base + static_cast<uint32_t>(t) * S::BKV;
+      if (leader) {
+        if (j < 16) ATTN_TRACE(192 + t * 16 + j);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           dev::mma_f16_ss(s_tmem, attn_kmajor_desc(q_addr, k), attn_kmajor_desc(k_addr, k),
                           kAttnIdescS, k > 0 ? 1u : 0u);
         dev::mma_commit(&s_full[t]);
-      };
-      auto pv = [&](int t, int j, int tnb) {
-        ok = ok && dev::mbar_wait(&p_full[t], static_cast<uint32_t>(j) & 1u, abort_flag);
+      }
+      __syncwarp();
+    };
+    // O_t += P_t.V over keys [0,64) as soon as the softmax has written them, then
+    // over [64,128): the first half's MMAs overlap the second half's exponentials.
+    auto pv = [&](int t, int j, int tnb) {
+      const uint32_t v_addr = dev::smem_u32(smem + S::OFF_V + (j & 1) * S::TILE);
+      const uint32_t p_tmem = tmem_base + static_cast<uint32_t>(t) * S::BKV;
+      const uint32_t o_tmem = tmem_base + S::O_COL + static_cast<uint32_t>(t) * S::BKV;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        ok = ok && wait_all(&p_full[2 * t + h], static_cast<uint32_t>(j) & 1u);
         if (!ok) return;
         dev::tc_fence_after_sync();
-        const uint32_t p_addr = dev::smem_u32(smem + S::OFF_P + t * S::TILE);
-        const uint32_t o_tmem = tmem_base + S::O_COL + static_cast<uint32_t>(t) * S::BKV;
+        if (leader) {
+          if (h == 0 && j < 16) ATTN_TRACE(160 + t * 16 + j);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          dev::mma_f16_ss(o_tmem, attn_kmajor_desc(p_addr, k), attn_v_desc(v_addr, k),
-                          kAttnIdescO, (j > 0 || k > 0) ? 1u : 0u);
-        dev::mma_commit(&p_empty[t]);
-        if (j == tnb - 1) dev::mma_commit(&o_full[t]);
-      };
-      if (nb > 0) {
-        if (nb0 > 0) qk(0, 0);
-        if (nb1 > 0) qk(1, 0);
-        if (ok) dev::mma_commit(&k_empty[0]);
+          for (int k = 4 * h; k < 4 * h + 4; ++k)
+            dev::mma_f16_ts(o_tmem, p_tmem + 8 * k, attn_v_desc(v_addr, k), kAttnIdescO,
+                            (j > 0 || k > 0) ? 1u : 0u);
+          if (h == 1 && j == tnb - 1) dev::mma_commit(&o_full[t]);
+
+        }
+        __syncwarp();
       }
-      for (int j = 0; j < nb && ok; ++j) {
-        ok = dev::mbar_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag);
-        const bool next = j + 1 < nb;
-        if (j < nb0) pv(0, j, nb0);
-        if (next && j + 1 < nb0) qk(0, j + 1);
-        if (j < nb1) pv(1, j, nb1);
-        if (next && j + 1 < nb1) qk(1, j + 1);
-        if (!ok) break;
-        if (next) dev::mma_commit(&k_empty[(j + 1) & 1]);  // block j+1's K: both S issued
-        dev::mma_commit(v_empty);                          // block j's V: both P.V issued
-      }
+    };
+    auto k_ready = [&](int j) {
+      ok = ok && wait_all(&k_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u);
+      if (ok) dev::tc_fence_after_sync();
+    };
+    auto commit = [&](uint64_t* bar) {
+      if (leader) dev::mma_commit(bar);
+      __syncwarp();
+    };
+    if (nb > 0) {
+      k_ready(0);
+      if (nb0 > 0) qk(0, 0);
+      if (nb1 > 0) qk(1, 0);
+      if (ok) commit(&k_empty[0]);  // block 0's K: both S issued
     }
-    __syncwarp();
+    for (int j = 0; j < nb && ok; ++j) {
+      // V of block j and K of block j+1 landed long ago (two-stage rings); waiting
+      // for them here keeps them off the path from a softmax to the next MMAs.
+      ok = wait_all(&v_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u);
+      const bool next = j + 1 < nb;
+      if (next) k_ready(j + 1);
+      if (j < nb0) pv(0, j, nb0);
+      if (next && j + 1 < nb0) qk(0, j + 1);
+      if (j < nb1) pv(1, j, nb1);
+      if (!ok) break;
+      commit(&v_empty[j & 1]);                              // block j's V: both P.V issued
+      if (next && j + 1 < nb1) qk(1, j + 1);
+      if (next && ok) commit(&k_empty[(j + 1) & 1]);        // block j+1's K: both S issued
+    }
   } else {
     // ------------------------------------------------------------ softmax (2 warpgroups)
     const int t = static_cast<int>(warp - 2) >> 2;   // this warpgroup's query tile
@@ -292,11 +329,11 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
     float m = -__int_as_float(0x7f800000);  // running maximum (log2 units), may be stale
     float l = 0.f;                           // running sum of p under m
     bool ok = true;
-    const uint32_t p_addr = dev::smem_u32(smem + S::OFF_P + t * S::TILE + row * 128);
     for (int j = 0; j < my_nb; ++j) {
       const uint32_t ph = static_cast<uint32_t>(j) & 1u;
       ok = __all_sync(0xffffffffu, dev::mbar_wait(&s_full[t], ph, abort_flag));
       if (!ok) break;
+      if (row == 0 && j < 16) ATTN_TRACE(64 + t * 16 + j);
       dev::tc_fence_after_sync();
       float s[128];
 #pragma unroll
@@ -307,9 +344,6 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
         for (int u = 0; u < 16; ++u) s[c + u] = __uint_as_float(r[u]);
       }
       dev::tmem_ld_wait();
-      dev::tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) dev::mbar_arrive(&s_empty[t]);
 
       const int k0 = j * S::BKV;
       // Keys past seq_len, and for causal attention keys after the query, are masked.
@@ -320,16 +354,16 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (k0 + i > lim) s[i] = -__int_as_float(0x7f800000);
       }
-      // Row maximum as 8 independent chains, then a short tree.
+      // Row maximum as 8 independent chains of 3-input maxima, then a short tree.
       float mx8[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = s[u];
+      for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(s[2 * u], s[2 * u + 1]);
 #pragma unroll
-      for (int i = 8; i < 128; i += 8)
+      for (int i = 16; i < 128; i += 16)
 #pragma unroll
-        for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(mx8[u], s[i + u]);
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int u = 0; u < 8; ++u) mx8[u] = dev::fmax3(mx8[u], s[i + 2 * u], s[i + 2 * u + 1]);
+      float mx = dev::fmax3(dev::fmax3(mx8[0], mx8[1], mx8[2]), dev::fmax3(mx8[3], mx8[4], mx8[5]),
+                            fmaxf(mx8[6], mx8[7]));
       mx *= scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool raise = m_new > m + 8.0f;
@@ -339,21 +373,7 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
         alpha = dev::ex2_approx(m - m_new);
         m = m_new;
       }
-      // p = 2^(s * scale * log2e - m), packed to fp16 pairs.
-      uint32_t pk[64];
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        const float p0 = dev::ex2_approx(fmaf(s[i], scale_log2, -m));
-        const float p1 = dev::ex2_approx(fmaf(s[i + 1], scale_log2, -m));
-        sum4[(i >> 1) & 3] += p0 + p1;
-        pk[i >> 1] = dev::pack_half2(p0, p1);
-      }
-      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      // The tile's P buffer and O are free once its previous P.V has completed.
-      ok = __all_sync(0xffffffffu, dev::mbar_wait(&p_empty[t], ph ^ 1u, abort_flag));
-      if (!ok) break;
-      dev::tc_fence_after_sync();
+      // O was last added to by P_t(j-1).V, which completed before S_t(j) did.
       if (any_raise && j > 0) {
 #pragma unroll 1
         for (int c = 0; c < 128; c += 16) {
@@ -364,20 +384,42 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
           for (int u = 0; u < 16; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * alpha);
           dev::tmem_st_x16(t_lane + o_col + c, r);
         }
-        dev::tmem_st_wait();
       }
-      // P row into the 128B-swizzled A operand: keys [0,64) in the first half tile,
-      // [64,128) in the second; 16-byte chunk c of a row at (c ^ row % 8).
+      // p = 2^(s * scale * log2e - m) on key pairs (packed fp32 arithmetic), packed to
+      // fp16 pairs (key 2c in the low half of column c of the tile's P), 32 keys per
+      // tensor-memory store.
+      const uint64_t sc2 = dev::f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = dev::f2_pack(-m, -m);
+      uint64_t sum2[2] = {0ull, 0ull};  // two packed partial sums (+0.0f pairs)
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint32_t half = static_cast<uint32_t>(c >> 3) * S::HALF_TILE;
-        const uint32_t off = half + ((static_cast<uint32_t>(c & 7) ^ (static_cast<uint32_t>(row) & 7u)) << 4);
-        dev::st_shared_v4(p_addr + off, pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      for (int c = 0; c < 64; c += 16) {
+        uint32_t r[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int i = 2 * (c + u);
+          const uint64_t x = dev::f2_fma(dev::f2_pack(s[i], s[i + 1]), sc2, nm2);
+          float x0, x1;
+          dev::f2_unpack(x, x0, x1);
+          const uint64_t pp = dev::f2_pack(dev::ex2_approx(x0), dev::ex2_approx(x1));
+          sum2[u & 1] = dev::f2_add(sum2[u & 1], pp);
+          float p0, p1;
+          dev::f2_unpack(pp, p0, p1);
+          r[u] = dev::pack_half2(p0, p1);
+        }
+        dev::tmem_st_x16(t_lane + s_col + c, r);
+        if (c == 16 || c == 48) {
+          // Keys [0,64) (then [64,128)) of P written: hand them to P.V.
+          dev::tmem_st_wait();
+          dev::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) dev::mbar_arrive(&p_full[2 * t + (c >> 5)]);
+        }
       }
-      dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
-      dev::tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) dev::mbar_arrive(&p_full[t]);
+      float sa, sb, sc, sd;
+      dev::f2_unpack(sum2[0], sa, sb);
+      dev::f2_unpack(sum2[1], sc, sd);
+      l = l * alpha + ((sa + sb) + (sc + sd));
+      if (row == 0 && j < 16) ATTN_TRACE(96 + t * 16 + j);
     }
     if (ok && my_nb > 0) {
       ok = __all_sync(0xffffffffu, dev::mbar_wait<true>(&o_full[t], 0u, abort_flag));
