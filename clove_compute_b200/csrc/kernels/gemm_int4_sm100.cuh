@@ -15,12 +15,14 @@
 //               and those arrays are 16-byte aligned; otherwise each transform
 //               thread loads its own row's scale and zero point, one group ahead).
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32) per
-//               group into one of four int32 TMEM buffers (a fresh accumulator per
-//               group), so every G leaves the tensor core exact.
+//               group into one of three int32 TMEM buffers (a fresh accumulator per
+//               group), so every G leaves the tensor core exact; the A operand comes
+//               from tensor memory, B from shared memory.
 //   warps 2-3   idle (fill the control warpgroup)
-//   warps 4-11  transform: warps 4-7 unpack row t of the A tile, warps 8-11 row t of
-//               the B tile, into a 128B-swizzled u8 stage (the MMA operand) holding
-//               the biased codes a'' = a - zA + 16 and b'' = b - zB + 16, both in
+//   warps 4-11  transform: warps 4-7 unpack row t of the A tile into TMEM lane t (a
+//               32-column stage: the MMA's A operand, no shared-memory round trip),
+//               warps 8-11 row t of the B tile into a 128B-swizzled u8 shared-memory
+//               stage, holding the biased codes a'' = a - zA + 16 and b'' = b - zB + 16, both in
 //               [1, 31], formed with plain adds (no per-byte carries). Within a
 //               group both operands use the same K order (the high nibbles of a
 //               4-byte word, then its low nibbles), which leaves the dot product
@@ -50,12 +52,11 @@ struct I4Shape {
   static constexpr int GB = 64;                       // packed bytes per group per row
   static constexpr int PK_STAGES = 4;
   static constexpr int UN_STAGES = 4;
-  static constexpr int ACC_BUFS = 4;                  // int32 TMEM accumulators
+  static constexpr int ACC_BUFS = 3;                  // int32 TMEM accumulators
   static constexpr int SB_SLOTS = 4;
   static constexpr int PK_A = BM * GB;                // 8 KB
   static constexpr int PK_BYTES = (BM + BN) * GB;     // 16 KB
-  static constexpr int UN_A = BM * 128;               // 16 KB
-  static constexpr int UN_BYTES = (BM + BN) * 128;    // 32 KB
+  static constexpr int UN_BYTES = BN * 128;           // 16 KB: unpacked B (A is in TMEM)
   static constexpr int META_BOX = 128 * 16;           // 128 rows x 8 groups x fp16
   static constexpr int META_BYTES = 4 * META_BOX;     // A scale, A zero, B scale, B zero
   static constexpr int META_SLOTS = 2;
@@ -82,7 +83,10 @@ struct I4Shape {
   // warpgroup: one control, two transform, two epilogue warps.
   static_assert(32 * (REGS_CTL + 2 * REGS_XFORM + 2 * REGS_EPI) <= 16384,
                 "per sub-partition register file");
-  static constexpr int TMEM_COLS = ACC_BUFS * BN;
+  // TMEM: accumulator b at columns b * BN; unpacked A stage u (128 lanes x 128 bytes)
+  // at A_COL + 32 u.
+  static constexpr int A_COL = ACC_BUFS * BN;
+  static constexpr int TMEM_COLS = 512;
   static constexpr int OFF_UN = 0;                                      // 1024-aligned
   static constexpr int OFF_PK = OFF_UN + UN_STAGES * UN_BYTES;
   static constexpr int OFF_META = OFF_PK + PK_STAGES * PK_BYTES;
@@ -95,8 +99,8 @@ struct I4Shape {
   static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
   static_assert(SMEM_BYTES <= 232448, "smem budget");
   static_assert(OFF_PK % 1024 == 0 && OFF_META % 1024 == 0 && OFF_EPI % 1024 == 0, "align");
-  static_assert(EPI_BYTES <= UN_BYTES, "staging alias");
-  static_assert(TMEM_COLS <= 512, "TMEM");
+  static_assert(EPI_BYTES <= UN_STAGES * UN_BYTES, "staging alias");
+  static_assert(A_COL + UN_STAGES * 32 <= TMEM_COLS, "TMEM");
 };
 
 // kind::i8, s32 accumulator, u8 x u8, both operands K-major, M = N = 128.
@@ -251,14 +255,13 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
           break;
         dev::tc_fence_after_sync();
         if (g < 32) CLOVE_TRACE_POINT(96 + g);
-        const uint32_t a_addr = dev::smem_u32(smem + S::OFF_UN + u * S::UN_BYTES);
-        const uint32_t b_addr = a_addr + S::UN_A;
+        const uint32_t a_tm = tmem_base + S::A_COL + static_cast<uint32_t>(u) * 32;
+        const uint32_t b_addr = dev::smem_u32(smem + S::OFF_UN + u * S::UN_BYTES);
         const uint32_t d = tmem_base + static_cast<uint32_t>(b) * S::BN;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = dev::make_smem_desc(a_addr + k * 32, 0, 1024, dev::kLayoutSw128);
           const uint64_t bd = dev::make_smem_desc(b_addr + k * 32, 0, 1024, dev::kLayoutSw128);
-          dev::mma_i8_ss(d, ad, bd, kI4Idesc, k > 0 ? 1u : 0u);
+          dev::mma_i8_ts(d, a_tm + 8 * k, bd, kI4Idesc, k > 0 ? 1u : 0u);
         }
         dev::mma_commit(&un_empty[u]);
         dev::mma_commit(&acc_full[b]);
@@ -340,27 +343,41 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       for (int op = 0; op < 2; ++op) {
         if (op != opw) continue;  // warp-uniform: this warp transforms one operand
         const uint8_t* src = pk + op * S::PK_A + t * 64;                 // 64B-swizzled packed row
-        const uint32_t dst = dev::smem_u32(un + op * S::UN_A + t * 128);  // 128B-swizzled row
         const int z = op == 0 ? za : zb;
         const uint32_t bias4 = static_cast<uint32_t>(16 - z) * 0x01010101u;
         uint32_t hs = 0, ls = 0;  // byte lanes: sums of 16 nibbles each (<= 240, no carries)
+        uint32_t o[16];           // 64 unpacked codes: 16-byte chunks 4h .. 4h + 3 of the row
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint4 q = *reinterpret_cast<const uint4*>(src + ((j ^ ((t >> 1) & 3)) << 4));
           const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-          uint32_t o[8];
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
             const uint32_t hi = (w[x] >> 4) & 0x0f0f0f0fu;
             const uint32_t lo = w[x] & 0x0f0f0f0fu;
             hs += hi;
             ls += lo;
-            o[2 * x] = hi + bias4;      // bytes code + 16 - z in [1, 31]: no carries
-            o[2 * x + 1] = lo + bias4;
+            o[(j & 1) * 8 + 2 * x] = hi + bias4;      // bytes code + 16 - z in [1, 31]: no carries
+            o[(j & 1) * 8 + 2 * x + 1] = lo + bias4;
           }
-          const int c0 = 2 * j, c1 = 2 * j + 1;
-          dev::st_shared_v4(dst + ((c0 ^ (t & 7)) << 4), o[0], o[1], o[2], o[3]);
-          dev::st_shared_v4(dst + ((c1 ^ (t & 7)) << 4), o[4], o[5], o[6], o[7]);
+          if (j & 1) {
+            // Chunks c = 2j - 2 .. 2j + 1 (K bytes 16c ..) of the row.
+            if (op == 0) {
+              // A: TMEM lane t, columns 4c .. (four K-consecutive bytes per column).
+              dev::tmem_st_x16(tmem_base + ((static_cast<uint32_t>(t & ~31)) << 16) + S::A_COL +
+                                   static_cast<uint32_t>(u) * 32 + (j >> 1) * 16,
+                               o);
+            } else {
+              // B: the 128B-swizzled K-major shared-memory operand.
+              const uint32_t dst = dev::smem_u32(un + t * 128);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c = 2 * (j - 1) + e;
+                dev::st_shared_v4(dst + ((c ^ (t & 7)) << 4), o[4 * e], o[4 * e + 1], o[4 * e + 2],
+                                  o[4 * e + 3]);
+              }
+            }
+          }
         }
         const int codes = static_cast<int>(__dp4a(hs, 0x01010101u, __dp4a(ls, 0x01010101u, 0u)));
         const int r = codes - 128 * z;  // sum over the group of (code - z)
@@ -372,7 +389,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
 #ifdef CLOVE_TRACE
       if (xf_probe) xt2 = clock64();
 #endif
-      dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+      if (opw == 0) {
+        dev::tmem_st_wait();            // A stage written to TMEM
+        dev::tc_fence_before_sync();
+      } else {
+        dev::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+      }
 #ifdef CLOVE_TRACE
       if (xf_probe) xt3 = clock64();
 #endif
