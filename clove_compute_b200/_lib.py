@@ -51,6 +51,7 @@ SIGNATURES = {
     "clove_nsplit_destroy": ([_P], _I),
     "clove_nsplit_rank": ([_P, _P, _P], _I),
     "clove_nsplit_register_output": ([_P, _P, _SZ], _I),
+    "clove_nsplit_register_output_multicast": ([_P, _P, _P, _SZ], _I),
     "clove_nsplit_unregister_output": ([_P, _P], _I),
     "clove_nsplit_gemm_fp16": ([_P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P], _I),
     "clove_nsplit_gemm_int4": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),

@@ -520,18 +520,26 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
       }
       dev::fence_proxy_async_smem();
       __syncwarp();
+      int peer_n = 0;
       if (lane == 0) {
         dev::tma_store_2d(&tmC, stg, n0 + h * 64, m0 + static_cast<int>(q) * 32);
         // Replicated output of an N-split: the same staged slab to every rank's C,
         // once every rank is ready to receive it (none after a timeout).
-        const int peer_n = peer.count > 0 && dev::peer_ready_wait(peer, ready_e) ? peer.count : 0;
-        for (int d = 0; d < peer_n; ++d)
-          dev::tma_store_2d(&peer.maps[d], stg, peer.col0 + n0 + h * 64,
-                            m0 + static_cast<int>(q) * 32);
+        peer_n = peer.count > 0 && dev::peer_ready_wait(peer, ready_e) ? peer.count : 0;
+        if (peer.mc == 0)
+          for (int d = 0; d < peer_n; ++d)
+            dev::tma_store_2d(&peer.maps[d], stg, peer.col0 + n0 + h * 64,
+                              m0 + static_cast<int>(q) * 32);
         dev::bulk_commit_group();
         dev::bulk_wait_group<0>();
-        if (peer.count > 0) __threadfence_system();  // before the cross-rank signal
       }
+      peer_n = __shfl_sync(0xffffffffu, peer_n, 0);
+      // Multicast replicated output: the whole warp sends the staged slab once.
+      if (peer_n > 0 && peer.mc != 0)
+        dev::multicast_slab<128>(peer.mc, peer.ldc, sa_, m0 + static_cast<int>(q) * 32, M,
+                                 peer.col0, n0 + h * 64, N, lane,
+                                 [](uint32_t r, uint32_t c) { return c ^ (r & 7u); });
+      if (peer.count > 0) __threadfence_system();  // before the cross-rank signal
       __syncwarp();
     }
   }

@@ -474,12 +474,12 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (*abort_flag) break;
     }
-    if (lane == 0) {
-      dev::bulk_wait_group<0>();
-      // Replicated output: the completed remote stores are ordered before the
-      // cross-rank signal that follows the kernel on the stream.
-      if (ep.peer.count > 0) __threadfence_system();
-    }
+    if (lane == 0) dev::bulk_wait_group<0>();
+    __syncwarp();
+    // Replicated output: the completed remote stores (lane 0's TMA stores, or every
+    // lane's multicast stores) are ordered before the cross-rank signal that
+    // follows the kernel on the stream.
+    if (ep.peer.count > 0) __threadfence_system();
     __syncwarp();
   }
 

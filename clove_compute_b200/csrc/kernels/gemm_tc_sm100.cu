@@ -225,13 +225,19 @@ int encode_peer_maps(const PeerTargets& pt, int M, int N, uint32_t box_cols, int
   out->count = pt.count;
   out->col0 = pt.col0;
   out->rank = pt.rank;
+  out->ldc = pt.ldc;
+  out->mc = reinterpret_cast<unsigned long long>(pt.mc);
   out->ready_in = pt.ready_in;
   out->epoch = pt.epoch;
+  if (pt.mc != nullptr && ((reinterpret_cast<uintptr_t>(pt.mc) & 15u) != 0 || pt.ldc % 8 != 0 ||
+                           pt.col0 % 8 != 0 || N % 8 != 0))
+    return fail(CLOVE_ERR_UNSUPPORTED, "multicast output needs 16-byte aligned rows and columns");
   for (int d = 0; d < kern::kMaxPeers; ++d)
     out->ready_slot[d] = d < pt.count ? pt.ready_slot[d] : nullptr;
   for (int d = 0; d < pt.count; ++d) {
     if (d != pt.rank && pt.ready_slot[d] == nullptr)
       return fail(CLOVE_ERR_INVALID_ARG, "replicated output without its ready handshake");
+    if (pt.mc != nullptr) continue;  // one multicast store per tile instead of maps
     const int rc = encode_tmap_2d(&out->maps[d], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pt.dst[d],
                                   static_cast<uint64_t>(pt.col0) + N, M,
                                   static_cast<uint64_t>(pt.ldc) * 2, box_cols, 32, swizzle);

@@ -235,11 +235,21 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&v)[CHUNK], const Ep
       // rank's C. `ep` is the kernel's __grid_constant__ parameter here, so the
       // maps are addressed in parameter space. peer_n is ep.peer.count once the
       // warp has passed the receiver-ready handshake, 0 if that timed out.
+      if (ep.peer.mc == 0) {
 #pragma unroll 1
-      for (int d = 0; d < peer_n; ++d)
-        dev::tma_store_2d(&ep.peer.maps[d], stg, ep.peer.col0 + ncol0, store_row0);
+        for (int d = 0; d < peer_n; ++d)
+          dev::tma_store_2d(&ep.peer.maps[d], stg, ep.peer.col0 + ncol0, store_row0);
+      }
     }
     dev::bulk_commit_group();
+  }
+  if constexpr (OUT_BYTES == 2) {
+    // Multicast replicated output: the whole warp sends the staged slab once.
+    if (peer_n > 0 && ep.peer.mc != 0)
+      dev::multicast_slab<STG_ROW>(ep.peer.mc, ep.peer.ldc, stg_addr, store_row0, M, ep.peer.col0,
+                                   ncol0, N, lane, [](uint32_t r, uint32_t c) {
+                                     return swz_chunk(r, c, STG_ROW);
+                                   });
   }
   ++stg_count;
 }
@@ -625,12 +635,12 @@ __global__ void __launch_bounds__(192, 1)
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);
       if (*abort_flag) break;
     }
-    if (lane == 0) {
-      dev::bulk_wait_group<0>();
-      // Replicated output: the completed remote stores are ordered before the
-      // cross-rank signal that follows the kernel on the stream.
-      if (ep.peer.count > 0) __threadfence_system();
-    }
+    if (lane == 0) dev::bulk_wait_group<0>();
+    __syncwarp();
+    // Replicated output: the completed remote stores (lane 0's TMA stores, or every
+    // lane's multicast stores) are ordered before the cross-rank signal that
+    // follows the kernel on the stream.
+    if (ep.peer.count > 0) __threadfence_system();
     if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(8);
     if (lane == 0) CLOVE_TRACE_MAX(20);
     __syncwarp();

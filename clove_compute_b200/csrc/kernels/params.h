@@ -30,11 +30,18 @@ enum EpiMode : int {
 // ready array (ready_slot[d] = &ready_d[rank], system-scope release) and its
 // epilogue waits until every slot of its own array (ready_in) has reached
 // epoch + 1 before the first remote store (bounded, like every wait here).
+//
+// mc != 0: the ranks' C are bound to one NVLink multicast object and mc is its
+// address in this process (row pitch ldc elements). Each staged tile then leaves
+// once, as multimem stores that the NVSwitch fabric delivers to every rank's C
+// (this rank's included); the maps are unused.
 constexpr int kMaxPeers = 8;
 struct PeerOut {
   int count;
   int col0;
   int rank;
+  int ldc;
+  unsigned long long mc;
   unsigned long long* ready_slot[kMaxPeers];
   const unsigned long long* ready_in;
   const unsigned long long* epoch;

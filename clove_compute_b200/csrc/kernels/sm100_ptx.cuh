@@ -637,6 +637,40 @@ __device__ __forceinline__ unsigned long long peer_ready_publish(const PeerOutT&
     if (d != po.rank) st_release_sys_u64(po.ready_slot[d], e);
   return e;
 }
+// 16 bytes to every device bound to the multicast object behind `mc` (an address
+// of the multicast mapping, 16-byte aligned); plain data movement, bit-exact.
+__device__ __forceinline__ void multimem_st_v4(unsigned long long mc, uint32_t a, uint32_t b,
+                                               uint32_t c, uint32_t d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// A warp's staged slab of rows [row0, row0 + 32) x bytes [0, row_bytes) of a
+// row-major fp16 tile (16-byte chunks swizzled with `swz(row, chunk)`), written to
+// the multicast C at (row0 + r, col0 + 8 chunk): consecutive lanes take consecutive
+// chunks of a row, so each row leaves as one contiguous run. Rows >= rows and
+// columns >= cols (the local tile's extent) are not stored.
+template <int ROW_BYTES, class Swz>
+__device__ __forceinline__ void multicast_slab(unsigned long long mc, int ldc, uint32_t stg_addr,
+                                               int row0, int rows, int col0, int ncol0, int cols,
+                                               uint32_t lane, Swz swz) {
+  constexpr int PKTS = ROW_BYTES / 16;
+#pragma unroll
+  for (int it = 0; it < PKTS; ++it) {
+    const int i = it * 32 + static_cast<int>(lane);
+    const int r = i / PKTS, c = i % PKTS;
+    if (row0 + r < rows && ncol0 + 8 * c < cols) {
+      uint32_t v0, v1, v2, v3;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                   : "r"(stg_addr + r * ROW_BYTES + swz(r, c) * 16));
+      multimem_st_v4(mc + (static_cast<unsigned long long>(row0 + r) * ldc + col0 + ncol0 + 8 * c) * 2,
+                     v0, v1, v2, v3);
+    }
+  }
+}
+
 template <class PeerOutT>
 __device__ __forceinline__ bool peer_ready_wait(const PeerOutT& po, unsigned long long e) {
   bool ok = true;

@@ -55,11 +55,14 @@ bool ws2_selected();
 // receiver-ready handshake (kern::PeerOut) uses ready_slot[q] = slot `rank` of
 // rank q's ready array, ready_in = this rank's ready array and epoch = this
 // rank's count of completed replicated calls.
+// mc: the multicast address of every rank's C (one NVLink multicast object bound
+// to all of them), or null for per-rank stores through dst.
 struct PeerTargets {
   int count;
   int ldc;
   int col0;
   int rank;
+  void* mc;
   void* dst[8];
   unsigned long long* ready_slot[8];
   const unsigned long long* ready_in;

@@ -76,6 +76,7 @@ constexpr size_t kFlagBytes = sizeof(unsigned long long) * (2 * kMaxPeers + 1);
 struct SharedBuf {
   void* local = nullptr;
   size_t bytes = 0;
+  void* mc = nullptr;            // multicast address of every rank's buffer (else null)
   void* opened[kMaxPeers] = {};  // IPC mapping bases (to close), null for this rank
   void* ptr[kMaxPeers] = {};     // every rank's buffer as seen from this process
 };
@@ -389,6 +390,7 @@ PeerTargets peer_targets(const clove_nsplit_ctx* ctx, const SharedBuf& out, int 
   peer.ldc = N;
   peer.col0 = clove_nsplit_col_begin(N, ctx->nranks, ctx->rank);
   peer.rank = ctx->rank;
+  peer.mc = out.mc;
   unsigned long long* own = static_cast<unsigned long long*>(ctx->flags.local);
   peer.ready_in = own + kFlagReady;
   peer.epoch = own + kFlagEpoch;
@@ -538,6 +540,70 @@ int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t byt
     ctx->flags = flags;
     ctx->flags_ready = true;
   }
+  ctx->outputs.push_back(out);
+  return CLOVE_OK;
+}
+
+// The same collective for a C_full that the caller has bound, on every rank, to one
+// NVLink multicast object (e.g. symmetric memory with a multicast mapping): mc is
+// that object's address for this rank's C_full. No IPC mapping of C_full is made;
+// the handshake flags are shared as for clove_nsplit_register_output.
+int clove_nsplit_register_output_multicast(clove_nsplit_ctx* ctx, void* C_full, void* mc,
+                                           size_t bytes) {
+  if (ctx == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "ctx is NULL");
+  ctx->ipc_used = true;
+  const size_t fb = kFlagBytes;
+  int lrc = CLOVE_OK;
+  if (C_full == nullptr || mc == nullptr || bytes == 0)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "bad register_output_multicast arguments");
+  else if (ctx->nranks > kMaxPeers)
+    lrc = fail(CLOVE_ERR_UNSUPPORTED, "replicated output supports up to %d ranks", kMaxPeers);
+  else if (((reinterpret_cast<uintptr_t>(C_full) | reinterpret_cast<uintptr_t>(mc)) & 15u) != 0)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "replicated C and its multicast address must be 16-byte aligned");
+  else if (find_output(ctx, C_full) != nullptr)
+    lrc = fail(CLOVE_ERR_INVALID_ARG, "buffer already registered");
+  if (!lrc && ctx->flags_mem == nullptr) {
+    void* f = nullptr;
+    lrc = check_cuda(cudaMalloc(&f, fb), "cudaMalloc(flags)");
+    if (!lrc) lrc = check_cuda(cudaMemset(f, 0, fb), "cudaMemset(flags)");
+    if (!lrc) lrc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(flags)");
+    if (!lrc)
+      ctx->flags_mem = f;
+    else if (f)
+      cudaFree(f);
+  }
+  struct Entry {
+    IpcRecord flags;
+    unsigned long long bytes;
+    int status;
+  } mine = {};
+  if (!lrc) lrc = make_record(ctx->flags_mem, fb, &mine.flags);
+  mine.bytes = bytes;
+  mine.status = lrc == CLOVE_OK ? 1 : 0;
+  std::vector<Entry> all(ctx->nranks);
+  int rc = all_gather_host(ctx, &mine, sizeof(Entry), all.data());
+  if (rc) return rc;
+  bool ok = true;
+  for (const Entry& e : all) ok = ok && e.status == 1 && e.bytes == bytes;
+  if (!ok) return lrc ? lrc : fail(CLOVE_ERR_INVALID_ARG, "another rank could not register");
+  SharedBuf flags;
+  std::vector<IpcRecord> fr(ctx->nranks);
+  for (int q = 0; q < ctx->nranks; ++q) fr[q] = all[q].flags;
+  int orc = CLOVE_OK;
+  if (!ctx->flags_ready) orc = open_shared(ctx, ctx->flags_mem, fb, fr.data(), &flags);
+  if (!all_ok(ctx, orc == CLOVE_OK)) {
+    if (flags.local != nullptr) close_shared(ctx, &flags);
+    return orc ? orc : fail(CLOVE_ERR_CUDA, "another rank could not map the shared buffers");
+  }
+  if (!ctx->flags_ready) {
+    ctx->flags = flags;
+    ctx->flags_ready = true;
+  }
+  SharedBuf out;
+  out.local = C_full;
+  out.bytes = bytes;
+  out.mc = mc;
+  for (int q = 0; q < ctx->nranks; ++q) out.ptr[q] = q == ctx->rank ? C_full : nullptr;
   ctx->outputs.push_back(out);
   return CLOVE_OK;
 }

@@ -6,9 +6,11 @@ single-GPU kernel on its shard; with ``replicate_C`` the shards are all-gathered
 over NCCL (NVLink) into the full row-major C on every rank. A C registered with
 ``register_output`` (a collective that maps it into every rank through CUDA IPC)
 is instead filled by the GEMM's own epilogue (fp16, INT8 row/col, INT4), which stores each
-finished tile into every rank's copy over NVLink. The NCCL communicator belongs to the C
-library; its unique id is exchanged through the torch.distributed store of the
-already-initialised process group.
+finished tile into every rank's copy over NVLink. A C from ``multicast_output`` (CUDA
+symmetric memory bound to one NVLink multicast object) takes the same route with one
+multicast store per tile, which the NVSwitch fabric delivers to every rank. The NCCL
+communicator belongs to the C library; its unique id is exchanged through the
+torch.distributed store of the already-initialised process group.
 """
 from __future__ import annotations
 
@@ -68,6 +70,29 @@ class NSplit:
             raise err
         check(rc)
         self._outputs[C_full.data_ptr()] = C_full  # keeps the memory alive while mapped
+
+    def multicast_output(self, M: int, N: int, group=None) -> torch.Tensor:
+        """Collective: an [M, N] fp16 replicated output in CUDA symmetric memory, every
+        rank's copy bound to one NVLink multicast object, registered for the
+        replicated route (each finished tile then leaves once, as multicast stores).
+        Raises on every rank when any rank's GPU offers no multicast. Release with
+        ``unregister_output`` on every rank."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        g = group if group is not None else dist.group.WORLD
+        C = symm_mem.empty((int(M), int(N)), dtype=torch.float16,
+                           device=torch.device("cuda", torch.cuda.current_device()))
+        handle = symm_mem.rendezvous(C, g)
+        mc = int(getattr(handle, "multicast_ptr", 0) or 0)
+        # Every rank calls the registration (a rank without multicast passes NULL,
+        # which fails it on every rank) so that no rank waits alone.
+        rc = lib().clove_nsplit_register_output_multicast(
+            self._ctx, C.data_ptr(), mc if mc else None, C.numel() * C.element_size())
+        if rc != 0:
+            del handle, C
+            check(rc)
+        self._outputs[C.data_ptr()] = (C, handle)  # keeps memory and binding alive
+        return C
 
     def unregister_output(self, C_full: torch.Tensor) -> None:
         """Collective: unmaps C_full on every rank."""

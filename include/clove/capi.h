@@ -245,6 +245,16 @@ int clove_nsplit_rank(const clove_nsplit_ctx* ctx, int* rank, int* nranks);
  * No host barrier is needed between calls.
  * (Extension; no counterpart in the reference.) */
 int clove_nsplit_register_output(clove_nsplit_ctx* ctx, void* C_full, size_t bytes);
+/* Collective, as clove_nsplit_register_output, for a C_full that every rank has
+ * bound to one NVLink multicast object (NVSwitch; e.g. CUDA symmetric memory with a
+ * multicast mapping): mc is the multicast object's address in this process (the
+ * mapping of C_full, 16-byte aligned). The replicated route then sends each finished
+ * tile once, as multimem stores that the switch fabric delivers to every rank's
+ * C_full, instead of one store per rank; same shapes, same ordering contract. The
+ * caller keeps the binding alive until clove_nsplit_unregister_output returns on
+ * every rank. (Extension; no counterpart in the reference.) */
+int clove_nsplit_register_output_multicast(clove_nsplit_ctx* ctx, void* C_full, void* mc,
+                                           size_t bytes);
 /* Collective: unmaps C_full everywhere; returns once no rank maps it any more. */
 int clove_nsplit_unregister_output(clove_nsplit_ctx* ctx, void* C_full);
 

@@ -330,3 +330,121 @@ def test_nsplit_replicated_output_back_to_back_two_gpus(clove_lib, cuda):
         # Every call's copy holds that call's product: a result overwritten by the
         # next call's stores (or a tile left NaN) fails here.
         assert all(e < 2e-3 for e in errs), res[r]
+
+
+def _worker_multicast(rank, world, port, q):
+    """The replicated route with a multicast C_full (CUDA symmetric memory bound to one
+    NVLink multicast object): each tile leaves once as multicast stores. Back-to-back
+    calls with a lagging reader on rank 1, as above, for fp16 (CTA-pair kernel) and
+    INT4; every call's copy must hold that call's product on every rank."""
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import clove_compute_b200 as cc
+        import oracle
+        from clove_compute_b200 import workloads as wl
+        ns = cc.NSplit(rank, world)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        lag = 2_000_000
+        out = []
+        try:
+            probe = ns.multicast_output(128, 128)
+        except Exception as e:  # the same on every rank: registration is collective
+            ns.close()
+            q.put((rank, "skip", "no multicast: " + repr(e)[:200]))
+            return
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.unregister_output(probe)
+        del probe
+
+        calls = 8
+        M, N, K = 1024, 1024, 512
+        A, _ = wl.fp16_operands(M, N, K, seed=5)
+        Bs = [wl.fp16_operands(M, N, K, seed=400 + i)[1] for i in range(calls)]
+        c0, c1 = ns.cols(N)
+        Ad = t(A)
+        Bsh = [t(B[:, c0:c1]) for B in Bs]
+        C_full = ns.multicast_output(M, N)
+        C_full.fill_(float("nan"))
+        hist = torch.empty((calls, M, N), dtype=torch.float16, device="cuda")
+        torch.cuda.synchronize()
+        dist.barrier()
+        for i in range(calls):
+            ns.gemm_fp16(Ad, Bsh[i], N, C_full=C_full, replicate_C=True)
+            if rank == 1:
+                torch.cuda._sleep(lag)
+            hist[i].copy_(C_full)
+        torch.cuda.synchronize()
+        h = hist.cpu().numpy().astype(np.float64)
+        for i in range(calls):
+            ref = oracle.gemm_fp16(A, Bs[i])
+            out.append(float(np.linalg.norm(h[i] - ref) / np.linalg.norm(ref)))
+        dist.barrier()
+        ns.unregister_output(C_full)
+        del C_full
+
+        calls = 4
+        M, N, K = 256, 512, 2048
+        ops = [wl.int4_operands(M, N, K, seed=500 + i) for i in range(calls)]
+        c0, c1 = ns.cols(N)
+        Aq, As, Az = t(ops[0].A_q), t(ops[0].A_scale), t(ops[0].A_zero)
+        Bq = [(t(o.B_q[c0:c1]), t(o.B_scale[c0:c1]), t(o.B_zero[c0:c1])) for o in ops]
+        C_full = ns.multicast_output(M, N)
+        C_full.fill_(float("nan"))
+        hist = torch.empty((calls, M, N), dtype=torch.float16, device="cuda")
+        torch.cuda.synchronize()
+        dist.barrier()
+        for i in range(calls):
+            ns.gemm_int4(Aq, As, Az, *Bq[i], N, C_full=C_full, replicate_C=True)
+            if rank == 1:
+                torch.cuda._sleep(lag)
+            hist[i].copy_(C_full)
+        torch.cuda.synchronize()
+        h = hist.cpu().numpy().astype(np.float64)
+        o0 = ops[0]
+        for i, o in enumerate(ops):
+            ref = oracle.gemm_int4(o0.A_q, o0.A_scale, o0.A_zero, o.B_q, o.B_scale, o.B_zero, K)
+            out.append(float(np.linalg.norm(h[i] - ref) / np.linalg.norm(ref)))
+        dist.barrier()
+        ns.unregister_output(C_full)
+        del C_full
+        err = cc.device_error()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.close()
+        q.put((rank, "ok", out + [float(err)]))
+    except Exception as e:
+        q.put((rank, "error", repr(e)[:300]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nsplit_multicast_output_two_gpus(clove_lib, cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_multicast, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (k, v)) for r, k, v in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    if all(res[r][0] == "skip" for r in range(2)):
+        pytest.skip(res[0][1])
+    for r in range(2):
+        assert res[r][0] == "ok", res[r]
+        errs, dev_err = res[r][1][:-1], res[r][1][-1]
+        assert dev_err == 0, res[r]
+        assert all(e < 2e-3 for e in errs), res[r]
