@@ -547,13 +547,32 @@ def _secondary(cc, torch, peaks):
     return out
 
 
-def _replicated(cc, torch, dist, world, rank, wl, np):
+def _multicast_out(ns, torch, dist, M, N):
+    """Collective: a multicast-bound replicated output ([M, N] fp16), or (None, why)
+    on every rank when any rank cannot have one."""
+    C, err = None, ""
+    try:
+        C = ns.multicast_output(M, N)
+    except Exception as e:  # raised on every rank: the registration is collective
+        err = repr(e)[:200]
+    ok = torch.tensor([1 if C is not None else 0], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not ok.item() and C is not None:
+        torch.cuda.synchronize()
+        ns.unregister_output(C)
+        C = None
+    return C, err or ("" if ok.item() else "another rank has no multicast")
+
+
+def _replicated(cc, torch, dist, world, rank, wl, np, multicast=False):
     """Config 4's FFN up (11008 x 2048 x 4096) split over the ranks' token columns with
     the output C [11008, 2048] replicated on every rank, and config 5's INT4 8192^3
     with the weight rows sharded and C [8192, 8192] replicated: the shard GEMM alone,
     the GEMM whose epilogue stores every tile into all ranks' C (registered output,
-    CUDA IPC over NVLink), and the shard GEMM + NCCL all-gather + re-layout. Per
-    call, device time (CUDA events, max over ranks), median of 3 batches."""
+    CUDA IPC over NVLink), with `multicast` the same epilogue sending each tile once
+    to an NVLink multicast object bound to every rank's C, and the shard GEMM + NCCL
+    all-gather + re-layout. Per call, device time (CUDA events, max over ranks),
+    median of 3 batches."""
     M, N, K = UP
     ns = cc.NSplit(rank, world)
     c0, c1 = ns.cols(N)
@@ -577,6 +596,10 @@ def _replicated(cc, torch, dist, world, rank, wl, np):
     if ok.item():
         fns["epilogue_to_peers"] = lambda: ns.gemm_fp16(A, Bs, N, C_shard=Cs, C_full=Cf,
                                                         replicate_C=True)
+    Cm, merr = _multicast_out(ns, torch, dist, M, N) if multicast else (None, "")
+    if Cm is not None:
+        fns["epilogue_multicast"] = lambda: ns.gemm_fp16(A, Bs, N, C_shard=Cs, C_full=Cm,
+                                                         replicate_C=True)
     times = {k: [] for k in fns}
     for _ in range(3):
         for k, fn in fns.items():
@@ -607,6 +630,16 @@ def _replicated(cc, torch, dist, world, rank, wl, np):
         ns.unregister_output(Cf)
     else:
         out["epilogue_to_peers"] = f"unavailable: {err or 'another rank could not register'}"
+    if Cm is not None:
+        same = torch.tensor([1 if torch.equal(Cn, Cm) else 0], device="cuda")
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        out["multicast_equals_all_gather"] = bool(same.item())
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.unregister_output(Cm)
+        del Cm
+    elif multicast:
+        out["epilogue_multicast"] = f"unavailable: {merr}"
     del A, B, Bs, Cs, Cn, Cf
     # Config 5: INT4 8192^3 with B's rows (weights) sharded, C [8192, 8192] replicated.
     n = 8192
@@ -631,6 +664,10 @@ def _replicated(cc, torch, dist, world, rank, wl, np):
     if ok4.item():
         fns["epilogue_to_peers"] = lambda: ns.gemm_int4(*a4, *b4, n, C_shard=Cs, C_full=Cf,
                                                         replicate_C=True)
+    Cm, merr = _multicast_out(ns, torch, dist, n, n) if multicast else (None, "")
+    if Cm is not None:
+        fns["epilogue_multicast"] = lambda: ns.gemm_int4(*a4, *b4, n, C_shard=Cs, C_full=Cm,
+                                                         replicate_C=True)
     times = {k: [] for k in fns}
     for _ in range(3):
         for k, fn in fns.items():
@@ -658,6 +695,16 @@ def _replicated(cc, torch, dist, world, rank, wl, np):
         ns.unregister_output(Cf)
     else:
         out4["epilogue_to_peers"] = f"unavailable: {err4 or 'another rank could not register'}"
+    if Cm is not None:
+        same = torch.tensor([1 if torch.equal(Cn, Cm) else 0], device="cuda")
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        out4["multicast_equals_all_gather"] = bool(same.item())
+        torch.cuda.synchronize()
+        dist.barrier()
+        ns.unregister_output(Cm)
+        del Cm
+    elif multicast:
+        out4["epilogue_multicast"] = f"unavailable: {merr}"
     out["int4_8192_config5"] = out4
     out["device_error"] = cc.device_error()
     ns.close()
@@ -999,7 +1046,7 @@ def run_gpu(args):
     if world == 1 and rank == 0 and not args.no_secondary:
         line["secondary"] = _secondary(cc, torch, peaks)
     if world > 1 and not args.no_secondary:
-        rep = _replicated(cc, torch, dist, world, rank, wl, np)  # collective: every rank
+        rep = _replicated(cc, torch, dist, world, rank, wl, np, multicast=args.multicast)  # collective: every rank
         if rank == 0:
             line["replicated_output"] = rep
     if not args.no_secondary:
@@ -1023,6 +1070,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["clove", "reference"], default="clove")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--multicast", action="store_true",
+                    help="N > 1: also time the replicated output through an NVLink multicast object")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096",
                                        "attention"],
