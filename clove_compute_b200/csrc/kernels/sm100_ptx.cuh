@@ -652,7 +652,7 @@ __device__ __forceinline__ void multimem_st_v4(unsigned long long mc, uint32_t a
 // chunks of a row, so each row leaves as one contiguous run. Rows >= rows and
 // columns >= cols (the local tile's extent) are not stored.
 template <int ROW_BYTES, class Swz>
-__device__ __forceinline__ void multicast_slab(unsigned long long mc, int ldc, uint32_t stg_addr,
+__device__ __noinline__ void multicast_slab(unsigned long long mc, int ldc, uint32_t stg_addr,
                                                int row0, int rows, int col0, int ncol0, int cols,
                                                uint32_t lane, Swz swz) {
   constexpr int PKTS = ROW_BYTES / 16;
