@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
           dev::tma_store_4d(&tmO, stg, 0, r0, head, batch);
           dev::tma_store_4d(&tmO, stg + 4096, 64, r0, head, batch);
           dev::bulk_commit_group();
-          dev::bulk_wait_group<0>();
+          dev::bulk_wait_group_read<0>();  // source read before exit; writes complete with the grid
         }
         __syncwarp();
       }

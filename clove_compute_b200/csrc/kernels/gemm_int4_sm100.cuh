@@ -531,7 +531,12 @@ __global__ void __launch_bounds__(I4Shape::THREADS, 1)
             dev::tma_store_2d(&peer.maps[d], stg, peer.col0 + n0 + h * 64,
                               m0 + static_cast<int>(q) * 32);
         dev::bulk_commit_group();
-        dev::bulk_wait_group<0>();
+        // Shared-memory source read before exit; the global writes themselves only
+        // when a cross-rank signal follows (replicated output).
+        if (peer.count > 0)
+          dev::bulk_wait_group<0>();
+        else
+          dev::bulk_wait_group_read<0>();
       }
       peer_n = __shfl_sync(0xffffffffu, peer_n, 0);
       // Multicast replicated output: the whole warp sends the staged slab once.

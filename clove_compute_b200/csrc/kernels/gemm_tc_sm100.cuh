@@ -635,11 +635,18 @@ __global__ void __launch_bounds__(192, 1)
       if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(7);
       if (*abort_flag) break;
     }
-    if (lane == 0) dev::bulk_wait_group<0>();
+    // Before the CTA exits its TMA stores must have read their shared-memory source
+    // (their global writes complete with the grid). A replicated output waits for the
+    // writes themselves: the remote stores (lane 0's TMA stores, or every lane's
+    // multicast stores) are ordered before the cross-rank signal that follows the
+    // kernel on the stream.
+    if (lane == 0) {
+      if (ep.peer.count > 0)
+        dev::bulk_wait_group<0>();
+      else
+        dev::bulk_wait_group_read<0>();
+    }
     __syncwarp();
-    // Replicated output: the completed remote stores (lane 0's TMA stores, or every
-    // lane's multicast stores) are ordered before the cross-rank signal that
-    // follows the kernel on the stream.
     if (ep.peer.count > 0) __threadfence_system();
     if (warp == 2 && lane == 0) CLOVE_TRACE_POINT(8);
     if (lane == 0) CLOVE_TRACE_MAX(20);
