@@ -325,36 +325,49 @@ def _secondary(cc, torch, peaks):
             "note": "clove_debug_stream_read of the same byte count, one launch per call: the "
                     "bandwidth a single kernel of this size reaches, without any math"}}
 
+    def decode_case(Mx, Kx, seed, n_copies, note):
+        """One INT4 decode call (N = 1) with Mx x Kx weights: plain, with weight
+        prefetch, and against the bare read of the same bytes."""
+        opx = wl.int4_operands(Mx, 1, Kx, seed=seed)
+        Aqx = [dev(opx.A_q) for _ in range(n_copies)]
+        Asx = [dev(opx.A_scale) for _ in range(n_copies)]
+        Azx = [dev(opx.A_zero) for _ in range(n_copies)]
+        Bqx, Bsx, Bzx = dev(opx.B_q), dev(opx.B_scale), dev(opx.B_zero)
+        Cx = torch.empty((Mx, 1), dtype=torch.float16, device="cuda")
+        tx = timeit(lambda i: cc.gemm_int4(Aqx[i], Asx[i], Azx[i], Bqx, Bsx, Bzx, Cx), n_copies, 200)
+        cc.set_weight_prefetch(True)
+        tx_pf = timeit(lambda i: cc.gemm_int4(Aqx[i], Asx[i], Azx[i], Bqx, Bsx, Bzx, Cx),
+                       n_copies, 200)
+        cc.set_weight_prefetch(False)
+        nbx = Mx * Kx // 2 + 2 * 2 * Mx * Kx // 128 + Kx // 2 + 2 * 2 * Kx // 128 + 2 * Mx
+        del Aqx, Asx, Azx
+        tx_floor = read_floor(nbx, n_copies)
+        return {
+            "kernel": cc.describe_dispatch("int4", Mx, 1, Kx), "us_per_call": round(tx * 1e6, 3),
+            "GBps": round(nbx / tx / 1e9, 1), "bytes_per_call": nbx,
+            "roofline": {"bound": "hbm", "achieved": round(nbx / tx / 1e9, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(nbx / tx / 1e9 / peaks["hbm_gbs"], 4)},
+            "weight_prefetch": {"us_per_call": round(tx_pf * 1e6, 3),
+                                "GBps": round(nbx / tx_pf / 1e9, 1),
+                                "frac": round(nbx / tx_pf / 1e9 / peaks["hbm_gbs"], 4)},
+            "read_floor": {"us_per_call": round(tx_floor * 1e6, 3),
+                           "GBps": round(nbx / tx_floor / 1e9, 1),
+                           "decode_over_floor": round(tx / tx_floor, 3)},
+            "note": note}
+
     # Grouped decode: Q, K and V projection weights of one layer concatenated by rows
     # (W_qkv [3 * 4096, 4096], INTEGRATION.md) and streamed by one gemm_int4 call,
-    # N = 1; same distributions as config 2.
-    M3 = 3 * 4096
-    op3 = wl.int4_operands(M3, 1, K, seed=3)
-    copies3 = 16
-    Aq3 = [dev(op3.A_q) for _ in range(copies3)]
-    As3 = [dev(op3.A_scale) for _ in range(copies3)]
-    Az3 = [dev(op3.A_zero) for _ in range(copies3)]
-    Bq3, Bs3, Bz3 = dev(op3.B_q), dev(op3.B_scale), dev(op3.B_zero)
-    C3 = torch.empty((M3, 1), dtype=torch.float16, device="cuda")
-    t3 = timeit(lambda i: cc.gemm_int4(Aq3[i], As3[i], Az3[i], Bq3, Bs3, Bz3, C3), copies3, 200)
-    cc.set_weight_prefetch(True)
-    t3_pf = timeit(lambda i: cc.gemm_int4(Aq3[i], As3[i], Az3[i], Bq3, Bs3, Bz3, C3), copies3, 200)
-    cc.set_weight_prefetch(False)
-    nb3 = M3 * K // 2 + 2 * 2 * M3 * K // 128 + K // 2 + 2 * 2 * K // 128 + 2 * M3
-    del Aq3, As3, Az3
-    t3_floor = read_floor(nb3, copies3)
-    out["int4_decode_qkv_3x4096x4096"] = {
-        "kernel": cc.describe_dispatch("int4", M3, 1, K), "us_per_call": round(t3 * 1e6, 3),
-        "GBps": round(nb3 / t3 / 1e9, 1), "bytes_per_call": nb3,
-        "roofline": {"bound": "hbm", "achieved": round(nb3 / t3 / 1e9, 1),
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(nb3 / t3 / 1e9 / peaks["hbm_gbs"], 4)},
-        "weight_prefetch": {"us_per_call": round(t3_pf * 1e6, 3),
-                            "GBps": round(nb3 / t3_pf / 1e9, 1),
-                            "frac": round(nb3 / t3_pf / 1e9 / peaks["hbm_gbs"], 4)},
-        "read_floor": {"us_per_call": round(t3_floor * 1e6, 3),
-                       "decode_over_floor": round(t3 / t3_floor, 3)},
-        "note": "W_q, W_k, W_v [4096, 4096] concatenated by rows: one launch, M = 12288, N = 1"}
+    # N = 1; same distributions as config 2. Then the Llama-7B MLP's decode GEMVs:
+    # gate and up concatenated by rows ([2 * 11008, 4096]) and down ([4096, 11008],
+    # 86 groups per row).
+    out["int4_decode_qkv_3x4096x4096"] = decode_case(
+        3 * 4096, 4096, 3, 16,
+        "W_q, W_k, W_v [4096, 4096] concatenated by rows: one launch, M = 12288, N = 1")
+    out["int4_decode_gate_up_22016x4096"] = decode_case(
+        2 * 11008, 4096, 4, 6, "W_gate, W_up [11008, 4096] concatenated by rows, N = 1")
+    out["int4_decode_down_4096x11008"] = decode_case(
+        4096, 11008, 5, 12, "W_down [4096, 11008] (86 groups per row), N = 1")
 
     # config 3: int8 batch-32 with per-row / per-column scales
     M, N, K = 4096, 32, 4096
@@ -838,11 +851,14 @@ def _summary(line):
                                    "over_floor": d["read_floor"]["decode_over_floor"],
                                    "prefetch_us": d["weight_prefetch"]["us_per_call"],
                                    "prefetch_frac": d["weight_prefetch"]["frac"]}
-    gq = sec.get("int4_decode_qkv_3x4096x4096")
-    if gq:
-        out["decode_int4_qkv"] = {"us": gq["us_per_call"], "GBps": gq["GBps"],
-                                  "frac": gq["roofline"]["frac"],
-                                  "prefetch_frac": gq["weight_prefetch"]["frac"]}
+    for key, name in (("int4_decode_qkv_3x4096x4096", "decode_int4_qkv"),
+                      ("int4_decode_gate_up_22016x4096", "decode_int4_gate_up"),
+                      ("int4_decode_down_4096x11008", "decode_int4_down")):
+        gq = sec.get(key)
+        if gq:
+            out[name] = {"us": gq["us_per_call"], "GBps": gq["GBps"],
+                         "frac": gq["roofline"]["frac"],
+                         "prefetch_frac": gq["weight_prefetch"]["frac"]}
     b = sec.get("int8_batch32_4096x32x4096")
     if b:
         out["int8_batch32"] = {"us": b["us_per_call"], "GBps": b["GBps"],

@@ -107,6 +107,9 @@ template <int NC, int PW>
 int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                   const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
                   long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
+  // Rows per warp and round: 8, or 4 when three windows per lane (K up to 12288)
+  // would not leave the registers for 8.
+  constexpr int RMAX = PW > 2 ? 4 : 8;
   int grid = dev.num_sms;
   if (rows < grid * 8) grid = (rows + 7) / 8;
   cudaLaunchConfig_t cfg = {};
@@ -121,7 +124,7 @@ int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8
   cfg.numAttrs = 1;
   const int early = weight_prefetch_enabled() ? 1 : 0;
   return check_cuda(
-      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, 8>, Aq,
+      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, RMAX>, Aq,
                          static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
                          static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
                          static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),
@@ -218,17 +221,18 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
                      int K, long long ldc_row, long long ldc_col, long long ldg_row,
                      long long ldg_col, const DeviceInfo& dev, cudaStream_t stream) {
   // Register-resident B when this lane's share of the vectors fits (nc * P <= 8,
-  // P = 1024-element windows per row) and the 16-byte B loads are aligned.
+  // P = 1024-element windows per row, the last one possibly partial) and the
+  // 16-byte B loads are aligned.
   const int P = (K + 1023) / 1024;
-  // Whole 1024-element windows, 16-byte aligned rows of codes, scales and zero
-  // points (K % 1024 == 0), no debug output.
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (Gdbg == nullptr && K % 1024 == 0 && K <= 24576 && nc * P <= 8 && a16(Aq) && a16(As) &&
-      a16(Az) && a16(Bq) && !ws_disabled()) {
+  // Direct 128-bit loads (gemv_int4_ldg_kernel): whole 128-code groups (16-byte
+  // aligned rows of codes), up to 8 windows per vector (12 for one vector), no
+  // debug output. The bulk-copy ring variant (gemv_int4_ws2_kernel, whole windows
+  // only) stays reachable through the test override.
+  if (Gdbg == nullptr && K % 128 == 0 && (nc * P <= 8 || (nc == 1 && P <= 12)) && a16(Aq) &&
+      a16(As) && a16(Az) && a16(Bq) && !ws_disabled()) {
     const int PW = (P + kern::kWs2WindowGroups - 1) / kern::kWs2WindowGroups;
-    // Direct 128-bit loads (gemv_int4_ldg_kernel); the bulk-copy ring variant
-    // (gemv_int4_ws2_kernel) stays reachable through the test override.
-    if (ws2_selected()) {
+    if (ws2_selected() && K % 1024 == 0) {
 #define WS2(n, pw)                                                                            \
   if (nc == n && PW == pw)                                                                     \
     return gemv_int4_ws2<n, pw>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
@@ -238,7 +242,7 @@ int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const ui
 #define LDG(n, pw)                                                                            \
   if (nc == n && PW == pw)                                                                     \
     return gemv_int4_ldg<n, pw>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row, ldc_col, dev, stream);
-    LDG(1, 1) LDG(1, 2) LDG(2, 1)
+    LDG(1, 1) LDG(1, 2) LDG(1, 3) LDG(2, 1)
 #undef LDG
   }
   if (nc * P <= 8 && (reinterpret_cast<uintptr_t>(Bq) & 15u) == 0) {

@@ -561,11 +561,12 @@ __global__ void __launch_bounds__(kLdgThreads, 1)
                          const __half* __restrict__ Bs, const __half* __restrict__ Bz,
                          __half* __restrict__ C, int rows, int K, long long ldc_row,
                          long long ldc_col, int weights_early) {
-  static_assert(RMAX == 8, "the transposed butterfly reduces 8 row partials");
+  static_assert(RMAX == 8 || RMAX == 4, "the transposed butterfly reduces 8 or 4 row partials");
   constexpr int ROWS = kLdgRowGroups * RMAX;  // rows of the block per round
   __shared__ float part[ROWS][kLdgWindowGroups][NC];
   const int NG = K >> 7;
-  const int P = K >> 10;
+  const int P = (K + 1023) >> 10;  // 1024-code windows, the last one possibly partial
+  const int KC = K >> 5;           // 16-byte chunks of a row (32 codes each)
   const int KB = K >> 1;
   const int warp = static_cast<int>(dev::warp_idx());
   const int lane = static_cast<int>(dev::lane_idx());
@@ -587,9 +588,9 @@ __global__ void __launch_bounds__(kLdgThreads, 1)
 #pragma unroll
       for (int pw = 0; pw < PW; ++pw) {
         const int p = wg + kLdgWindowGroups * pw;
-        if (rl < nrows && p < P) {
+        const int ch = p * 32 + lane;
+        if (rl < nrows && p < P && ch < KC) {
           const size_t m = static_cast<size_t>(r0 + rl);
-          const int ch = p * 32 + lane;
           a[i][pw] = dev::ld_nc_v4(Aq + m * KB + static_cast<size_t>(ch) * 16);
           const size_t gi = m * NG + (ch >> 2);
           zs[i][pw] = __halves2half2(Az[gi], As[gi]);
@@ -615,7 +616,8 @@ __global__ void __launch_bounds__(kLdgThreads, 1)
       uint4 q = make_uint4(0u, 0u, 0u, 0u);
       int zb = 0;
       bsc[n][pw] = 0.f;
-      if (p < P) {
+      const bool valid = p < P && ch < KC;  // lanes past K (partial last window) add 0
+      if (valid) {
         q = *reinterpret_cast<const uint4*>(Bq + static_cast<size_t>(n) * KB + static_cast<size_t>(ch) * 16);
         zb = __half2int_rn(Bz[static_cast<size_t>(n) * NG + (ch >> 2)]);
         bsc[n][pw] = __half2float(Bs[static_cast<size_t>(n) * NG + (ch >> 2)]);
@@ -630,7 +632,7 @@ __global__ void __launch_bounds__(kLdgThreads, 1)
         sum = __dp4a(static_cast<int>(bw[n][pw][2 * u]), 0x01010101, sum);
         sum = __dp4a(static_cast<int>(bw[n][pw][2 * u + 1]), 0x01010101, sum);
       }
-      bsum[n][pw] = p < P ? sum : 0;
+      bsum[n][pw] = valid ? sum : 0;
     }
 
   const bool b4 = (lane & 16) != 0;
@@ -665,23 +667,40 @@ __global__ void __launch_bounds__(kLdgThreads, 1)
     if (base + ROWS < nrows) load_round(base + ROWS);
 #pragma unroll
     for (int n = 0; n < NC; ++n) {
-      float x[4], y[2];
+      if constexpr (RMAX == 8) {
+        float x[4], y[2];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float keep = b4 ? v[4 + q][n] : v[q][n];
-        const float send = b4 ? v[q][n] : v[4 + q][n];
-        x[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-      }
+        for (int q = 0; q < 4; ++q) {
+          const float keep = b4 ? v[4 + q][n] : v[q][n];
+          const float send = b4 ? v[q][n] : v[4 + q][n];
+          x[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const float keep = b3 ? x[2 + q] : x[q];
-        const float send = b3 ? x[q] : x[2 + q];
-        y[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        for (int q = 0; q < 2; ++q) {
+          const float keep = b3 ? x[2 + q] : x[q];
+          const float send = b3 ? x[q] : x[2 + q];
+          y[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+        float z = (b2 ? y[1] : y[0]) + __shfl_xor_sync(0xffffffffu, b2 ? y[0] : y[1], 4);
+        z += __shfl_xor_sync(0xffffffffu, z, 2);
+        z += __shfl_xor_sync(0xffffffffu, z, 1);
+        if ((lane & 3) == 0) part[rg + kLdgRowGroups * (lane >> 2)][wg][n] = z;  // row lane/4
+      } else {
+        // Four row partials: after the 16- and 8-lane exchanges lane l holds row
+        // l / 8 of its 8-lane group, summed over the group by three more steps.
+        float x[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const float keep = b4 ? v[2 + q][n] : v[q][n];
+          const float send = b4 ? v[q][n] : v[2 + q][n];
+          x[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+        float z = (b3 ? x[1] : x[0]) + __shfl_xor_sync(0xffffffffu, b3 ? x[0] : x[1], 8);
+        z += __shfl_xor_sync(0xffffffffu, z, 4);
+        z += __shfl_xor_sync(0xffffffffu, z, 2);
+        z += __shfl_xor_sync(0xffffffffu, z, 1);
+        if ((lane & 7) == 0) part[rg + kLdgRowGroups * (lane >> 3)][wg][n] = z;  // row lane/8
       }
-      float z = (b2 ? y[1] : y[0]) + __shfl_xor_sync(0xffffffffu, b2 ? y[0] : y[1], 4);
-      z += __shfl_xor_sync(0xffffffffu, z, 2);
-      z += __shfl_xor_sync(0xffffffffu, z, 1);
-      if ((lane & 3) == 0) part[rg + kLdgRowGroups * (lane >> 2)][wg][n] = z;  // row slot lane/4
     }
     __syncthreads();
     for (int t = static_cast<int>(threadIdx.x); t < ROWS * NC; t += kLdgThreads) {

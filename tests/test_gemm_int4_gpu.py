@@ -60,6 +60,16 @@ def test_gemv_k_sizes(clove_lib, oracle_mod, cuda, K):
     _check(clove_lib, oracle_mod, 300, 1, K, seed=K)
 
 
+@pytest.mark.parametrize("M,K", [(4096, 11008), (9000, 11008), (1000, 7040), (300, 3200)])
+def test_gemv_partial_windows(clove_lib, oracle_mod, cuda, M, K):
+    """K a multiple of 128 but not of 1024 (the Llama-7B down projection, K = 11008:
+    11 windows of 1024 codes, the last one 768): the direct-load decode kernel masks
+    the lanes past K; with 3 windows per lane it runs 4-row rounds (M = 9000: several
+    rounds per CTA)."""
+    assert clove_lib.describe_dispatch("int4", M, 1, K).startswith("gemv_int4")
+    _check(clove_lib, oracle_mod, M, 1, K, seed=M + K)
+
+
 @pytest.mark.parametrize("M", [1, 3, 8])
 def test_gemv_small_m_transposed(clove_lib, oracle_mod, cuda, M):
     _check(clove_lib, oracle_mod, M, 600, 1024, seed=M)
