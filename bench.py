@@ -887,6 +887,70 @@ def _summary(line):
     return out
 
 
+def run_host_links(args):
+    """Host<->device bandwidth of the box as the end-to-end run uses it: every rank
+    (one per GPU, launched like the benchmark) copies the step's 16.8 MB between
+    pinned, NUMA-local host memory and its GPU, all ranks at once: host->device
+    alone, device->host alone, then both directions together. Device time, max over
+    ranks; rank 0 prints one JSON line."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    numa = _bind_to_gpu_numa(torch, local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    n = UP[1] * UP[2] * 2  # the step's activations, 16.8 MB (the result is the same size)
+    hin = torch.empty(n, dtype=torch.uint8).pin_memory()
+    hin.fill_(1)
+    hout = torch.empty(n, dtype=torch.uint8).pin_memory()
+    hout.fill_(0)
+    din = torch.empty(n, dtype=torch.uint8, device="cuda")
+    dout = torch.ones(n, dtype=torch.uint8, device="cuda")
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    main_s = torch.cuda.current_stream()
+    res = {}
+    for mode in ("h2d", "d2h", "both"):
+        def issue(reps):
+            s_in.wait_stream(main_s)
+            s_out.wait_stream(main_s)
+            for _ in range(reps):
+                if mode in ("h2d", "both"):
+                    with torch.cuda.stream(s_in):
+                        din.copy_(hin, non_blocking=True)
+                if mode in ("d2h", "both"):
+                    with torch.cuda.stream(s_out):
+                        hout.copy_(dout, non_blocking=True)
+            main_s.wait_stream(s_in)
+            main_s.wait_stream(s_out)
+        issue(3)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        reps = max(args.steps, 10)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(main_s)
+        issue(reps)
+        e1.record(main_s)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e-3], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[mode] = reps * n / t.item() / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "host<->device copy bandwidth per direction (all ranks at once)",
+            "n_gpus": world, "bytes_per_copy": n, "unit": "GB/s",
+            "per_rank": {k: round(v, 1) for k, v in res.items()},
+            "aggregate": {k: round(v * world, 1) for k, v in res.items()},
+            "host_binding": numa}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_gpu(args):
     import numpy as np
     import torch
@@ -1093,6 +1157,9 @@ def main():
     ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096",
                                        "attention"],
                     help="profiling mode: warm-up + steps plain launches of one secondary config")
+    ap.add_argument("--host-links", action="store_true",
+                    help="measure the host<->device copy bandwidth the end-to-end run uses "
+                         "(all ranks at once) instead of the benchmark")
     ap.add_argument("--kernel-only", action="store_true",
                     help="run only the warm-up and timed FFN GEMMs (for ncu), print nothing")
     ap.add_argument("--cpu-frac", type=int, default=32,
@@ -1100,7 +1167,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.case:
+    if args.host_links:
+        run_host_links(args)
+    elif args.case:
         run_case(args)
     elif args.impl == "reference":
         run_reference(args)
