@@ -193,14 +193,31 @@ def test_reference_kernels_build_against_dropin_headers(clove_lib, tmp_path):
                for f in ("layernorm", "softmax", "activations", "rope", "attention")]
     exe = str(tmp_path / "block_with_reference_kernels")
     # The reference's own build flags plus the two forced includes its headers
-    # need with GCC 13 (<cstdint>, <cassert>).
-    cmd = [nvcc, "-std=c++17", "-O3", "--use_fast_math", "--expt-relaxed-constexpr",
-           "-include", "cstdint", "-include", "cassert",
-           "-gencode", "arch=compute_100a,code=sm_100a",
-           "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(ref, "include"),
-           os.path.join(ROOT, "tests", "cxx", "runtime_linear_layers.cu"), *kernels,
-           "-o", exe, "-L" + lib_dir, "-lclove_b200", "-Xlinker", "-rpath=" + lib_dir]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    # need with GCC 13 (<cstdint>, <cassert>). One object per source, compiled in
+    # parallel, then one link.
+    flags = ["-std=c++17", "-O3", "--use_fast_math", "--expt-relaxed-constexpr",
+             "-include", "cstdint", "-include", "cassert",
+             "-gencode", "arch=compute_100a,code=sm_100a",
+             "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(ref, "include")]
+    srcs = [os.path.join(ROOT, "tests", "cxx", "runtime_linear_layers.cu"), *kernels]
+    objs = [str(tmp_path / (os.path.basename(f) + ".o")) for f in srcs]
+
+    def compile_one(i):
+        # attention.cu's kernels take minutes in the device optimiser (cicc): they are
+        # compiled unoptimised (-Xcicc -O0), which still runs the front end these
+        # headers affect, and keeps this CPU test to seconds.
+        extra = ["-Xcicc", "-O0"] if srcs[i].endswith("attention.cu") else []
+        return subprocess.run([nvcc, *flags, *extra, "-c", srcs[i], "-o", objs[i]],
+                              capture_output=True, text=True)
+
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=len(srcs)) as ex:
+        results = list(ex.map(compile_one, range(len(srcs))))
+    for f, r in zip(srcs, results):
+        assert r.returncode == 0, f + ": " + r.stderr[-3000:]
+    r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", exe,
+                        "-L" + lib_dir, "-lclove_b200", "-Xlinker", "-rpath=" + lib_dir],
+                       capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-3000:]
     assert os.path.exists(exe)
 
