@@ -90,3 +90,46 @@ def test_attention_rejects_unsupported(clove_lib, cuda):
     kv = torch.zeros((1, 2, 64, 128), dtype=torch.float16, device="cuda")
     with pytest.raises(clove_lib.CloveError):
         clove_lib.flash_attention(q, kv, kv)  # 3 heads over 2 kv heads
+
+
+def _torch_ref(q, k, v, causal):
+    """Plain PyTorch fp32 attention on the GPU (scale 1/sqrt(128))."""
+    qf, kf, vf = q.float(), k.float(), v.float()
+    s = torch.matmul(qf, kf.transpose(-1, -2)) / np.sqrt(128.0)
+    if causal:
+        n = s.shape[-1]
+        s = s.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool, device=s.device), 1),
+                          float("-inf"))
+    return torch.matmul(torch.softmax(s, dim=-1), vf)
+
+
+@pytest.mark.parametrize("B,H,S,causal", [(1, 32, 2048, True), (1, 32, 2048, False),
+                                          (8, 32, 1024, True)])
+def test_attention_benchmark_shapes(clove_lib, cuda, B, H, S, causal):
+    """The benchmark's shapes: hundreds of CTAs over several waves, heaviest tile pairs
+    first, every (batch, head) of the one-dimensional grid; against PyTorch fp32."""
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S + causal)
+    q, k, v = (torch.randn((B, H, S, 128), device="cuda", generator=g).half() for _ in range(3))
+    O = clove_lib.flash_attention(q, k, v, causal=causal)
+    ref = _torch_ref(q, k, v, causal)
+    err = float((O.float() - ref).norm() / ref.norm())
+    assert err < TOL, err
+    assert clove_lib.device_error() == 0
+
+
+def test_attention_back_to_back_calls(clove_lib, cuda):
+    """Consecutive calls on one stream with different inputs (each kernel's set-up
+    overlaps the previous kernel's tail): every output holds its own inputs' result."""
+    g = torch.Generator(device="cuda").manual_seed(77)
+    sets = [tuple(torch.randn((2, 8, 640, 128), device="cuda", generator=g).half()
+                  for _ in range(3)) for _ in range(4)]
+    outs = [torch.empty_like(s[0]) for s in sets]
+    for rep in range(2):
+        for (q, k, v), o in zip(sets, outs):
+            clove_lib.flash_attention(q, k, v, causal=rep == 0, O=o)
+    torch.cuda.synchronize()
+    for (q, k, v), o in zip(sets, outs):
+        ref = _torch_ref(q, k, v, False)
+        err = float((o.float() - ref).norm() / ref.norm())
+        assert err < TOL, err
+    assert clove_lib.device_error() == 0
