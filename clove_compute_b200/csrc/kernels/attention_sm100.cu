@@ -70,6 +70,16 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, int b
   const uint64_t bit = 1ull << (dev.device & 63);
   std::atomic<uint64_t>& attr = g_attn_attr[causal ? 1 : 0];
   if ((attr.load(std::memory_order_acquire) & bit) == 0) {
+    // The kernel moves registers between its warpgroups with setmaxnreg, planned for
+    // a launch allocation of S::REGS_LAUNCH per thread: with fewer, an increase
+    // would wait forever, so such a build is refused here rather than launched.
+    cudaFuncAttributes fa{};
+    rc = check_cuda(cudaFuncGetAttributes(&fa, fn), "cudaFuncGetAttributes(attention)");
+    if (rc) return rc;
+    if (fa.numRegs != S::REGS_LAUNCH)
+      return fail(CLOVE_ERR_UNSUPPORTED,
+                  "attention: built with %d registers per thread, its register plan needs %d",
+                  fa.numRegs, S::REGS_LAUNCH);
     rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::SMEM_BYTES),
                     "cudaFuncSetAttribute(attention smem)");

@@ -8,7 +8,8 @@
 // fp16 in and out, fp32 accumulation. head_dim 128.
 //
 // One CTA computes two consecutive 128-query tiles of one (batch, head), which share
-// every K and V tile; keys advance 128 at a time. 10 warps:
+// every K and V tile; keys advance 128 at a time. 12 warps in three warpgroups
+// (setmaxnreg: 56 registers for the control group, 224 for the softmax groups):
 //   warp 0     TMA producer (one thread): both Q tiles once (two 64-column boxes
 //              each, 128B swizzle), then K and V, each in a 2-stage ring, in the
 //              order the tensor core frees their stages (K of block j+2 once both
@@ -22,7 +23,8 @@
 //              PV_1(j), QK_1(j+1): while one tile's softmax runs, the tensor core
 //              works on the other tile. P.V starts on keys [0,64) as soon as the
 //              softmax has written them.
-//   warps 2-9  softmax, one warpgroup per tile, one query row per thread (its TMEM
+//   warps 2-3  idle (fill the control warpgroup)
+//   warps 4-11 softmax, one warpgroup per tile, one query row per thread (its TMEM
 //              lane): the row of S into registers, mask, row maximum,
 //              p = 2^(s*scale*log2e - m), row sum, P as fp16 pairs written back over
 //              the first 64 columns of the tile's S buffer (the A operand of P.V), in
@@ -65,7 +67,19 @@ struct AttnShape {
   static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
-  static constexpr int THREADS = (2 + 4 * TILES) * 32;
+  // 12 warps in warpgroups: warps 0-3 control (0 producer, 1 MMA, 2-3 idle), then
+  // one softmax warpgroup per tile. Registers: launched at 168 per thread (the cap
+  // for 384 threads), setmaxnreg then gives the control warpgroup 56 and the
+  // softmax warpgroups 224 (a row of S, 128 fp32, plus the exponential's constants).
+  static constexpr int SOFT0 = 4;
+  static constexpr int THREADS = (SOFT0 + 4 * TILES) * 32;
+  static constexpr int REGS_LAUNCH = 168;
+  static constexpr int REGS_CTL = 56;
+  static constexpr int REGS_SOFT = 224;
+  static_assert(128 * REGS_CTL + (THREADS - 128) * REGS_SOFT <= THREADS * REGS_LAUNCH,
+                "register split exceeds the launch allocation");
+  // Warp w runs on sub-partition w % 4: one control and two softmax warps each.
+  static_assert(32 * (REGS_CTL + TILES * REGS_SOFT) <= 16384, "per sub-partition registers");
   // S of tile t at columns t*128 (P_t over its first 64), O of tile t at 256 + t*128.
   static constexpr int TMEM_COLS = 512;
   static constexpr int O_COL = 256;
@@ -76,6 +90,17 @@ struct AttnShape {
 // O: A (P, in tensor memory) K-major, B (V) MN-major.
 constexpr uint32_t kAttnIdescS = dev::make_idesc(1, 0, 0, 0, 0, 128, 128);
 constexpr uint32_t kAttnIdescO = dev::make_idesc(1, 0, 0, 0, 1, 128, 128);
+
+// Key pairs (of every 16) whose exponentials run as the FMA-pipe polynomial
+// (dev::f2_exp2_poly) rather than on the MUFU, spread evenly over the 16.
+#ifndef CLOVE_ATTN_POLY
+#define CLOVE_ATTN_POLY 4
+#endif
+constexpr int kAttnPolyPairs = CLOVE_ATTN_POLY;
+static_assert(kAttnPolyPairs >= 0 && kAttnPolyPairs <= 16, "poly pairs per 16");
+__device__ __forceinline__ constexpr bool attn_poly_pair(int u) {
+  return (u * kAttnPolyPairs) / 16 != ((u + 1) * kAttnPolyPairs) / 16;
+}
 
 // K-major descriptor of a [128 rows x 128 fp16] operand held as two 64-column
 // 128B-swizzled halves, for the 16-column K step k.
@@ -192,6 +217,10 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
   dev::grid_dependency_wait();
   if (threadIdx.x == 0) ATTN_TRACE(0);
 
+  // Roles by warpgroup; each branch first reallocates its registers (one setmaxnreg
+  // executed by all four warps of the group, ahead of the role's code).
+  if (warp < S::SOFT0) {
+    dev::setmaxnreg_dec<S::REGS_CTL>();
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -315,9 +344,11 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
       if (next && j + 1 < nb1) qk(1, j + 1);
       if (next && ok) commit(&k_empty[(j + 1) & 1]);        // block j+1's K: both S issued
     }
+  }  // warps 2-3: idle
   } else {
     // ------------------------------------------------------------ softmax (2 warpgroups)
-    const int t = static_cast<int>(warp - 2) >> 2;   // this warpgroup's query tile
+    dev::setmaxnreg_inc<S::REGS_SOFT>();
+    const int t = static_cast<int>(warp - S::SOFT0) >> 2;  // this warpgroup's query tile
     const uint32_t quarter = warp & 3u;             // TMEM lane quarter of this warp
     const int row = static_cast<int>(quarter * 32 + lane);
     const int qt0 = q0 + t * S::BQ;                 // the tile's first query
@@ -387,7 +418,8 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
       }
       // p = 2^(s * scale * log2e - m) on key pairs (packed fp32 arithmetic), packed to
       // fp16 pairs (key 2c in the low half of column c of the tile's P), 32 keys per
-      // tensor-memory store.
+      // tensor-memory store. kAttnPolyPairs of every 16 pairs take the FMA-pipe
+      // exponential, the rest the MUFU's ex2, whose rate alone would bound the row.
       const uint64_t sc2 = dev::f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = dev::f2_pack(-m, -m);
       uint64_t sum2[2] = {0ull, 0ull};  // two packed partial sums (+0.0f pairs)
@@ -398,9 +430,14 @@ __global__ void __launch_bounds__(AttnShape::THREADS, 1)
         for (int u = 0; u < 16; ++u) {
           const int i = 2 * (c + u);
           const uint64_t x = dev::f2_fma(dev::f2_pack(s[i], s[i + 1]), sc2, nm2);
-          float x0, x1;
-          dev::f2_unpack(x, x0, x1);
-          const uint64_t pp = dev::f2_pack(dev::ex2_approx(x0), dev::ex2_approx(x1));
+          uint64_t pp;
+          if (attn_poly_pair(u)) {
+            pp = dev::f2_exp2_poly(x);
+          } else {
+            float x0, x1;
+            dev::f2_unpack(x, x0, x1);
+            pp = dev::f2_pack(dev::ex2_approx(x0), dev::ex2_approx(x1));
+          }
           sum2[u & 1] = dev::f2_add(sum2[u & 1], pp);
           float p0, p1;
           dev::f2_unpack(pp, p0, p1);

@@ -572,6 +572,33 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// 2^x for both lanes of a packed pair, on the FMA pipe instead of the MUFU
+// (Cody-Waite style reduction, polynomial fitted here by the Remez exchange):
+// x = j + f with j = round(x) (adding 1.5 * 2^23 leaves j in the low mantissa bits)
+// and f = x - j in [-0.5, 0.5] (exact); 2^f from a degree-4 polynomial with minimax
+// relative error 2.6e-6 on that interval (2.7e-6 evaluated in fp32); j added to the
+// exponent field ((bits(x + 1.5 * 2^23) << 23) == j << 23 modulo 2^32). Inputs below
+// -125 are clamped there (2^-125 = 2.4e-38: zero once rounded to fp16, and the
+// exponent field stays normal); inputs must be <= 128.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = f2_add(xc, f2_pack(12582912.f, 12582912.f));
+  const uint64_t j = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), xc);
+  uint64_t q = f2_fma(f, f2_pack(0.009570102207362652f, 0.009570102207362652f),
+                      f2_pack(0.05591785907745361f, 0.05591785907745361f));
+  q = f2_fma(q, f, f2_pack(0.240247443318367f, 0.240247443318367f));
+  q = f2_fma(q, f, f2_pack(0.6931217908859253f, 0.6931217908859253f));
+  q = f2_fma(q, f, f2_pack(0.9999992847442627f, 0.9999992847442627f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  return f2_pack(__uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)),
+                 __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
