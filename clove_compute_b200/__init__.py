@@ -14,7 +14,8 @@ from ._lib import (CloveError, lib, library_path, INT4_GROUP_SIZE,  # noqa: F401
                    CLOVE_ERR_NCCL, CLOVE_ERR_DEVICE, CLOVE_ERR_TIMEOUT)
 from .api import (gemm_fp16, gemm_fp16_batched, gemm_int8, gemm_int8_rowcol, gemm_int4,  # noqa: F401
                   debug_int8_acc, debug_int4_group_acc, debug_stream_read, debug_stream_k_plan,
-                  debug_peer_wait_timeout, quantize_int4, swiglu_fused, flash_attention,
+                  debug_peer_wait_timeout, debug_exp2_poly, quantize_int4, swiglu_fused,
+                  flash_attention,
                   set_dispatch_override, set_weight_prefetch,
                   describe_dispatch, device_error, version)
 from .nsplit import NSplit, col_begin  # noqa: F401
@@ -22,7 +23,7 @@ from .nsplit import NSplit, col_begin  # noqa: F401
 __all__ = [
     "gemm_fp16", "gemm_fp16_batched", "gemm_int8", "gemm_int8_rowcol", "gemm_int4",
     "debug_int8_acc", "debug_int4_group_acc", "debug_stream_read", "debug_stream_k_plan",
-    "debug_peer_wait_timeout", "quantize_int4",
+    "debug_peer_wait_timeout", "debug_exp2_poly", "quantize_int4",
     "swiglu_fused", "flash_attention",
     "set_dispatch_override",
     "set_weight_prefetch",

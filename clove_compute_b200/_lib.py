@@ -40,6 +40,7 @@ SIGNATURES = {
     "clove_quantize_int4": ([_P, _I, _I, _P, _P, _P, _P], _I),
     "clove_swiglu_fused": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
     "clove_debug_stream_read": ([_P, _SZ, _P, _P], _I),
+    "clove_debug_exp2_poly": ([_P, _P, _I, _P], _I),
     "clove_debug_peer_wait_timeout": ([_P, ctypes.c_ulonglong, _P], _I),
     "clove_debug_stream_k_plan": ([_I, _I, _I, _I, _P], _I),
     "clove_set_dispatch_override": ([_I, _I, _I], _I),

@@ -254,6 +254,17 @@ def debug_stream_read(src, out, stream=None) -> None:
                                         _stream(stream)))
 
 
+def debug_exp2_poly(x: torch.Tensor, stream=None) -> torch.Tensor:
+    """2^x through the attention softmax's FMA-pipe polynomial exponential (an even
+    number of fp32 CUDA elements)."""
+    _need(x, "x", torch.float32, 1)
+    if x.numel() % 2:
+        raise ValueError("x needs an even number of elements")
+    y = torch.empty_like(x)
+    check(lib().clove_debug_exp2_poly(_ptr(x), _ptr(y), x.numel(), _stream(stream)))
+    return y
+
+
 def debug_peer_wait_timeout(words: torch.Tensor, timeout_ns: int, stream=None) -> None:
     """Runs the N-split's cross-rank completion wait for a two-rank group whose
     other rank never signals (``words``: 8 int64 of device scratch); the bounded

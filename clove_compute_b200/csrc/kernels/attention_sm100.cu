@@ -47,6 +47,27 @@ void attn_strides(int layout, int heads, int seq, uint64_t out[3]) {
 }
 }  // namespace
 
+namespace {
+// The softmax's polynomial exponential on an array, pair by pair (test hook).
+__global__ void exp2_poly_probe_kernel(const float2* __restrict__ x, float2* __restrict__ y,
+                                       int pairs) {
+  const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= pairs) return;
+  const float2 v = x[i];
+  float a, b;
+  dev::f2_unpack(dev::f2_exp2_poly(dev::f2_pack(v.x, v.y)), a, b);
+  y[i] = make_float2(a, b);
+}
+}  // namespace
+
+int launch_exp2_poly_probe(const float* x, float* y, int n, cudaStream_t stream) {
+  const int pairs = n / 2;
+  if (pairs <= 0) return CLOVE_OK;
+  exp2_poly_probe_kernel<<<(pairs + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const float2*>(x), reinterpret_cast<float2*>(y), pairs);
+  return check_cuda(cudaGetLastError(), "exp2_poly_probe launch");
+}
+
 int launch_attention(const void* Q, const void* K, const void* V, void* O, int batch, int heads,
                      int kv_heads, int seq, float scale, bool causal, int layout,
                      const DeviceInfo& dev, cudaStream_t stream) {

@@ -617,13 +617,22 @@ int clove_flash_attention(const void* Q, const void* K, const void* V, void* O, 
                 head_dim);
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
     return fail(CLOVE_ERR_UNSUPPORTED, "attention needs 16-byte aligned tensors");
-  if (num_heads > 65535 || batch > 65535)
-    return fail(CLOVE_ERR_UNSUPPORTED, "at most 65535 heads and batches");
   DeviceInfo dev;
   const int rc = current_device(&dev);
   if (rc) return rc;
   return launch_attention(Q, K, V, O, batch, num_heads, num_kv_heads, seq_len, scale, causal != 0,
                           layout, dev, as_stream(stream));
+}
+
+int clove_debug_exp2_poly(const float* x, float* y, int n, void* stream) {
+  if (x == nullptr || y == nullptr) return fail(CLOVE_ERR_INVALID_ARG, "null pointer");
+  if (n < 0 || n % 2 != 0) return fail(CLOVE_ERR_INVALID_ARG, "n must be even and non-negative");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 7u) != 0)
+    return fail(CLOVE_ERR_INVALID_ARG, "x and y must be 8-byte aligned");
+  DeviceInfo dev;
+  const int rc = current_device(&dev);
+  if (rc) return rc;
+  return launch_exp2_poly_probe(x, y, n, as_stream(stream));
 }
 
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream) {

@@ -140,6 +140,8 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, int b
                      int kv_heads, int seq, float scale, bool causal, int layout,
                      const DeviceInfo& dev, cudaStream_t stream);
 int read_clear_error_attn();
+// y[i] = 2^x[i] through the attention kernel's FMA-pipe polynomial (test hook; n even).
+int launch_exp2_poly_probe(const float* x, float* y, int n, cudaStream_t stream);
 
 // ---- INT4 packing tool (kernels/quant_int4.cu)
 int launch_quantize_int4(const void* W, int rows, int K, uint8_t* codes, void* scales, void* zeros,

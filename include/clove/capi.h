@@ -162,6 +162,12 @@ int clove_debug_int4_group_acc(const uint8_t* A_q, const void* A_scale, const vo
  * (Measurement hook; no counterpart in the reference.) */
 int clove_debug_stream_read(const void* src, size_t nbytes, uint32_t* out, void* stream);
 
+/* y[i] = 2^x[i] (n even, fp32 device arrays, 8-byte aligned) through the polynomial
+ * exponential the attention softmax runs on the FMA pipe for part of its keys:
+ * relative error <= 2.7e-6 for x in [-125, 128], inputs below -125 clamped to -125.
+ * (Test hook; no counterpart in the reference.) */
+int clove_debug_exp2_poly(const float* x, float* y, int n, void* stream);
+
 /* Runs the N-split's cross-rank completion wait for rank 0 of a two-rank group
  * whose other rank never signals, with a wait limit of timeout_ns (at most 2 s;
  * the product uses 2 s): the wait runs out, the kernel records device error 1

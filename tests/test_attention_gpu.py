@@ -133,3 +133,22 @@ def test_attention_back_to_back_calls(clove_lib, cuda):
         err = float((o.float() - ref).norm() / ref.norm())
         assert err < TOL, err
     assert clove_lib.device_error() == 0
+
+
+def test_exp2_polynomial_error_bound(clove_lib, cuda):
+    """The softmax's FMA-pipe exponential (Remez-fitted degree-4 polynomial after a
+    round-to-nearest range reduction) against float64 exp2: relative error within
+    2.7e-6 over [-125, 8] (the arguments the softmax produces: s*scale*log2e - m <= 8),
+    at integers, half-integers and random points; below -125 it returns 2^-125."""
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.uniform(-125.0, 8.0, 1 << 20), np.arange(-125, 9, dtype=np.float64),
+                        np.arange(-124.5, 8.0, 1.0), [-1e-7, 1e-7, 0.0]]).astype(np.float32)
+    if x.size % 2:
+        x = np.append(x, np.float32(0.0))
+    y = clove_lib.debug_exp2_poly(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.float64)
+    ref = np.exp2(x.astype(np.float64))
+    rel = np.abs(y / ref - 1.0)
+    assert rel.max() <= 2.7e-6, (rel.max(), x[np.argmax(rel)])
+    low = clove_lib.debug_exp2_poly(torch.tensor([-126.0, -1000.0], device="cuda")).cpu().numpy()
+    assert np.all(np.abs(low / 2.0 ** -125 - 1.0) <= 2.7e-6)
+    assert clove_lib.device_error() == 0
