@@ -175,7 +175,7 @@ int settle_nccl(ncclComm_t comm, ncclResult_t r, const char* what, double deadli
                 bool* aborted = nullptr) {
   if (r != ncclInProgress) return check_nccl(r, what);
   const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
+  for (long polls = 0;; ++polls) {
     ncclResult_t st = ncclSuccess;
     const ncclResult_t q = g_nccl.CommGetAsyncError(comm, &st);
     if (q != ncclSuccess) return check_nccl(q, "ncclCommGetAsyncError");
@@ -188,7 +188,13 @@ int settle_nccl(ncclComm_t comm, ncclResult_t r, const char* what, double deadli
       return fail(CLOVE_ERR_TIMEOUT, "%s: not done after %.0f s (a rank missing?); communicator aborted",
                   what, deadline_s);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    // An enqueue finishes within microseconds: poll without sleeping for the first
+    // millisecond (a fixed sleep here left the GPU idle between back-to-back calls),
+    // then back off so that a long wait (communicator creation) does not spin a core.
+    if (el < 1e-3)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(el < 0.1 ? 20 : 200));
   }
 }
 
