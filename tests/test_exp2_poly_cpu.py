@@ -1,8 +1,9 @@
 """The attention softmax's FMA-pipe exponential (f2_exp2_poly in
 csrc/kernels/sm100_ptx.cuh), restated on the CPU from the coefficients in the source:
 x = j + f with j = round(x) through the 1.5 * 2^23 shifter, 2^f from the degree-4
-polynomial in Horner form with fp32 rounding after every operation (the device fuses
-each multiply-add, which only rounds less), 2^j added to the exponent field. The
+polynomial in Horner form with each multiply-add rounded once to fp32 as the device's
+fused multiply-add does (the fp32 product is exact in float64), 2^j added to the
+exponent field. The
 relative error must stay within the 2.7e-6 the source states, over the whole range
 the softmax feeds it ([-125, 8]) and at the interval ends f = +-0.5."""
 import os
@@ -31,10 +32,12 @@ def _exp2_poly(x):
     t = (x + f32(12582912.0)).astype(np.float32)
     j = (t - f32(12582912.0)).astype(np.float32)
     f = (x - j).astype(np.float32)
-    q = (f * c4).astype(np.float32) + c3
+    def fma(a, b, c):  # a * b + c with one rounding to fp32
+        return (a.astype(np.float64) * b.astype(np.float64) + np.float64(c)).astype(np.float32)
+
+    q = fma(f, np.full_like(f, c4), c3)
     for c in (c2, c1, c0):
-        q = (q.astype(np.float32) * f).astype(np.float32) + c
-    q = q.astype(np.float32)
+        q = fma(q, f, c)
     bits = q.view(np.uint32) + (t.view(np.uint32) << np.uint32(23))
     return bits.view(np.float32)
 
