@@ -112,6 +112,32 @@ int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8
   constexpr int RMAX = PW > 2 ? 4 : 8;
   int grid = dev.num_sms;
   if (rows < grid * 8) grid = (rows + 7) / 8;
+  if constexpr (NC == 1 && PW == 1) {
+    // One 1024-code window per lane (K <= 4096): two CTAs per SM at <= 64 registers,
+    // 4 rows per warp and round, so that one CTA's loads are in flight while the
+    // other computes, and under programmatic launch the next call's CTAs start in
+    // the slots this call's CTAs leave.
+    if (rows >= 2 * dev.num_sms * 8) {
+      const int grid2 = 2 * dev.num_sms;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.gridDim = dim3(static_cast<unsigned>(grid2), 1, 1);
+      cfg.blockDim = dim3(kern::kLdgThreads, 1, 1);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = stream;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      const int early = weight_prefetch_enabled() ? 1 : 0;
+      return check_cuda(
+          cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<1, 1, 4, 2>, Aq,
+                             static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
+                             static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
+                             static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),
+          "gemv_int4_ldg launch");
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -124,7 +150,7 @@ int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8
   cfg.numAttrs = 1;
   const int early = weight_prefetch_enabled() ? 1 : 0;
   return check_cuda(
-      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, RMAX>, Aq,
+      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, RMAX, 1>, Aq,
                          static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
                          static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
                          static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),

@@ -554,8 +554,8 @@ constexpr int kLdgRowGroups = 4;
 constexpr int kLdgWindowGroups = 4;
 constexpr int kLdgThreads = kLdgRowGroups * kLdgWindowGroups * 32;
 
-template <int NC, int PW, int RMAX>
-__global__ void __launch_bounds__(kLdgThreads, 1)
+template <int NC, int PW, int RMAX, int MINB>
+__global__ void __launch_bounds__(kLdgThreads, MINB)
     gemv_int4_ldg_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
                          const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
                          const __half* __restrict__ Bs, const __half* __restrict__ Bz,
