@@ -103,58 +103,53 @@ int gemv_int4_ws2(const uint8_t* Aq, const void* As, const void* Az, const uint8
       "gemv_int4_ws2 launch");
 }
 
-template <int NC, int PW>
-int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
-                  const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
-                  long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
-  // Rows per warp and round: 8, or 4 when three windows per lane (K up to 12288)
-  // would not leave the registers for 8.
-  constexpr int RMAX = PW > 2 ? 4 : 8;
-  int grid = dev.num_sms;
-  if (rows < grid * 8) grid = (rows + 7) / 8;
-  if constexpr (NC == 1 && PW == 1) {
-    // One 1024-code window per lane (K <= 4096): two CTAs per SM at <= 64 registers,
-    // 4 rows per warp and round, so that one CTA's loads are in flight while the
-    // other computes, and under programmatic launch the next call's CTAs start in
-    // the slots this call's CTAs leave.
-    if (rows >= 2 * dev.num_sms * 8) {
-      const int grid2 = 2 * dev.num_sms;
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = 1;
-      cfg.gridDim = dim3(static_cast<unsigned>(grid2), 1, 1);
-      cfg.blockDim = dim3(kern::kLdgThreads, 1, 1);
-      cfg.dynamicSmemBytes = 0;
-      cfg.stream = stream;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      const int early = weight_prefetch_enabled() ? 1 : 0;
-      return check_cuda(
-          cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<1, 1, 4, 2>, Aq,
-                             static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
-                             static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
-                             static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),
-          "gemv_int4_ldg launch");
-    }
-  }
+template <int NC, int PW, int RMAX, int MINB, int RG, int WG>
+int launch_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                    const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
+                    long long ldc_col, int grid, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(kern::kLdgThreads, 1, 1);
+  cfg.blockDim = dim3(RG * WG * 32, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int early = weight_prefetch_enabled() ? 1 : 0;
   return check_cuda(
-      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, RMAX, 1>, Aq,
+      cudaLaunchKernelEx(&cfg, kern::gemv_int4_ldg_kernel<NC, PW, RMAX, MINB, RG, WG>, Aq,
                          static_cast<const __half*>(As), static_cast<const __half*>(Az), Bq,
                          static_cast<const __half*>(Bs), static_cast<const __half*>(Bz),
                          static_cast<__half*>(C), rows, K, ldc_row, ldc_col, early),
       "gemv_int4_ldg launch");
+}
+
+template <int NC, int PW>
+int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
+                  const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
+                  long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
+  // One vector with at least 8 rows per CTA: two CTAs per SM, one window per lane,
+  // so that one CTA's loads are in flight while the other reduces, and under
+  // programmatic launch the next call's CTAs start in the slots this call's CTAs
+  // leave. Rows up to 4096 codes take 4 x 4 warps (<= 64 registers, 4 rows per
+  // warp and round), longer rows (up to 12288 codes) 1 x 12 warps (8 rows per warp
+  // and round, <= 85 registers).
+  if (NC == 1 && rows >= 2 * dev.num_sms * 8) {
+    if (PW == 1)
+      return launch_int4_ldg<1, 1, 4, 2, 4, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
+                                               ldc_col, 2 * dev.num_sms, stream);
+    return launch_int4_ldg<1, 1, 8, 2, 1, 12>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
+                                              ldc_col, 2 * dev.num_sms, stream);
+  }
+  // Rows per warp and round: 8, or 4 when three windows per lane (K up to 12288)
+  // would not leave the registers for 8.
+  constexpr int RMAX = PW > 2 ? 4 : 8;
+  int grid = dev.num_sms;
+  if (rows < grid * 8) grid = (rows + 7) / 8;
+  return launch_int4_ldg<NC, PW, RMAX, 1, 4, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
+                                                ldc_col, grid, stream);
 }
 
 template <int NC, int P>

@@ -541,37 +541,35 @@ __global__ void __launch_bounds__(kWs2Threads, 2)
 #endif
 }
 
-// INT4 decode with direct 128-bit loads (no shared-memory ring): the consumer
-// decomposition of gemv_int4_ws2_kernel -- warp w = 4 * rg + wg takes rows
-// rg, rg + 4, ... of the CTA's block and the 1024-element windows wg, wg + 4, ...
-// of each -- but every lane loads its own 16-byte chunks of up to RMAX rows with
-// ld.global.nc straight into registers, all issued before any math, like a bare
-// streaming read. With weights_early those loads are issued before
+// INT4 decode with direct 128-bit loads (no shared-memory ring). RG x WG warps:
+// warp w = WG * rg + wg takes rows rg, rg + RG, ... of the CTA's block and the
+// 1024-element windows wg, wg + WG, ... of each (4 x 4, the consumer decomposition
+// of gemv_int4_ws2_kernel; 1 x 12 gives every lane a single window of rows up to
+// 12288 codes) -- but every lane loads its own 16-byte chunks of up to RMAX rows
+// with ld.global.nc straight into registers, all issued before any math, like a
+// bare streaming read. With weights_early those loads are issued before
 // griddepcontrol.wait. The RMAX row partials of a warp are reduced by one
-// transposed butterfly (lane 4i ends with row i), the four window partials of a
-// row are added in fixed order through shared memory.
-constexpr int kLdgRowGroups = 4;
-constexpr int kLdgWindowGroups = 4;
-constexpr int kLdgThreads = kLdgRowGroups * kLdgWindowGroups * 32;
-
-template <int NC, int PW, int RMAX, int MINB>
-__global__ void __launch_bounds__(kLdgThreads, MINB)
+// transposed butterfly (lane 4i ends with row i), the WG window partials of a row
+// are added in fixed order through shared memory.
+template <int NC, int PW, int RMAX, int MINB, int RG, int WG>
+__global__ void __launch_bounds__(RG * WG * 32, MINB)
     gemv_int4_ldg_kernel(const uint8_t* __restrict__ Aq, const __half* __restrict__ As,
                          const __half* __restrict__ Az, const uint8_t* __restrict__ Bq,
                          const __half* __restrict__ Bs, const __half* __restrict__ Bz,
                          __half* __restrict__ C, int rows, int K, long long ldc_row,
                          long long ldc_col, int weights_early) {
   static_assert(RMAX == 8 || RMAX == 4, "the transposed butterfly reduces 8 or 4 row partials");
-  constexpr int ROWS = kLdgRowGroups * RMAX;  // rows of the block per round
-  __shared__ float part[ROWS][kLdgWindowGroups][NC];
+  constexpr int ROWS = RG * RMAX;  // rows of the block per round
+  constexpr int THREADS = RG * WG * 32;
+  __shared__ float part[ROWS][WG][NC];
   const int NG = K >> 7;
   const int P = (K + 1023) >> 10;  // 1024-code windows, the last one possibly partial
   const int KC = K >> 5;           // 16-byte chunks of a row (32 codes each)
   const int KB = K >> 1;
   const int warp = static_cast<int>(dev::warp_idx());
   const int lane = static_cast<int>(dev::lane_idx());
-  const int rg = warp >> 2;
-  const int wg = warp & 3;
+  const int rg = warp / WG;
+  const int wg = warp - rg * WG;
   const int per_cta = (rows + gridDim.x - 1) / gridDim.x;
   const int r0 = blockIdx.x * per_cta;
   const int nrows = max(0, min(rows, r0 + per_cta) - r0);
@@ -584,10 +582,10 @@ __global__ void __launch_bounds__(kLdgThreads, MINB)
   auto load_round = [&](int base) {
 #pragma unroll
     for (int i = 0; i < RMAX; ++i) {
-      const int rl = base + rg + kLdgRowGroups * i;
+      const int rl = base + rg + RG * i;
 #pragma unroll
       for (int pw = 0; pw < PW; ++pw) {
-        const int p = wg + kLdgWindowGroups * pw;
+        const int p = wg + WG * pw;
         const int ch = p * 32 + lane;
         if (rl < nrows && p < P && ch < KC) {
           const size_t m = static_cast<size_t>(r0 + rl);
@@ -611,7 +609,7 @@ __global__ void __launch_bounds__(kLdgThreads, MINB)
   for (int n = 0; n < NC; ++n)
 #pragma unroll
     for (int pw = 0; pw < PW; ++pw) {
-      const int p = wg + kLdgWindowGroups * pw;
+      const int p = wg + WG * pw;
       const int ch = p * 32 + lane;
       uint4 q = make_uint4(0u, 0u, 0u, 0u);
       int zb = 0;
@@ -684,7 +682,7 @@ __global__ void __launch_bounds__(kLdgThreads, MINB)
         float z = (b2 ? y[1] : y[0]) + __shfl_xor_sync(0xffffffffu, b2 ? y[0] : y[1], 4);
         z += __shfl_xor_sync(0xffffffffu, z, 2);
         z += __shfl_xor_sync(0xffffffffu, z, 1);
-        if ((lane & 3) == 0) part[rg + kLdgRowGroups * (lane >> 2)][wg][n] = z;  // row lane/4
+        if ((lane & 3) == 0) part[rg + RG * (lane >> 2)][wg][n] = z;  // row lane/4
       } else {
         // Four row partials: after the 16- and 8-lane exchanges lane l holds row
         // l / 8 of its 8-lane group, summed over the group by three more steps.
@@ -699,15 +697,17 @@ __global__ void __launch_bounds__(kLdgThreads, MINB)
         z += __shfl_xor_sync(0xffffffffu, z, 4);
         z += __shfl_xor_sync(0xffffffffu, z, 2);
         z += __shfl_xor_sync(0xffffffffu, z, 1);
-        if ((lane & 7) == 0) part[rg + kLdgRowGroups * (lane >> 3)][wg][n] = z;  // row lane/8
+        if ((lane & 7) == 0) part[rg + RG * (lane >> 3)][wg][n] = z;  // row lane/8
       }
     }
     __syncthreads();
-    for (int t = static_cast<int>(threadIdx.x); t < ROWS * NC; t += kLdgThreads) {
+    for (int t = static_cast<int>(threadIdx.x); t < ROWS * NC; t += THREADS) {
       const int r = t / NC;
       const int n = t - r * NC;
       if (base + r < nrows) {
-        const float sum = ((part[r][0][n] + part[r][1][n]) + part[r][2][n]) + part[r][3][n];
+        float sum = part[r][0][n];
+#pragma unroll
+        for (int g = 1; g < WG; ++g) sum += part[r][g][n];  // fixed order
         C[static_cast<long long>(r0 + base + r) * ldc_row + n * ldc_col] = __float2half_rn(sum);
       }
     }
