@@ -130,16 +130,16 @@ template <int NC, int PW>
 int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                   const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
                   long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
-  // One vector with at least 8 rows per CTA: two CTAs per SM, one window per lane,
-  // so that one CTA's loads are in flight while the other reduces, and under
+  // One vector and at least 2 x 148 x 8 rows: several CTAs per SM, one window per
+  // lane, so that some CTAs' loads are in flight while others reduce, and under
   // programmatic launch the next call's CTAs start in the slots this call's CTAs
-  // leave. Rows up to 4096 codes take 4 x 4 warps (<= 64 registers, 4 rows per
-  // warp and round), longer rows (up to 12288 codes) 1 x 12 warps (8 rows per warp
-  // and round, <= 85 registers).
+  // leave. Rows up to 4096 codes: four CTAs of 2 x 4 warps per SM (<= 64 registers,
+  // 4 rows per warp and round); longer rows (up to 12288 codes): two CTAs of 1 x 12
+  // warps (8 rows per warp and round, <= 85 registers).
   if (NC == 1 && rows >= 2 * dev.num_sms * 8) {
     if (PW == 1)
-      return launch_int4_ldg<1, 1, 4, 2, 4, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
-                                               ldc_col, 2 * dev.num_sms, stream);
+      return launch_int4_ldg<1, 1, 4, 4, 2, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
+                                               ldc_col, 4 * dev.num_sms, stream);
     return launch_int4_ldg<1, 1, 8, 2, 1, 12>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
                                               ldc_col, 2 * dev.num_sms, stream);
   }

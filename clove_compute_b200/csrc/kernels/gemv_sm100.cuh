@@ -544,8 +544,8 @@ __global__ void __launch_bounds__(kWs2Threads, 2)
 // INT4 decode with direct 128-bit loads (no shared-memory ring). RG x WG warps:
 // warp w = WG * rg + wg takes rows rg, rg + RG, ... of the CTA's block and the
 // 1024-element windows wg, wg + WG, ... of each (4 x 4, the consumer decomposition
-// of gemv_int4_ws2_kernel; 1 x 12 gives every lane a single window of rows up to
-// 12288 codes) -- but every lane loads its own 16-byte chunks of up to RMAX rows
+// of gemv_int4_ws2_kernel; 2 x 4 and 1 x 12 give every lane a single window of
+// rows up to 4096 and 12288 codes) -- but every lane loads its own 16-byte chunks of up to RMAX rows
 // with ld.global.nc straight into registers, all issued before any math, like a
 // bare streaming read. With weights_early those loads are issued before
 // griddepcontrol.wait. The RMAX row partials of a warp are reduced by one

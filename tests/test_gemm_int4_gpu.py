@@ -65,10 +65,11 @@ def test_gemv_k_sizes(clove_lib, oracle_mod, cuda, K):
 def test_gemv_partial_windows(clove_lib, oracle_mod, cuda, M, K):
     """K a multiple of 128 but not of 1024 (the Llama-7B down projection, K = 11008:
     11 windows of 1024 codes, the last one 768): the direct-load decode kernel masks
-    the lanes past K. From 2 x 148 x 8 rows on, two CTAs per SM run with one window
-    per lane: 4 x 4 warps up to 4096 codes, 1 x 12 warps beyond (8 windows of 12
-    used at K = 8192, all 12 at 12288; M = 9000: several rounds per CTA); below it
-    one CTA per SM, with 3 windows per lane in 4-row rounds at M = 1000."""
+    the lanes past K. From 2 x 148 x 8 rows on, several CTAs per SM run with one
+    window per lane: four of 2 x 4 warps up to 4096 codes, two of 1 x 12 warps
+    beyond (8 windows of 12 used at K = 8192, all 12 at 12288; M = 9000: several
+    rounds per CTA); below it one CTA of 4 x 4 warps per SM, with 3 windows per
+    lane in 4-row rounds at M = 1000."""
     assert clove_lib.describe_dispatch("int4", M, 1, K).startswith("gemv_int4")
     _check(clove_lib, oracle_mod, M, 1, K, seed=M + K)
 
