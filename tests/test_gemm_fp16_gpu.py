@@ -71,9 +71,17 @@ def test_ffn_shapes_choose_cta_pairs(clove_lib, cuda):
     assert clove_lib.describe_dispatch("fp16", 4096, 2048, 11008).startswith("tc2_f16")
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 1024, 1024), (16, 4096, 1024)])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 1024, 1024), (16, 4096, 1024),
+                                   (1, 4096, 11008), (37, 4096, 6144)])
 def test_small_m_decode(clove_lib, oracle_mod, cuda, M, N, K):
     _run(clove_lib, oracle_mod, M, N, K)
+
+
+def test_small_m_long_k_plan(clove_lib, cuda):
+    """One 128-row band with a long K takes 128-column tiles over 4-CTA clusters;
+    K = 4096 keeps 64-column tiles over pairs."""
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 11008) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=64 split=2"
 
 
 def test_alpha_beta(clove_lib, oracle_mod, cuda):
