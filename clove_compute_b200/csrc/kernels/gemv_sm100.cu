@@ -237,6 +237,18 @@ size_t gemv_f16_smem(int nc, int K) { return kern::gemv_f16_smem_bytes(nc, K); }
     default: break;               \
   }
 
+// The variant launch_gemv_int4 takes for aligned operands and no debug output.
+const char* describe_gemv_int4(int rows, int nc, int K, const DeviceInfo& dev) {
+  const int P = (K + 1023) / 1024;
+  if (K % 128 == 0 && (nc * P <= 8 || (nc == 1 && P <= 12))) {
+    if (nc == 1 && rows >= 2 * dev.num_sms * 8)
+      return P <= 4 ? "ldg 4 CTAs/SM of 2x4 warps" : "ldg 2 CTAs/SM of 1x12 warps";
+    return "ldg 1 CTA/SM of 4x4 warps";
+  }
+  if (nc * P <= 8) return "register-B";
+  return "shared-B";
+}
+
 int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                      const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int nc,
                      int K, long long ldc_row, long long ldc_col, long long ldg_row,

@@ -716,6 +716,13 @@ int clove_describe_dispatch(int dtype, int M, int N, int K, char* buf, size_t bu
     int path = ov.path ? ov.path : (gemv ? 2 : (tc ? 1 : 3));
     name = path == 2 ? (N <= 8 && (N <= M || M > 8) ? "gemv_int4" : "gemv_int4_t")
                      : path == 1 ? "tc_int4" : "simt_int4";
+    if (path == 2 && ov.path == 0) {
+      // Vectors on the N side, or (transposed) on the M side.
+      const bool t = !(N <= 8 && (N <= M || M > 8));
+      snprintf(buf, buflen, "%s (%s)", name,
+               describe_gemv_int4(t ? N : M, t ? M : N, K, dev));
+      return CLOVE_OK;
+    }
   }
   snprintf(buf, buflen, "%s bn=%d split=%d", name, bn, split);
   return CLOVE_OK;

@@ -113,6 +113,7 @@ bool gemm_tc_supported(int op, int bn, int split, int out_bytes);
 int read_clear_error_tc();
 
 // ---- GEMV kernels (kernels/gemv_sm100.cu)
+const char* describe_gemv_int4(int rows, int nc, int K, const DeviceInfo& dev);
 int launch_gemv_int4(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                      const void* Bs, const void* Bz, void* C, int32_t* Gdbg, int rows, int nc,
                      int K, long long ldc_row, long long ldc_col, long long ldg_row,
