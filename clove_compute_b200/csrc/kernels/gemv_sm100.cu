@@ -130,12 +130,16 @@ template <int NC, int PW>
 int gemv_int4_ldg(const uint8_t* Aq, const void* As, const void* Az, const uint8_t* Bq,
                   const void* Bs, const void* Bz, void* C, int rows, int K, long long ldc_row,
                   long long ldc_col, const DeviceInfo& dev, cudaStream_t stream) {
-  // One vector and at least 2 x 148 x 8 rows: several CTAs per SM, one window per
-  // lane, so that some CTAs' loads are in flight while others reduce, and under
-  // programmatic launch the next call's CTAs start in the slots this call's CTAs
-  // leave. Rows up to 4096 codes: four CTAs of 2 x 4 warps per SM (<= 64 registers,
-  // 4 rows per warp and round); longer rows (up to 12288 codes): two CTAs of 1 x 12
-  // warps (8 rows per warp and round, <= 85 registers).
+  // One or two vectors and at least 2 x 148 x 8 rows: several CTAs per SM, one
+  // window per lane, so that some CTAs' loads are in flight while others reduce,
+  // and under programmatic launch the next call's CTAs start in the slots this
+  // call's CTAs leave. Rows up to 4096 codes: four CTAs of 2 x 4 warps per SM
+  // (<= 64 registers, 4 rows per warp and round); one vector with longer rows (up
+  // to 12288 codes): two CTAs of 1 x 12 warps (8 rows per warp and round, <= 85
+  // registers).
+  if (NC == 2 && PW == 1 && rows >= 2 * dev.num_sms * 8)
+    return launch_int4_ldg<2, 1, 4, 4, 2, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
+                                             ldc_col, 4 * dev.num_sms, stream);
   if (NC == 1 && rows >= 2 * dev.num_sms * 8) {
     if (PW == 1)
       return launch_int4_ldg<1, 1, 4, 4, 2, 4>(Aq, As, Az, Bq, Bs, Bz, C, rows, K, ldc_row,
@@ -241,7 +245,7 @@ size_t gemv_f16_smem(int nc, int K) { return kern::gemv_f16_smem_bytes(nc, K); }
 const char* describe_gemv_int4(int rows, int nc, int K, const DeviceInfo& dev) {
   const int P = (K + 1023) / 1024;
   if (K % 128 == 0 && (nc * P <= 8 || (nc == 1 && P <= 12))) {
-    if (nc == 1 && rows >= 2 * dev.num_sms * 8)
+    if (nc <= 2 && rows >= 2 * dev.num_sms * 8)
       return P <= 4 ? "ldg 4 CTAs/SM of 2x4 warps" : "ldg 2 CTAs/SM of 1x12 warps";
     return "ldg 1 CTA/SM of 4x4 warps";
   }

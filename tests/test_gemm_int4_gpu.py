@@ -55,6 +55,13 @@ def test_gemv_small_n(clove_lib, oracle_mod, cuda, N):
     _check(clove_lib, oracle_mod, 1000, N, 2048, seed=N)
 
 
+@pytest.mark.parametrize("M,K", [(4096, 4096), (2368, 2048), (5000, 3200)])
+def test_gemv_two_vectors_several_ctas(clove_lib, oracle_mod, cuda, M, K):
+    """Two decode vectors from 2 x 148 x 8 rows on: four CTAs of 2 x 4 warps per SM."""
+    assert clove_lib.describe_dispatch("int4", M, 2, K) == "gemv_int4 (ldg 4 CTAs/SM of 2x4 warps)"
+    _check(clove_lib, oracle_mod, M, 2, K, seed=M + K)
+
+
 @pytest.mark.parametrize("K", [128, 384, 8192, 12288])
 def test_gemv_k_sizes(clove_lib, oracle_mod, cuda, K):
     _check(clove_lib, oracle_mod, 300, 1, K, seed=K)
