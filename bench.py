@@ -325,25 +325,26 @@ def _secondary(cc, torch, peaks):
             "note": "clove_debug_stream_read of the same byte count, one launch per call: the "
                     "bandwidth a single kernel of this size reaches, without any math"}}
 
-    def decode_case(Mx, Kx, seed, n_copies, note):
-        """One INT4 decode call (N = 1) with Mx x Kx weights: plain, with weight
+    def decode_case(Mx, Kx, seed, n_copies, note, Nx=1):
+        """One INT4 decode call (Nx vectors) with Mx x Kx weights: plain, with weight
         prefetch, and against the bare read of the same bytes."""
-        opx = wl.int4_operands(Mx, 1, Kx, seed=seed)
+        opx = wl.int4_operands(Mx, Nx, Kx, seed=seed)
         Aqx = [dev(opx.A_q) for _ in range(n_copies)]
         Asx = [dev(opx.A_scale) for _ in range(n_copies)]
         Azx = [dev(opx.A_zero) for _ in range(n_copies)]
         Bqx, Bsx, Bzx = dev(opx.B_q), dev(opx.B_scale), dev(opx.B_zero)
-        Cx = torch.empty((Mx, 1), dtype=torch.float16, device="cuda")
+        Cx = torch.empty((Mx, Nx), dtype=torch.float16, device="cuda")
         tx = timeit(lambda i: cc.gemm_int4(Aqx[i], Asx[i], Azx[i], Bqx, Bsx, Bzx, Cx), n_copies, 200)
         cc.set_weight_prefetch(True)
         tx_pf = timeit(lambda i: cc.gemm_int4(Aqx[i], Asx[i], Azx[i], Bqx, Bsx, Bzx, Cx),
                        n_copies, 200)
         cc.set_weight_prefetch(False)
-        nbx = Mx * Kx // 2 + 2 * 2 * Mx * Kx // 128 + Kx // 2 + 2 * 2 * Kx // 128 + 2 * Mx
+        nbx = (Mx * Kx // 2 + 2 * 2 * Mx * Kx // 128 + Nx * (Kx // 2 + 2 * 2 * Kx // 128)
+               + 2 * Mx * Nx)
         del Aqx, Asx, Azx
         tx_floor = read_floor(nbx, n_copies)
         return {
-            "kernel": cc.describe_dispatch("int4", Mx, 1, Kx), "us_per_call": round(tx * 1e6, 3),
+            "kernel": cc.describe_dispatch("int4", Mx, Nx, Kx), "us_per_call": round(tx * 1e6, 3),
             "GBps": round(nbx / tx / 1e9, 1), "bytes_per_call": nbx,
             "roofline": {"bound": "hbm", "achieved": round(nbx / tx / 1e9, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -368,6 +369,10 @@ def _secondary(cc, torch, peaks):
         2 * 11008, 4096, 4, 6, "W_gate, W_up [11008, 4096] concatenated by rows, N = 1")
     out["int4_decode_down_4096x11008"] = decode_case(
         4096, 11008, 5, 12, "W_down [4096, 11008] (86 groups per row), N = 1")
+    # Config 2's weights against two vectors: the shape the reference INT4 kernel is
+    # timed at (it takes B as [K, N/2], so N = 1 is not expressible there).
+    out["int4_decode_4096x2x4096"] = decode_case(
+        4096, 4096, 6, 40, "config 2 weights, N = 2 (two decode tokens)", Nx=2)
 
     # config 3: int8 batch-32 with per-row / per-column scales
     M, N, K = 4096, 32, 4096
