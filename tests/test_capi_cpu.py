@@ -59,6 +59,30 @@ def test_dispatch_description_without_gpu(clove_lib):
     assert "split" in clove_lib.describe_dispatch("int8", 4096, 32, 4096)
 
 
+@pytest.mark.parametrize("M,N,K,want", [
+    (4096, 1, 4096, "ldg 4 CTAs/SM of 2x4 warps"),      # config 2
+    (12288, 1, 4096, "ldg 4 CTAs/SM of 2x4 warps"),     # Q/K/V in one call
+    (4096, 1, 11008, "ldg 2 CTAs/SM of 1x12 warps"),    # down projection, 11 windows
+    (4096, 2, 4096, "ldg 4 CTAs/SM of 2x4 warps"),      # two vectors
+    (2367, 1, 4096, "ldg 1 CTA/SM of 4x4 warps"),       # below 2 x 148 x 8 rows
+    (4096, 2, 8192, "shared-B"),                        # 16 windows of B
+    (1, 4096, 4096, "ldg 4 CTAs/SM of 2x4 warps"),      # transposed: rows of B stream
+])
+def test_int4_decode_variant_without_gpu(clove_lib, M, N, K, want):
+    """The decode GEMV variant follows from the shape alone (148 SMs assumed here)."""
+    d = clove_lib.describe_dispatch("int4", M, N, K)
+    assert d.startswith("gemv_int4") and d.endswith(f"({want})"), d
+
+
+def test_small_m_fp16_plan_without_gpu(clove_lib):
+    # One 128-row band: 64-column tiles on 2-CTA clusters at K = 4096, 128-column
+    # tiles on 4-CTA clusters once K reaches 96 blocks of 64.
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=64 split=2"
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 6144) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 128, 4096, 11008) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 6080) == "tc_f16 bn=64 split=2"
+
+
 def test_swiglu_dispatch_without_gpu(clove_lib):
     assert clove_lib.describe_dispatch("swiglu", 2048, 11008, 4096).startswith("tc2_swiglu")
     assert clove_lib.describe_dispatch("swiglu", 64, 11008, 4096).startswith("unfused")
