@@ -316,10 +316,16 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     if constexpr (SPLIT) {
       // This CTA finishes rows [rank*BM/S, (rank+1)*BM/S) of the tile and receives
-      // those rows' partials from the other S-1 CTAs of the cluster.
-      const uint32_t parts = gridDim.x;
+      // those rows' partials from the other S-1 CTAs of the cluster -- only the
+      // rows below M, the only ones stored (decode tiles hold a few live rows).
+      const int parts = static_cast<int>(gridDim.x);
+      const int rs = S::BM / parts;
+      const int tiles_n_ = (N + BN - 1) / BN;
+      const int first = static_cast<int>(blockIdx.y) / tiles_n_ * S::BM +
+                        static_cast<int>(blockIdx.x) * rs;
+      const int live = min(max(M - first, 0), rs);
       dev::mbar_init(rbar, 1);
-      dev::mbar_arrive_expect_tx(rbar, (parts - 1) * (S::BM / parts) * BN * 4);
+      dev::mbar_arrive_expect_tx(rbar, static_cast<uint32_t>((parts - 1) * live * BN * 4));
     }
     dev::fence_mbarrier_init();
   }
@@ -551,7 +557,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0u;
           }
-          if (!mine) {
+          if (!mine && row < M) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
               dev::st_async_v4(dst + (c + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3], rb);

@@ -75,12 +75,14 @@ def test_int4_decode_variant_without_gpu(clove_lib, M, N, K, want):
 
 
 def test_small_m_fp16_plan_without_gpu(clove_lib):
-    # One 128-row band: 64-column tiles on 2-CTA clusters at K = 4096, 128-column
-    # tiles on 4-CTA clusters once K reaches 96 blocks of 64.
-    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=64 split=2"
-    assert clove_lib.describe_dispatch("fp16", 1, 4096, 6144) == "tc_f16 bn=128 split=4"
+    # One 128-row band: 128-column tiles on 4-CTA clusters for up to 32 live rows
+    # or K of at least 96 blocks of 64; otherwise 64-column tiles on 2-CTA clusters.
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 32, 4096, 4096) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 64, 4096, 4096) == "tc_f16 bn=64 split=2"
+    assert clove_lib.describe_dispatch("fp16", 64, 4096, 6080) == "tc_f16 bn=64 split=2"
+    assert clove_lib.describe_dispatch("fp16", 64, 4096, 6144) == "tc_f16 bn=128 split=4"
     assert clove_lib.describe_dispatch("fp16", 128, 4096, 11008) == "tc_f16 bn=128 split=4"
-    assert clove_lib.describe_dispatch("fp16", 1, 4096, 6080) == "tc_f16 bn=64 split=2"
 
 
 def test_swiglu_dispatch_without_gpu(clove_lib):

@@ -78,10 +78,19 @@ def test_small_m_decode(clove_lib, oracle_mod, cuda, M, N, K):
 
 
 def test_small_m_long_k_plan(clove_lib, cuda):
-    """One 128-row band with a long K takes 128-column tiles over 4-CTA clusters;
-    K = 4096 keeps 64-column tiles over pairs."""
+    """One 128-row band with few live rows or a long K takes 128-column tiles over
+    4-CTA clusters; 64 live rows at K = 4096 keep 64-column tiles over pairs."""
     assert clove_lib.describe_dispatch("fp16", 1, 4096, 11008) == "tc_f16 bn=128 split=4"
-    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=64 split=2"
+    assert clove_lib.describe_dispatch("fp16", 1, 4096, 4096) == "tc_f16 bn=128 split=4"
+    assert clove_lib.describe_dispatch("fp16", 64, 4096, 4096) == "tc_f16 bn=64 split=2"
+
+
+@pytest.mark.parametrize("M", [1, 5, 31, 32, 33, 100])
+def test_split_k_live_rows(clove_lib, oracle_mod, cuda, M):
+    """Split-K clusters exchange only the rows below M: every cluster size and tile
+    width with a partly live tile."""
+    for bn, split in [(128, 4), (64, 2), (32, 8), (64, 8)]:
+        _run(clove_lib, oracle_mod, M, 256, 4096, path=1, bn=bn, split=split, seed=M + bn)
 
 
 def test_alpha_beta(clove_lib, oracle_mod, cuda):

@@ -35,6 +35,14 @@ def test_tc_split_acc_exact(clove_lib, oracle_mod, cuda, bn, split):
     _acc(clove_lib, oracle_mod, 256, 64, 4096, path=1, bn=bn, split=split, seed=split)
 
 
+@pytest.mark.parametrize("M", [1, 37, 100])
+def test_tc_split_live_rows_exact(clove_lib, oracle_mod, cuda, M):
+    """Split-K clusters exchange only the rows below M; int32 stays exact."""
+    for bn, split in [(32, 4), (64, 8), (128, 2)]:
+        _acc(clove_lib, oracle_mod, M, 128, 4096, za=3, zb=-5, path=1, bn=bn, split=split,
+             seed=M + split)
+
+
 def test_tc_ragged_and_zero_points(clove_lib, oracle_mod, cuda):
     _acc(clove_lib, oracle_mod, 200, 48, 160, seed=1)
     _acc(clove_lib, oracle_mod, 300, 272, 512, za=3, zb=-7, seed=2)
