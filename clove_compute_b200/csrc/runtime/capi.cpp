@@ -135,14 +135,16 @@ TcPlan plan_tc(int M, int N, int K, int elem, int num_sms) {
       long long p2 = 1;  // cluster sizes 2, 4, 8 (a tile's rows split evenly)
       while (p2 * 2 <= s) p2 *= 2;
       best.split = static_cast<int>(p2);
-      // fp16 with one 128-row band (decode in the runtime's orientation):
-      // 128-column tiles over 4-CTA clusters read 256 contiguous bytes of every B
-      // row instead of 128. That outweighs the larger cluster exchange when few
-      // rows are live (only rows below M are exchanged) or K is long: 1 x 4096 x
-      // 4096 11.7 -> 10.4 us, 1 x 4096 x 11008 24.8 -> 19.0 us; with all 128 rows
-      // live at K = 4096 the 64-column tiles stay ahead (12.6 against 13.3 us).
-      if (ov.bn == 0 && elem == 2 && tm == 1 && best.bn == 64 && best.split == 2 &&
-          (M <= 32 || kb_total >= 96) &&
+      // One 128-row band (decode in the runtime's orientation): 128-column tiles
+      // over 4-CTA clusters read twice the contiguous bytes of every B row (256
+      // for fp16, 128 for int8) per CTA. fp16: that outweighs the larger cluster
+      // exchange when few rows are live (only rows below M are exchanged) or K is
+      // long -- 1 x 4096 x 4096 11.7 -> 10.4 us, 1 x 4096 x 11008 24.8 -> 19.0 us,
+      // while with all 128 rows live at K = 4096 the 64-column tiles stay ahead
+      // (12.6 against 13.3 us). int8: for long K only (1 x 4096 x 11008 14.1 ->
+      // 12.6 us; at K = 4096 7.7 against 8.1 us even with one live row).
+      const bool wide = elem == 2 ? (M <= 32 || kb_total >= 96) : kb_total >= 64;
+      if (ov.bn == 0 && tm == 1 && best.bn == 64 && best.split == 2 && wide &&
           static_cast<long long>((N + 127) / 128) * 4 <= num_sms) {
         best.bn = 128;
         best.split = 4;

@@ -83,6 +83,11 @@ def test_small_m_fp16_plan_without_gpu(clove_lib):
     assert clove_lib.describe_dispatch("fp16", 64, 4096, 6080) == "tc_f16 bn=64 split=2"
     assert clove_lib.describe_dispatch("fp16", 64, 4096, 6144) == "tc_f16 bn=128 split=4"
     assert clove_lib.describe_dispatch("fp16", 128, 4096, 11008) == "tc_f16 bn=128 split=4"
+    # int8 (128 codes per K block): long K only.
+    assert clove_lib.describe_dispatch("int8", 1, 4096, 4096) == "tc_int8 bn=64 split=2"
+    assert clove_lib.describe_dispatch("int8", 1, 4096, 8064) == "tc_int8 bn=64 split=2"
+    assert clove_lib.describe_dispatch("int8", 1, 4096, 8192) == "tc_int8 bn=128 split=4"
+    assert clove_lib.describe_dispatch("int8", 1, 4096, 11008) == "tc_int8 bn=128 split=4"
 
 
 def test_swiglu_dispatch_without_gpu(clove_lib):

@@ -38,9 +38,15 @@ def test_tc_split_acc_exact(clove_lib, oracle_mod, cuda, bn, split):
 @pytest.mark.parametrize("M", [1, 37, 100])
 def test_tc_split_live_rows_exact(clove_lib, oracle_mod, cuda, M):
     """Split-K clusters exchange only the rows below M; int32 stays exact."""
-    for bn, split in [(32, 4), (64, 8), (128, 2)]:
-        _acc(clove_lib, oracle_mod, M, 128, 4096, za=3, zb=-5, path=1, bn=bn, split=split,
+    for bn, split in [(32, 4), (64, 8), (128, 2), (128, 4)]:
+        _acc(clove_lib, oracle_mod, M, 256, 4096, za=3, zb=-5, path=1, bn=bn, split=split,
              seed=M + split)
+
+
+def test_decode_long_k_plan_exact(clove_lib, oracle_mod, cuda):
+    """One live row with K = 11008: 128-column tiles over 4-CTA clusters, exact."""
+    assert clove_lib.describe_dispatch("int8", 1, 4096, 11008) == "tc_int8 bn=128 split=4"
+    _acc(clove_lib, oracle_mod, 1, 4096, 11008, seed=11)
 
 
 def test_tc_ragged_and_zero_points(clove_lib, oracle_mod, cuda):
