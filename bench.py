@@ -497,10 +497,15 @@ def _secondary(cc, torch, peaks):
     qkv = [torch.randn((B, H, S, D), device="cuda", generator=gen).half() for _ in range(3)]
     Oa = torch.empty_like(qkv[0])
     flop = 4.0 * D * B * H * (S * (S + 1) / 2)  # QK^T and PV over the unmasked pairs
-    # 20 calls per captured graph (same operands), so a graph launch is not timed per call.
-    t_a = timeit(lambda i: cc.flash_attention(*qkv, causal=True, O=Oa), 20, 100)
+    # 20 calls per captured graph (same operands), so a graph launch is not timed per
+    # call; the two kernels alternate three times (median of each), so that neither
+    # is timed only in the clock state the other left behind.
     sdpa = torch.nn.functional.scaled_dot_product_attention
-    t_t = timeit(lambda i: sdpa(*qkv, is_causal=True), 20, 100)
+    ta, tt = [], []
+    for _ in range(3):
+        ta.append(timeit(lambda i: cc.flash_attention(*qkv, causal=True, O=Oa), 20, 100))
+        tt.append(timeit(lambda i: sdpa(*qkv, is_causal=True), 20, 100))
+    t_a, t_t = statistics.median(ta), statistics.median(tt)
     out["attention_causal_1x32x2048x128"] = {
         "us_per_call": round(t_a * 1e6, 2), "TFLOPS": round(flop / t_a / 1e12, 1),
         "frac_of_bf16_peak": round(flop / t_a / 1e12 / peaks["bf16_tflops"], 4),
