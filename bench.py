@@ -823,8 +823,9 @@ def run_case(args):
     import clove_compute_b200 as cc
     from clove_compute_b200 import workloads as wl
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-    if args.case == "int4_decode":
-        op = wl.int4_operands(4096, 1, 4096, seed=0)
+    if args.case in ("int4_decode", "int4_decode_down"):
+        K = 4096 if args.case == "int4_decode" else 11008
+        op = wl.int4_operands(4096, 1, K, seed=0)
         t = [dev(x) for x in (op.A_q, op.A_scale, op.A_zero, op.B_q, op.B_scale, op.B_zero)]
         fn = lambda: cc.gemm_int4(*t)
     elif args.case == "int8_batch32":
@@ -1164,7 +1165,7 @@ def main():
     ap.add_argument("--multicast", action="store_true",
                     help="N > 1: also time the replicated output through an NVLink multicast object")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--case", choices=["int4_decode", "int8_batch32", "fp16_1024", "int4_4096",
+    ap.add_argument("--case", choices=["int4_decode", "int4_decode_down", "int8_batch32", "fp16_1024", "int4_4096",
                                        "attention"],
                     help="profiling mode: warm-up + steps plain launches of one secondary config")
     ap.add_argument("--host-links", action="store_true",
