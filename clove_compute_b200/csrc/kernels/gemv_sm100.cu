@@ -244,8 +244,9 @@ size_t gemv_f16_smem(int nc, int K) { return kern::gemv_f16_smem_bytes(nc, K); }
 // The variant launch_gemv_int4 takes for aligned operands and no debug output.
 const char* describe_gemv_int4(int rows, int nc, int K, const DeviceInfo& dev) {
   const int P = (K + 1023) / 1024;
-  if (K % 128 == 0 && (nc * P <= 8 || (nc == 1 && P <= 12))) {
-    if (nc <= 2 && rows >= 2 * dev.num_sms * 8)
+  // Direct-load instances: one vector with up to 12 windows, two with up to 4.
+  if (K % 128 == 0 && ((nc == 1 && P <= 12) || (nc == 2 && P <= 4))) {
+    if (rows >= 2 * dev.num_sms * 8)
       return P <= 4 ? "ldg 4 CTAs/SM of 2x4 warps" : "ldg 2 CTAs/SM of 1x12 warps";
     return "ldg 1 CTA/SM of 4x4 warps";
   }

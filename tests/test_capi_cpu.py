@@ -66,6 +66,7 @@ def test_dispatch_description_without_gpu(clove_lib):
     (4096, 2, 4096, "ldg 4 CTAs/SM of 2x4 warps"),      # two vectors
     (2367, 1, 4096, "ldg 1 CTA/SM of 4x4 warps"),       # below 2 x 148 x 8 rows
     (4096, 2, 8192, "shared-B"),                        # 16 windows of B
+    (4096, 4, 2048, "register-B"),                      # 3-8 vectors, <= 8 windows in all
     (1, 4096, 4096, "ldg 4 CTAs/SM of 2x4 warps"),      # transposed: rows of B stream
 ])
 def test_int4_decode_variant_without_gpu(clove_lib, M, N, K, want):
