@@ -844,6 +844,10 @@ def run_case(args):
         A, B = wl.fp16_operands(1024, 1024, 1024, seed=0)
         t = [dev(A), dev(B)]
         fn = lambda: cc.gemm_fp16(*t)
+    elif args.case == "fp16_decode":
+        A, B = wl.fp16_operands(1, 4096, 4096, seed=0)  # the runtime's decode orientation
+        t = [dev(A), dev(B)]
+        fn = lambda: cc.gemm_fp16(*t)
     else:
         raise SystemExit(f"unknown case {args.case}")
     for _ in range(args.warmup + args.steps):
@@ -1166,7 +1170,7 @@ def main():
                     help="N > 1: also time the replicated output through an NVLink multicast object")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--case", choices=["int4_decode", "int4_decode_down", "int8_batch32", "fp16_1024", "int4_4096",
-                                       "attention"],
+                                       "attention", "fp16_decode"],
                     help="profiling mode: warm-up + steps plain launches of one secondary config")
     ap.add_argument("--host-links", action="store_true",
                     help="measure the host<->device copy bandwidth the end-to-end run uses "
